@@ -1,0 +1,367 @@
+// Persistent grouped GEMM on sm_100a tensor cores (tcgen05 + TMEM + TMA),
+// in "swap-AB" form: the expert's weight rows fill the 128-row MMA M
+// dimension and the tokens routed to that expert form the MMA N dimension.
+// This lets a decode step with 1-3 tokens per expert stream its weights at
+// full HBM rate (N = 32) and lets prefill reuse each weight tile across 128
+// tokens (N = 128).
+//
+// Operands are K-major byte rows (NVFP4: two E2M1 codes per byte; BF16: two
+// bytes per element), staged by TMA with 128-byte swizzle, 128 bytes of K per
+// pipeline stage (256 NVFP4 or 64 BF16 elements = 4 MMAs).  NVFP4 block
+// scales live in the 128x4 atom layout of crates/glm-format/src/nvfp4.rs:493
+// (512 bytes per 128 rows x 64 K); that layout is exactly what
+// tcgen05.cp.32x128b.warpx4 moves into TMEM for kind::mxf4nvf4, so weights are
+// consumed as packed by the reference codec with no repacking.
+//
+// Warp roles (192 threads): warp 0 issues TMA, warp 1 owns TMEM and issues
+// MMAs, warps 2..5 run the epilogue (warp w reads TMEM lanes 32*(w%4)..).
+// Every wait is bounded (device.cuh: mbar_wait); a timeout raises the CTA's
+// abort flag, sets kStatusWaitTimeout, drains in-flight copies and MMAs with
+// bounded waits, frees TMEM and returns.
+#pragma once
+
+#include <cuda.h>
+
+#include "device.cuh"
+
+namespace glmaxx {
+
+// One N tile of a grouped GEMM: up to NT consecutive B rows of one expert.
+// B values and per-row metadata are in compacted (expert, token, slot) row
+// order; B scale factors live in the expert-local 128-padded row space of the
+// reference's grouped SFA plan (crates/glm-cuda/src/abi.rs:44-91), where every
+// expert's rows start on a 128-row atom boundary.
+struct NTile {
+  uint32_t expert;        // expert index (A operand slab)
+  uint32_t row_start;     // first B row (compacted row space)
+  uint32_t sf_row_start;  // same row in the padded scale-factor row space
+  uint32_t rows;          // valid rows in this tile (<= NT)
+};
+
+enum EpilogueKind : int {
+  kEpiSwiGLU = 0,       // out_bf16[row][col] = bf16(silu(g) * u)
+  kEpiRoutedPlane = 1,  // plane[token][slot][col] = w * acc (deterministic combine later)
+  kEpiRoutedAtomic = 2, // out_f32[token][col] += w * acc
+  kEpiStoreF32 = 3,     // out_f32[row][col] = acc
+};
+
+struct GemmArgs {
+  const NTile* tiles;         // explicit n-tile list, or null for implicit tiles
+  const uint32_t* tile_count; // device count for explicit lists
+  uint32_t implicit_rows;     // implicit tiles: q -> rows [q*NT, min(+NT, implicit_rows))
+  uint32_t m_tiles;           // 128-row output tiles (per half in dual mode)
+  uint32_t k_chunks;          // K bytes / 128
+  uint32_t up_row_offset;     // dual: first up row inside an expert's A rows
+  uint32_t kblocks;           // K / 64: scale atoms along K
+  uint32_t ldo;               // output row stride (elements)
+  uint32_t top_k;
+  uint32_t pad0;
+  const uint8_t* sfa;         // A scale atoms, expert-major
+  uint64_t sfa_expert_bytes;
+  const uint8_t* sfb;         // B scale atoms (padded row space, 128-row tiles)
+  const float* a_global;      // [experts] per-tensor scale of A, or null
+  const float* b_global;      // [rows] per-row scale of B (compacted rows), or null
+  void* out;
+  const uint32_t* row_token;  // compacted row -> token
+  const uint32_t* row_slot;   // compacted row -> slot
+  const float* row_weight;    // compacted row -> routing weight
+  uint32_t* status;
+};
+
+template <bool FP4, bool DUAL, int NT>
+struct GemmShape {
+  static constexpr int kAcc = DUAL ? 2 : 1;
+  static constexpr int kNJ = NT >= 128 ? NT / 128 : 1;              // SFB atoms along N
+  static constexpr int kSfCols = FP4 ? (kAcc * 16 + 16 * kNJ) : 0;  // TMEM columns for scales
+  static constexpr int kAccBufs = (2 * kAcc * NT + kSfCols) <= 512 ? 2 : 1;
+  static constexpr int kUsedCols = kAccBufs * kAcc * NT + kSfCols;
+  static constexpr int kTmemCols = kUsedCols <= 32    ? 32
+                                   : kUsedCols <= 64  ? 64
+                                   : kUsedCols <= 128 ? 128
+                                   : kUsedCols <= 256 ? 256
+                                                      : 512;
+  static constexpr int kABytes = 128 * 128;
+  static constexpr int kBBytes = NT * 128;
+  static constexpr int kSfaBytes = FP4 ? 2048 : 0;
+  static constexpr int kSfbBytes = FP4 ? 2048 * kNJ : 0;
+  static constexpr int kStageBytes = kAcc * kABytes + kBBytes + kAcc * kSfaBytes + kSfbBytes;
+  static_assert(kUsedCols <= 512, "TMEM budget");
+  static_assert(NT % 32 == 0 && NT <= 128, "tile rows");
+  static_assert(kStageBytes % 1024 == 0, "stage alignment");
+};
+
+template <bool FP4, bool DUAL, int NT, int STAGES>
+constexpr int gemm_smem_bytes() {
+  return GemmShape<FP4, DUAL, NT>::kStageBytes * STAGES + 1024 /* align slack */ + 256;
+}
+
+template <bool FP4, bool DUAL, int NT, int STAGES, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
+  using S = GemmShape<FP4, DUAL, NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kStageBytes * STAGES);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* tfull_bar = bars + 2 * STAGES;
+  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
+  uint64_t* drain_bar = bars + 2 * STAGES + 4;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&tmap_a);
+    tma_prefetch(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, S::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  const uint32_t tiles_total = args.tiles ? *args.tile_count : (args.implicit_rows + NT - 1) / NT;
+  const uint32_t items = tiles_total * args.m_tiles;
+
+  auto stage_a = [&](int s, int h) { return stage_base + s * S::kStageBytes + h * S::kABytes; };
+  auto stage_b = [&](int s) { return stage_base + s * S::kStageBytes + S::kAcc * S::kABytes; };
+  auto stage_sfa = [&](int s, int h) {
+    return stage_base + s * S::kStageBytes + S::kAcc * S::kABytes + S::kBBytes + h * S::kSfaBytes;
+  };
+  auto stage_sfb = [&](int s) {
+    return stage_base + s * S::kStageBytes + S::kAcc * S::kABytes + S::kBBytes +
+           S::kAcc * S::kSfaBytes;
+  };
+  auto tile_of = [&](uint32_t q) {
+    if (args.tiles) return args.tiles[q];
+    NTile t;
+    t.expert = 0;
+    t.row_start = q * NT;
+    t.sf_row_start = q * NT;
+    t.rows = min(static_cast<uint32_t>(NT), args.implicit_rows - q * NT);
+    return t;
+  };
+  auto fail = [&](uint32_t bit) {
+    *s_abort = 1;
+    if (args.status) atomicOr(args.status, bit);
+  };
+
+  constexpr uint32_t kTx = S::kStageBytes;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (uint32_t item = blockIdx.x; ok && item < items; item += gridDim.x) {
+        const uint32_t q = item / args.m_tiles, i = item % args.m_tiles;
+        const NTile t = tile_of(q);
+        const uint8_t* sfa_e = FP4 ? args.sfa + uint64_t(t.expert) * args.sfa_expert_bytes : nullptr;
+        for (uint32_t kc = 0; kc < args.k_chunks; ++kc) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) {
+            fail(kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], kTx);
+          const int32_t kx = static_cast<int32_t>(kc * 128);
+          tma_load_3d(stage_a(stage, 0), &tmap_a, &full_bar[stage], kx, int32_t(i * 128),
+                      int32_t(t.expert));
+          if (DUAL)
+            tma_load_3d(stage_a(stage, 1), &tmap_a, &full_bar[stage], kx,
+                        int32_t(args.up_row_offset + i * 128), int32_t(t.expert));
+          tma_load_2d(stage_b(stage), &tmap_b, &full_bar[stage], kx, int32_t(t.row_start));
+          if (FP4) {
+            bulk_load(stage_sfa(stage, 0), sfa_e + 512ull * (uint64_t(i) * args.kblocks + kc * 4),
+                      2048, &full_bar[stage]);
+            if (DUAL)
+              bulk_load(stage_sfa(stage, 1),
+                        sfa_e + 512ull * (uint64_t(args.up_row_offset / 128 + i) * args.kblocks +
+                                          kc * 4),
+                        2048, &full_bar[stage]);
+#pragma unroll
+            for (int j = 0; j < S::kNJ; ++j)
+              bulk_load(stage_sfb(stage) + j * 2048,
+                        args.sfb + 512ull * (uint64_t(t.sf_row_start / 128 + j) * args.kblocks + kc * 4),
+                        2048, &full_bar[stage]);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: the last min(issued, STAGES) fills must land before the CTA exits.
+      const uint32_t pending = issued < STAGES ? issued : STAGES;
+      for (uint32_t b = 0; b < pending; ++b) {
+        stage = (stage == 0) ? STAGES - 1 : stage - 1;
+        if (stage == STAGES - 1) phase ^= 1;
+        if (!mbar_wait(&full_bar[stage], phase, nullptr)) fail(kStatusWaitTimeout);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t sf_base = tmem + S::kAccBufs * S::kAcc * NT;  // column offset
+      const uint32_t sfa_t0 = sf_base, sfa_t1 = sf_base + 16;
+      const uint32_t sfb_t = sf_base + S::kAcc * 16;
+      constexpr uint32_t kIdesc = FP4 ? idesc_mxf4nvf4(NT) : idesc_bf16(NT);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint32_t item = blockIdx.x; ok && item < items; item += gridDim.x) {
+        const uint32_t q = item / args.m_tiles;
+        const NTile t = tile_of(q);
+        const uint32_t sfb_shift = NT < 128 ? (t.sf_row_start % 128) / 32 : 0;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, s_abort)) {
+          fail(kStatusWaitTimeout);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d0 = tmem + acc * (S::kAcc * NT);
+        const uint32_t d1 = d0 + NT;
+        for (uint32_t kc = 0; kc < args.k_chunks; ++kc) {
+          if (!mbar_wait(&full_bar[stage], phase, s_abort)) {
+            fail(kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (FP4) {
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              tc_cp_sf(sfa_t0 + kb * 4, smem_desc_sf(stage_sfa(stage, 0) + kb * 512));
+              if (DUAL) tc_cp_sf(sfa_t1 + kb * 4, smem_desc_sf(stage_sfa(stage, 1) + kb * 512));
+#pragma unroll
+              for (int j = 0; j < S::kNJ; ++j)
+                tc_cp_sf(sfb_t + kb * 4 * S::kNJ + j * 4,
+                         smem_desc_sf(stage_sfb(stage) + (j * 4 + kb) * 512));
+            }
+          }
+          const uint64_t a0 = smem_desc_sw128(stage_a(stage, 0));
+          const uint64_t a1 = DUAL ? smem_desc_sw128(stage_a(stage, 1)) : 0;
+          const uint64_t bd = smem_desc_sw128(stage_b(stage));
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            const uint32_t accum = (kc > 0 || kb > 0) ? 1u : 0u;
+            // advancing the start address by 32 bytes steps K by one MMA inside the swizzle atom
+            if (FP4) {
+              mma_fp4(d0, a0 + 2 * kb, bd + 2 * kb, kIdesc, accum, sfa_t0 + kb * 4,
+                      sfb_t + kb * 4 * S::kNJ + sfb_shift);
+              if (DUAL)
+                mma_fp4(d1, a1 + 2 * kb, bd + 2 * kb, kIdesc, accum, sfa_t1 + kb * 4,
+                        sfb_t + kb * 4 * S::kNJ + sfb_shift);
+            } else {
+              mma_bf16(d0, a0 + 2 * kb, bd + 2 * kb, kIdesc, accum);
+              if (DUAL) mma_bf16(d1, a1 + 2 * kb, bd + 2 * kb, kIdesc, accum);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+        if (S::kAccBufs == 2) {
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1;
+        } else {
+          acc_phase ^= 1;
+        }
+      }
+      // Drain all tensor-core work issued by this thread before TMEM is freed.
+      tc_commit(drain_bar);
+      if (!mbar_wait(drain_bar, 0, nullptr)) fail(kStatusTmemTimeout);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const uint32_t m = quarter * 32 + lane;
+    uint32_t acc = 0, acc_phase = 0;
+    for (uint32_t item = blockIdx.x; item < items; item += gridDim.x) {
+      const uint32_t q = item / args.m_tiles, i = item % args.m_tiles;
+      const NTile t = tile_of(q);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, s_abort)) {
+        fail(kStatusWaitTimeout);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t col = i * 128 + m;
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t c_acc = acc * (S::kAcc * NT);
+      float scale_a = 1.0f;
+      if (FP4 && args.a_global) scale_a = args.a_global[t.expert];
+      for (uint32_t c0 = 0; c0 < t.rows; c0 += 16) {
+        float g[16], u[16];
+        tmem_ld16(lane_base + c_acc + c0, g);
+        if (DUAL) tmem_ld16(lane_base + c_acc + NT + c0, u);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t n = c0 + j;
+          if (n >= t.rows) break;
+          const uint32_t row = t.row_start + n;
+          float s = scale_a;
+          if (FP4 && args.b_global) s = __fmul_rn(s, args.b_global[row]);
+          if (EPI == kEpiSwiGLU) {
+            const float gv = __fmul_rn(g[j], s);
+            const float uv = DUAL ? __fmul_rn(u[j], s) : 1.0f;
+            const float h = __fmul_rn(silu(gv), uv);
+            reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(row) * args.ldo + col] =
+                __float2bfloat16_rn(h);
+          } else if (EPI == kEpiRoutedPlane) {
+            const float v = __fmul_rn(args.row_weight[row], __fmul_rn(g[j], s));
+            const uint64_t dst =
+                (uint64_t(args.row_token[row]) * args.top_k + args.row_slot[row]) * args.ldo + col;
+            reinterpret_cast<float*>(args.out)[dst] = v;
+          } else if (EPI == kEpiRoutedAtomic) {
+            const float v = __fmul_rn(args.row_weight[row], __fmul_rn(g[j], s));
+            atomicAdd(reinterpret_cast<float*>(args.out) + uint64_t(args.row_token[row]) * args.ldo + col,
+                      v);
+          } else {
+            reinterpret_cast<float*>(args.out)[uint64_t(row) * args.ldo + col] = __fmul_rn(g[j], s);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (S::kAccBufs == 2) {
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      } else {
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, S::kTmemCols);
+}
+
+}  // namespace glmaxx

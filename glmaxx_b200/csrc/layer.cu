@@ -1,0 +1,417 @@
+// Rank-local routed-MoE step and device router/compaction: descriptor
+// validation, workspace carving and the launch sequence.  The operation order
+// is the reference's frozen sparse-layer order (crates/glm-reference/src/
+// routed_fc2.rs:93-109): ProtectedRouter -> StableRouteCompaction -> RoutedFc1
+// -> Swiglu -> RoutedFc2WeightedScatter -> SharedExpert, producing the partial
+// that MoeTpReduce sums across ranks.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "../../include/glmaxx_kernel.h"
+#include "moe.h"
+#include "runtime.h"
+
+namespace glmaxx {
+
+namespace {
+
+constexpr uint64_t kAlign = 256;
+uint64_t up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+struct Carve {
+  uint64_t cursor = 0;
+  uint64_t take(uint64_t bytes) {
+    const uint64_t off = cursor;
+    cursor = up(cursor + (bytes ? bytes : 1), kAlign);
+    return off;
+  }
+};
+
+// Planes shared by the router/compaction and the full layer.
+struct RoutePlan {
+  uint32_t T, E, K, W, A;
+  uint64_t partial, bitmap, wprefix, counts, offsets, poffs, status;
+  void carve(Carve& c, uint32_t tokens, uint32_t experts, uint32_t top_k) {
+    T = tokens;
+    E = experts;
+    K = top_k;
+    W = (T + 31) / 32;
+    A = T * K;
+    partial = c.take(8ull * T * E * 4);
+    bitmap = c.take(uint64_t(E) * W * 4);
+    wprefix = c.take(uint64_t(E) * W * 4);
+    counts = c.take(uint64_t(E) * 4);
+    offsets = c.take(uint64_t(E + 1) * 4);
+    poffs = c.take(uint64_t(E + 1) * 4);
+    status = c.take(16);
+  }
+};
+
+struct LayerPlan {
+  RoutePlan r;
+  uint32_t H, I, Is, nt, sf_rows, max_tiles;
+  bool decode, shared;
+  uint64_t tiles, tile_count, route_row, row_token, row_slot, row_weight, gx, gh, row_prow;
+  uint64_t xq, xsf, hbuf, hq, hsf, plane, hs, sbuf, total;
+
+  void build(const glmaxx_moe_layer_descriptor& d) {
+    Carve c;
+    r.carve(c, d.tokens, d.experts, d.top_k);
+    H = d.hidden;
+    I = d.local_intermediate;
+    shared = (d.flags & GLMAXX_MOE_SHARED_EXPERT) != 0;
+    Is = shared ? d.shared_intermediate : 0;
+    decode = d.path == GLMAXX_FC1_DECODE_PERSISTENT || (d.path == 0 && d.tokens <= 256);
+    nt = decode ? 32 : 128;
+    const uint32_t A = r.A;
+    const uint32_t active = A < r.E ? A : r.E;
+    sf_rows = static_cast<uint32_t>(up(uint64_t(A) + 127ull * active, 128));
+    max_tiles = (A + nt - 1) / nt + active;
+    tiles = c.take(uint64_t(max_tiles) * sizeof(NTile));
+    tile_count = c.take(16);
+    route_row = c.take(uint64_t(A) * 4);
+    row_token = c.take(uint64_t(A) * 4);
+    row_slot = c.take(uint64_t(A) * 4);
+    row_weight = c.take(uint64_t(A) * 4);
+    gx = c.take(uint64_t(A) * 4);
+    gh = c.take(uint64_t(A) * 4);
+    row_prow = c.take(uint64_t(A) * 4);
+    xq = c.take(uint64_t(A) * H / 2);
+    xsf = c.take(uint64_t(sf_rows) * H / 16);
+    hbuf = c.take(uint64_t(A) * I * 2);
+    hq = c.take(uint64_t(A) * I / 2);
+    hsf = c.take(uint64_t(sf_rows) * I / 16);
+    plane = decode ? c.take(uint64_t(A) * H * 4) : c.take(0);
+    hs = shared ? c.take(uint64_t(r.T) * Is * 2) : c.take(0);
+    sbuf = (shared && decode) ? c.take(uint64_t(r.T) * H * 4) : c.take(0);
+    total = c.cursor + kAlign;  // slack so the caller's base need only be 16-byte aligned
+  }
+};
+
+bool aligned(uint64_t p, uint64_t a) { return p != 0 && p % a == 0; }
+
+bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
+  if (d.abi_version != GLMAXX_MOE_LAYER_ABI_VERSION || d.struct_bytes != sizeof(d)) return false;
+  for (uint32_t v : d.reserved0)
+    if (v) return false;
+  for (uint64_t v : d.reserved)
+    if (v) return false;
+  if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT)) return false;
+  if (d.path > GLMAXX_FC1_PREFILL_GROUPED) return false;
+  if (d.tokens == 0 || d.tokens > 65536) return false;
+  if (d.hidden == 0 || d.hidden % 256 != 0 || d.hidden > 16384) return false;
+  if (d.experts == 0 || d.experts > 256) return false;
+  if (d.top_k == 0 || d.top_k > 8 || d.top_k > d.experts) return false;
+  if (uint64_t(d.tokens) * d.top_k > (1u << 20)) return false;
+  // power of two in [256, 2048]: FC2 quantisation reduces a row over I/64 lanes
+  if (d.local_intermediate < 256 || d.local_intermediate > 2048 ||
+      (d.local_intermediate & (d.local_intermediate - 1)))
+    return false;
+  if (!(d.flags & GLMAXX_MOE_ROUTES_GIVEN)) {
+    if (d.groups == 0 || d.groups > 32 || d.experts % d.groups) return false;
+    if (d.topk_groups == 0 || d.topk_groups > d.groups) return false;
+    if (d.top_k > (d.experts / d.groups) * d.topk_groups) return false;
+    if (!(d.route_scale == d.route_scale)) return false;
+    if (!aligned(d.router_weight_bf16, 16) || !aligned(d.router_bias_f32, 4)) return false;
+  }
+  if (d.flags & GLMAXX_MOE_SHARED_EXPERT) {
+    if (d.shared_intermediate == 0 || d.shared_intermediate % 128 || d.shared_intermediate > 8192)
+      return false;
+    if (!aligned(d.shared13_bf16, 256) || !aligned(d.shared2_bf16, 256)) return false;
+  }
+  return aligned(d.input_bf16, 256) && aligned(d.w13_values, 256) && aligned(d.w13_scales, 16) &&
+         aligned(d.w13_global_f32, 4) && aligned(d.w2_values, 256) && aligned(d.w2_scales, 16) &&
+         aligned(d.w2_global_f32, 4) && aligned(d.route_experts_u16, 4) &&
+         aligned(d.route_weights_f32, 4) && aligned(d.output_f32, 16) && aligned(d.workspace, 16);
+}
+
+template <typename T>
+T* at(uint64_t base, uint64_t off) {
+  return reinterpret_cast<T*>(base + off);
+}
+
+}  // namespace
+
+uint64_t layer_workspace_bytes(const glmaxx_moe_layer_descriptor& d) {
+  LayerPlan p;
+  p.build(d);
+  return p.total;
+}
+
+int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_stream,
+                         int32_t* async_err) {
+  if (desc == nullptr || async_err == nullptr) return GLMAXX_ERR_NULL;
+  *async_err = 0;
+  const glmaxx_moe_layer_descriptor& d = *desc;
+  if (!valid_layer(d)) return GLMAXX_ERR_DESCRIPTOR;
+  LayerPlan p;
+  p.build(d);
+  if (d.workspace_bytes < p.total) return GLMAXX_ERR_DESCRIPTOR;
+  DeviceInfo info;
+  int32_t arch = current_device_info(&info);
+  if (arch != 0) return arch;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
+  const uint64_t ws = up(d.workspace, kAlign);
+  const RoutePlan& r = p.r;
+  uint32_t* status = d.validation_error_u32 ? reinterpret_cast<uint32_t*>(d.validation_error_u32)
+                                            : at<uint32_t>(ws, r.status);
+  uint16_t* experts = reinterpret_cast<uint16_t*>(d.route_experts_u16);
+  float* weights = reinterpret_cast<float*>(d.route_weights_f32);
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(d.input_bf16);
+  float* out = reinterpret_cast<float*>(d.output_f32);
+  const uint32_t bitmap_words = r.E * r.W;
+#define CHECK(expr)                          \
+  do {                                       \
+    cudaError_t _st = (expr);                \
+    if (_st != cudaSuccess) return int32_t(_st); \
+  } while (0)
+  CHECK(cudaMemsetAsync(status, 0, 4, stream));
+  // 1. router (or caller routes) -> dense routes + token-in-expert bitmap
+  if (d.flags & GLMAXX_MOE_ROUTES_GIVEN) {
+    CHECK(launch_routes_to_bitmap(experts, weights, r.T, r.E, r.K, at<uint32_t>(ws, r.bitmap),
+                                  bitmap_words, status, stream));
+  } else {
+    CHECK(launch_router_logits(x, reinterpret_cast<const uint16_t*>(d.router_weight_bf16),
+                               at<float>(ws, r.partial), r.T, p.H, r.E, at<uint32_t>(ws, r.bitmap),
+                               bitmap_words, stream));
+    CHECK(launch_router_select(at<float>(ws, r.partial),
+                               reinterpret_cast<const float*>(d.router_bias_f32), r.T, r.E,
+                               d.groups, d.topk_groups, r.K, d.route_scale, experts, weights,
+                               at<uint32_t>(ws, r.bitmap), r.W, status, stream));
+  }
+  // 2. stable compaction
+  NTile* tiles = at<NTile>(ws, p.tiles);
+  uint32_t* tile_count = at<uint32_t>(ws, p.tile_count);
+  CHECK(launch_compact(at<uint32_t>(ws, r.bitmap), r.T, r.E, p.nt, p.sf_rows, p.max_tiles,
+                       at<uint32_t>(ws, r.wprefix), at<uint32_t>(ws, r.counts),
+                       at<uint32_t>(ws, r.offsets), at<uint32_t>(ws, r.poffs), tiles, tile_count,
+                       status, stream));
+  // 3. NVFP4 quantisation of x into the assignment rows
+  QuantScatterArgs q{};
+  q.x = x;
+  q.route_experts = experts;
+  q.route_weights = weights;
+  q.bitmap = at<uint32_t>(ws, r.bitmap);
+  q.wprefix = at<uint32_t>(ws, r.wprefix);
+  q.poffs = at<uint32_t>(ws, r.poffs);
+  q.offsets = at<uint32_t>(ws, r.offsets);
+  q.xq = at<uint8_t>(ws, p.xq);
+  q.xsf = at<uint8_t>(ws, p.xsf);
+  q.row_token = at<uint32_t>(ws, p.row_token);
+  q.row_slot = at<uint32_t>(ws, p.row_slot);
+  q.row_weight = at<float>(ws, p.row_weight);
+  q.row_gscale = at<float>(ws, p.gx);
+  q.row_prow = at<uint32_t>(ws, p.row_prow);
+  q.route_row = at<uint32_t>(ws, p.route_row);
+  q.status = status;
+  q.T = r.T;
+  q.H = p.H;
+  q.E = r.E;
+  q.top_k = r.K;
+  q.sf_row_cap = p.sf_rows;
+  CHECK(launch_quant_scatter(q, stream));
+  // 4. grouped FC1 (gate+up) with fused SwiGLU -> h [A][I] bf16
+  {
+    GemmLaunch g{};
+    g.a = reinterpret_cast<const void*>(d.w13_values);
+    g.a_experts = r.E;
+    g.a_rows = 2 * p.I;
+    g.a_row_bytes = p.H / 2;
+    g.b = q.xq;
+    g.b_rows = r.A;
+    g.b_row_bytes = p.H / 2;
+    GemmArgs& a = g.args;
+    a.tiles = tiles;
+    a.tile_count = tile_count;
+    a.m_tiles = p.I / 128;
+    a.k_chunks = p.H / 256;
+    a.up_row_offset = p.I;
+    a.kblocks = p.H / 64;
+    a.ldo = p.I;
+    a.top_k = r.K;
+    a.sfa = reinterpret_cast<const uint8_t*>(d.w13_scales);
+    a.sfa_expert_bytes = 2ull * p.I * p.H / 16;
+    a.sfb = q.xsf;
+    a.a_global = reinterpret_cast<const float*>(d.w13_global_f32);
+    a.b_global = q.row_gscale;
+    a.out = at<void>(ws, p.hbuf);
+    a.status = status;
+    CHECK(launch_gemm(p.decode ? kFc1DecodeFp4 : kFc1PrefillFp4, g, info.sms, stream));
+  }
+  // 5. NVFP4 quantisation of h
+  Fc2QuantArgs f{};
+  f.h = at<uint16_t>(ws, p.hbuf);
+  f.row_prow = q.row_prow;
+  f.hq = at<uint8_t>(ws, p.hq);
+  f.hsf = at<uint8_t>(ws, p.hsf);
+  f.gscale = at<float>(ws, p.gh);
+  f.status = status;
+  f.count_ptr = at<uint32_t>(ws, r.offsets) + r.E;
+  f.count = r.A;
+  f.I = p.I;
+  f.sf_row_cap = p.sf_rows;
+  CHECK(launch_fc2_quant(f, stream));
+  // 6. shared expert (bf16), and the output initialisation it provides
+  if (p.shared) {
+    GemmLaunch g1{};
+    g1.a = reinterpret_cast<const void*>(d.shared13_bf16);
+    g1.a_experts = 1;
+    g1.a_rows = 2 * p.Is;
+    g1.a_row_bytes = 2 * p.H;
+    g1.b = x;
+    g1.b_rows = r.T;
+    g1.b_row_bytes = 2 * p.H;
+    g1.args.implicit_rows = r.T;
+    g1.args.m_tiles = p.Is / 128;
+    g1.args.k_chunks = 2 * p.H / 128;
+    g1.args.up_row_offset = p.Is;
+    g1.args.ldo = p.Is;
+    g1.args.out = at<void>(ws, p.hs);
+    g1.args.status = status;
+    CHECK(launch_gemm(p.decode ? kShared1Bf16N64 : kShared1Bf16N128, g1, info.sms, stream));
+    GemmLaunch g2{};
+    g2.a = reinterpret_cast<const void*>(d.shared2_bf16);
+    g2.a_experts = 1;
+    g2.a_rows = p.H;
+    g2.a_row_bytes = 2 * p.Is;
+    g2.b = at<void>(ws, p.hs);
+    g2.b_rows = r.T;
+    g2.b_row_bytes = 2 * p.Is;
+    g2.args.implicit_rows = r.T;
+    g2.args.m_tiles = p.H / 128;
+    g2.args.k_chunks = 2 * p.Is / 128;
+    g2.args.ldo = p.H;
+    g2.args.out = p.decode ? at<void>(ws, p.sbuf) : static_cast<void*>(out);
+    g2.args.status = status;
+    CHECK(launch_gemm(p.decode ? kShared2Bf16N64 : kShared2Bf16N128, g2, info.sms, stream));
+  } else if (!p.decode) {
+    CHECK(cudaMemsetAsync(out, 0, uint64_t(r.T) * p.H * 4, stream));
+  }
+  // 7. grouped FC2 with the routing-weighted combine
+  {
+    GemmLaunch g{};
+    g.a = reinterpret_cast<const void*>(d.w2_values);
+    g.a_experts = r.E;
+    g.a_rows = p.H;
+    g.a_row_bytes = p.I / 2;
+    g.b = f.hq;
+    g.b_rows = r.A;
+    g.b_row_bytes = p.I / 2;
+    GemmArgs& a = g.args;
+    a.tiles = tiles;
+    a.tile_count = tile_count;
+    a.m_tiles = p.H / 128;
+    a.k_chunks = p.I / 256;
+    a.kblocks = p.I / 64;
+    a.ldo = p.H;
+    a.top_k = r.K;
+    a.sfa = reinterpret_cast<const uint8_t*>(d.w2_scales);
+    a.sfa_expert_bytes = uint64_t(p.H) * p.I / 16;
+    a.sfb = f.hsf;
+    a.a_global = reinterpret_cast<const float*>(d.w2_global_f32);
+    a.b_global = f.gscale;
+    a.out = p.decode ? at<void>(ws, p.plane) : static_cast<void*>(out);
+    a.row_token = q.row_token;
+    a.row_slot = q.row_slot;
+    a.row_weight = q.row_weight;
+    a.status = status;
+    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4 : kFc2PrefillFp4, g, info.sms, stream));
+  }
+  // 8. deterministic combine (decode): ascending-expert sum + shared
+  if (p.decode)
+    CHECK(launch_combine(at<float>(ws, p.plane), experts,
+                         p.shared ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H, r.K, stream));
+#undef CHECK
+  return 0;
+}
+
+// -------------------------------------------------------------- router only
+namespace {
+bool valid_router(const glmaxx_router_descriptor& d) {
+  if (d.abi_version != GLMAXX_ROUTER_ABI_VERSION || d.struct_bytes != sizeof(d) || d.flags)
+    return false;
+  for (uint32_t v : d.reserved0)
+    if (v) return false;
+  for (uint64_t v : d.reserved)
+    if (v) return false;
+  if (d.tokens == 0 || d.tokens > 65536 || d.hidden == 0 || d.hidden % 256 || d.hidden > 16384)
+    return false;
+  if (d.experts == 0 || d.experts > 256 || d.top_k == 0 || d.top_k > 8) return false;
+  if (d.groups == 0 || d.groups > 32 || d.experts % d.groups) return false;
+  if (d.topk_groups == 0 || d.topk_groups > d.groups) return false;
+  if (d.top_k > (d.experts / d.groups) * d.topk_groups) return false;
+  return aligned(d.input_bf16, 16) && aligned(d.router_weight_bf16, 16) &&
+         aligned(d.router_bias_f32, 4) && aligned(d.route_experts_u16, 2) &&
+         aligned(d.route_weights_f32, 4) && aligned(d.compacted_tokens_u32, 4) &&
+         aligned(d.compacted_experts_u16, 2) && d.compacted_slots_u8 != 0 &&
+         aligned(d.compacted_weights_f32, 4) && aligned(d.expert_offsets_u32, 4) &&
+         aligned(d.workspace, 16);
+}
+}  // namespace
+
+uint64_t router_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k) {
+  Carve c;
+  RoutePlan r;
+  r.carve(c, tokens, experts, top_k);
+  return c.cursor + kAlign;
+}
+
+int32_t router_compact_launch(const glmaxx_router_descriptor* desc, void* cuda_stream,
+                              int32_t* async_err) {
+  if (desc == nullptr || async_err == nullptr) return GLMAXX_ERR_NULL;
+  *async_err = 0;
+  const glmaxx_router_descriptor& d = *desc;
+  if (!valid_router(d)) return GLMAXX_ERR_DESCRIPTOR;
+  if (d.workspace_bytes < router_workspace_bytes(d.tokens, d.experts, d.top_k))
+    return GLMAXX_ERR_DESCRIPTOR;
+  DeviceInfo info;
+  int32_t arch = current_device_info(&info);
+  if (arch != 0) return arch;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(cuda_stream);
+  Carve c;
+  RoutePlan r;
+  r.carve(c, d.tokens, d.experts, d.top_k);
+  const uint64_t ws = up(d.workspace, kAlign);
+  uint32_t* status = d.validation_error_u32 ? reinterpret_cast<uint32_t*>(d.validation_error_u32)
+                                            : at<uint32_t>(ws, r.status);
+  uint16_t* experts = reinterpret_cast<uint16_t*>(d.route_experts_u16);
+  float* weights = reinterpret_cast<float*>(d.route_weights_f32);
+  cudaError_t st = cudaMemsetAsync(status, 0, 4, stream);
+  if (st == cudaSuccess)
+    st = launch_router_logits(reinterpret_cast<const uint16_t*>(d.input_bf16),
+                              reinterpret_cast<const uint16_t*>(d.router_weight_bf16),
+                              at<float>(ws, r.partial), r.T, d.hidden, r.E,
+                              at<uint32_t>(ws, r.bitmap), r.E * r.W, stream);
+  if (st == cudaSuccess)
+    st = launch_router_select(at<float>(ws, r.partial),
+                              reinterpret_cast<const float*>(d.router_bias_f32), r.T, r.E,
+                              d.groups, d.topk_groups, r.K, d.route_scale, experts, weights,
+                              at<uint32_t>(ws, r.bitmap), r.W, status, stream);
+  // Offsets only: the n-tile list is not needed here (nt = 128, no tiles written).
+  if (st == cudaSuccess)
+    st = launch_compact(at<uint32_t>(ws, r.bitmap), r.T, r.E, 128, 0xffffffffu, 0xffffffffu,
+                        at<uint32_t>(ws, r.wprefix), at<uint32_t>(ws, r.counts),
+                        reinterpret_cast<uint32_t*>(d.expert_offsets_u32),
+                        at<uint32_t>(ws, r.poffs), nullptr, at<uint32_t>(ws, r.status) + 1,
+                        status, stream);
+  if (st == cudaSuccess) {
+    CompactWriteArgs a{};
+    a.route_experts = experts;
+    a.route_weights = weights;
+    a.bitmap = at<uint32_t>(ws, r.bitmap);
+    a.wprefix = at<uint32_t>(ws, r.wprefix);
+    a.offsets = reinterpret_cast<const uint32_t*>(d.expert_offsets_u32);
+    a.comp_token = reinterpret_cast<uint32_t*>(d.compacted_tokens_u32);
+    a.comp_expert = reinterpret_cast<uint16_t*>(d.compacted_experts_u16);
+    a.comp_slot = reinterpret_cast<uint8_t*>(d.compacted_slots_u8);
+    a.comp_weight = reinterpret_cast<float*>(d.compacted_weights_f32);
+    a.T = r.T;
+    a.E = r.E;
+    a.top_k = r.K;
+    st = launch_compact_write(a, stream);
+  }
+  return int32_t(st);
+}
+
+}  // namespace glmaxx

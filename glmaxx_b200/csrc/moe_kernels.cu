@@ -1,0 +1,860 @@
+// Routing, compaction, NVFP4 quantisation and combine kernels of the routed
+// MoE step (everything around the two grouped GEMMs).
+//
+// Data flow of one rank-local step (T tokens, H hidden, E experts, I local
+// intermediate, K = top_k):
+//   router_logits  x[T,H] bf16, Wr[E,H] bf16  -> partial[8][T][E] f32
+//   router_select  partial, bias              -> experts[T,K] u16, weights[T,K] f32,
+//                                                bitmap[E][ceil(T/32)] (token-in-expert bits)
+//   compact        bitmap                     -> counts, offsets, padded offsets, word
+//                                                prefixes, GEMM n-tile list
+//   quant_scatter  x, routes, prefixes        -> per-assignment NVFP4 rows in expert-
+//                                                contiguous, 128-padded "row space"
+//   (FC1 GEMM)                                -> h[row, I] bf16 (SwiGLU applied)
+//   fc2_quant      h                          -> NVFP4 rows of h
+//   (FC2 GEMM)                                -> plane[T][K][H] or atomics into out[T,H]
+//   combine        plane (+ shared expert)    -> out[T,H] f32
+//
+// Assignment order inside an expert is ascending token, i.e. the reference's
+// stable (expert, token, slot) compaction (crates/glm-reference/src/
+// routed_fc1.rs:20-58): a token's rank inside expert e is the number of
+// smaller tokens routed to e, read from the bitmap with popcounts.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "device.cuh"
+#include "moe.h"
+
+namespace glmaxx {
+
+// ---------------------------------------------------------------------------
+// Router logits.  Canonical order (shared with the CPU restatement):
+//   logit[t][e] = ((s_0 + s_1) + ...) + s_7,  s_c = fma-chain over the c-th
+//   eighth of H in ascending k from 0.
+// grid (E/32, ceil(T/32), 8), 256 threads: warp w -> experts e0+4w..e0+4w+3,
+// lane -> token t0+lane; both tiles staged in shared memory (padded pitch).
+// The first kernel of a step also clears the token-in-expert bitmap.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) router_logits_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
+    uint32_t T, uint32_t H, uint32_t E, uint32_t* __restrict__ bitmap, uint32_t bitmap_words) {
+  extern __shared__ uint32_t rsm[];
+  const uint32_t chunk_w = H / 16;  // 32-bit words (bf16 pairs) per chunk
+  const uint32_t pitch = chunk_w + 1;
+  uint32_t* xs = rsm;
+  uint32_t* ws = rsm + 32 * pitch;
+  const uint32_t e0 = blockIdx.x * 32, t0 = blockIdx.y * 32, c = blockIdx.z;
+  const uint32_t tid = threadIdx.x;
+  {
+    const uint64_t lin = (uint64_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const uint64_t nthreads = uint64_t(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
+    for (uint64_t i = lin * blockDim.x + tid; i < bitmap_words; i += nthreads) bitmap[i] = 0;
+  }
+  const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x);
+  const uint32_t* w32 = reinterpret_cast<const uint32_t*>(w);
+  for (uint32_t i = tid; i < 32 * chunk_w; i += 256) {
+    const uint32_t r = i / chunk_w, k = i % chunk_w;
+    const uint32_t tt = t0 + r, ee = e0 + r;
+    xs[r * pitch + k] = tt < T ? x32[uint64_t(tt) * (H / 2) + c * chunk_w + k] : 0u;
+    ws[r * pitch + k] = ee < E ? w32[uint64_t(ee) * (H / 2) + c * chunk_w + k] : 0u;
+  }
+  __syncthreads();
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint32_t* xr = xs + lane * pitch;
+  const uint32_t* wr = ws + (warp * 4) * pitch;
+#pragma unroll 4
+  for (uint32_t k = 0; k < chunk_w; ++k) {
+    const uint32_t xv = xr[k];
+    const float xl = __uint_as_float(xv << 16), xh = __uint_as_float(xv & 0xffff0000u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t wv = wr[j * pitch + k];
+      acc[j] = fmaf(xl, __uint_as_float(wv << 16), acc[j]);
+      acc[j] = fmaf(xh, __uint_as_float(wv & 0xffff0000u), acc[j]);
+    }
+  }
+  const uint32_t t = t0 + lane;
+  if (t < T) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t e = e0 + warp * 4 + j;
+      if (e < E) partial[(uint64_t(c) * T + t) * E + e] = acc[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Router selection, one warp per token (lane owns experts lane + 32j):
+//   s = sigmoid(logit), choice = s + bias; group score = top1 + top2 of choice;
+//   keep the best `topk_groups` groups; pick `top_k` experts by choice among
+//   them (slot order = descending choice, ties -> lower index);
+//   weight = (s / sum_slots s) * route_scale, the sum taken in slot order.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool better(float v, uint32_t e, float ov, uint32_t oe) {
+  return v > ov || (v == ov && e < oe);
+}
+
+__global__ void __launch_bounds__(256) router_select_kernel(
+    const float* __restrict__ partial, const float* __restrict__ bias, uint32_t T, uint32_t E,
+    uint32_t groups, uint32_t topk_groups, uint32_t top_k, float route_scale,
+    uint16_t* __restrict__ experts_out, float* __restrict__ weights_out,
+    uint32_t* __restrict__ bitmap, uint32_t bitmap_stride, uint32_t* __restrict__ status) {
+  __shared__ float gsm[8][32];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const uint32_t nj = (E + 31) / 32;
+  float s[8], ch[8];
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s[j] = 0.f;
+    ch[j] = -INFINITY;
+    const uint32_t e = lane + 32 * j;
+    if (j < nj && e < E) {
+      float L = partial[uint64_t(t) * E + e];
+#pragma unroll
+      for (int c = 1; c < 8; ++c) L = __fadd_rn(L, partial[(uint64_t(c) * T + t) * E + e]);
+      if (!isfinite(L)) bad = true;
+      s[j] = router_sigmoid(L);
+      ch[j] = __fadd_rn(s[j], bias[e]);
+    }
+  }
+  const uint32_t gs = E / groups;
+  for (uint32_t g = 0; g < groups; ++g) {
+    float t1 = -INFINITY, t2 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t e = lane + 32 * j;
+      if (j < nj && e < E && e / gs == g) {
+        const float v = ch[j];
+        if (v > t1) {
+          t2 = t1;
+          t1 = v;
+        } else if (v > t2) {
+          t2 = v;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, t1, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, t2, off);
+      if (o1 > t1) {
+        t2 = fmaxf(t1, o2);
+        t1 = o1;
+      } else {
+        t2 = fmaxf(t2, o1);
+      }
+    }
+    if (lane == 0) gsm[warp][g] = gs >= 2 ? __fadd_rn(t1, t2) : t1;
+  }
+  __syncwarp();
+  uint32_t gmask = 0;
+  for (uint32_t r = 0; r < topk_groups; ++r) {
+    float v = (lane < groups && !((gmask >> lane) & 1u)) ? gsm[warp][lane] : -INFINITY;
+    uint32_t gi = lane < groups && !((gmask >> lane) & 1u) ? lane : 0xffffffffu;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, gi, off);
+      if (better(ov, oi, v, gi)) {
+        v = ov;
+        gi = oi;
+      }
+    }
+    if (gi < groups) gmask |= 1u << gi;
+  }
+  uint32_t taken = 0;
+  uint32_t my_e = 0xffffffffu;
+  float my_s = 0.f;
+  float denom = 0.f;
+  for (uint32_t k = 0; k < top_k; ++k) {
+    float bv = -INFINITY, bs = 0.f;
+    uint32_t be = 0xffffffffu;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t e = lane + 32 * j;
+      if (j < nj && e < E && ((gmask >> (e / gs)) & 1u) && !((taken >> j) & 1u) &&
+          (be == 0xffffffffu || ch[j] > bv)) {
+        bv = ch[j];
+        bs = s[j];
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+      const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, off);
+      if (oe != 0xffffffffu && (be == 0xffffffffu || better(ov, oe, bv, be))) {
+        bv = ov;
+        bs = os;
+        be = oe;
+      }
+    }
+    if (be == 0xffffffffu) {
+      bad = true;
+      be = 0;
+    }
+    if ((be & 31u) == lane) taken |= 1u << (be >> 5);
+    denom = k == 0 ? bs : __fadd_rn(denom, bs);
+    if (lane == k) {
+      my_e = be;
+      my_s = bs;
+    }
+  }
+  if (lane < top_k) {
+    const float wgt = __fmul_rn(__fdiv_rn(my_s, denom), route_scale);
+    experts_out[uint64_t(t) * top_k + lane] = static_cast<uint16_t>(my_e);
+    weights_out[uint64_t(t) * top_k + lane] = wgt;
+    atomicOr(&bitmap[uint64_t(my_e) * bitmap_stride + t / 32], 1u << (t % 32));
+  }
+  if (bad && lane == 0 && status) atomicOr(status, kStatusNonFiniteInput);
+}
+
+// Routes supplied by the caller (dense [T][K]): validate and set bitmap bits.
+__global__ void routes_to_bitmap_kernel(const uint16_t* __restrict__ experts,
+                                        const float* __restrict__ weights, uint32_t T,
+                                        uint32_t E, uint32_t top_k, uint32_t* __restrict__ bitmap,
+                                        uint32_t bitmap_stride, uint32_t* __restrict__ status) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * top_k) return;
+  const uint32_t t = i / top_k;
+  const uint32_t e = experts[i];
+  const float w = weights[i];
+  uint32_t err = 0;
+  if (e >= E) err |= kStatusExpertOutOfRange;
+  if (!isfinite(w) || w < 0.f) err |= kStatusRouteWeightNotFinite;
+  if (err) {
+    atomicOr(status, err);
+    return;
+  }
+  const uint32_t prev = atomicOr(&bitmap[uint64_t(e) * bitmap_stride + t / 32], 1u << (t % 32));
+  if (prev & (1u << (t % 32))) atomicOr(status, kStatusDuplicateTokenSlot);
+}
+
+__global__ void zero_words_kernel(uint32_t* p, uint64_t n) {
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x)
+    p[i] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Compaction (single CTA, 1024 threads): per-expert counts and word prefixes
+// from the bitmap, exclusive offsets (plain and 128-padded), n-tile list.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) compact_kernel(
+    const uint32_t* __restrict__ bitmap, uint32_t W, uint32_t E, uint32_t nt, uint32_t sf_row_cap,
+    uint32_t max_tiles, uint32_t* __restrict__ wprefix, uint32_t* __restrict__ counts,
+    uint32_t* __restrict__ offsets, uint32_t* __restrict__ poffs, NTile* __restrict__ tiles,
+    uint32_t* __restrict__ tile_count, uint32_t* __restrict__ status) {
+  __shared__ uint32_t cnt_s[256], toff_s[257], poff_s[257], off_s[257];
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t e = warp; e < E; e += 32) {
+    uint32_t running = 0;
+    for (uint32_t w0 = 0; w0 < W; w0 += 32) {
+      const uint32_t w = w0 + lane;
+      const uint32_t pc = w < W ? __popc(bitmap[uint64_t(e) * W + w]) : 0;
+      uint32_t incl = pc;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      if (w < W) wprefix[uint64_t(e) * W + w] = running + incl - pc;
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) cnt_s[e] = running;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // each lane scans 8 consecutive experts; lane totals scanned across the warp
+    const uint32_t per = (E + 31) / 32;
+    uint32_t sc = 0, sp = 0, st = 0;
+    for (uint32_t q = 0; q < per; ++q) {
+      const uint32_t e = lane * per + q;
+      if (e < E) {
+        sc += cnt_s[e];
+        sp += (cnt_s[e] + 127) / 128 * 128;
+        st += (cnt_s[e] + nt - 1) / nt;
+      }
+    }
+    uint32_t ic = sc, ip = sp, it = st;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t a = __shfl_up_sync(0xffffffffu, ic, off);
+      const uint32_t b = __shfl_up_sync(0xffffffffu, ip, off);
+      const uint32_t c = __shfl_up_sync(0xffffffffu, it, off);
+      if (lane >= off) {
+        ic += a;
+        ip += b;
+        it += c;
+      }
+    }
+    uint32_t oc = ic - sc, op = ip - sp, ot = it - st;
+    for (uint32_t q = 0; q < per; ++q) {
+      const uint32_t e = lane * per + q;
+      if (e < E) {
+        offsets[e] = oc;
+        off_s[e] = oc;
+        poffs[e] = op;
+        poff_s[e] = op;
+        toff_s[e] = ot;
+        counts[e] = cnt_s[e];
+        oc += cnt_s[e];
+        op += (cnt_s[e] + 127) / 128 * 128;
+        ot += (cnt_s[e] + nt - 1) / nt;
+      }
+    }
+    if (lane == 31) {
+      offsets[E] = ic;
+      off_s[E] = ic;
+      poffs[E] = ip;
+      poff_s[E] = ip;
+      toff_s[E] = it;
+      const bool over = ip > sf_row_cap || it > max_tiles;
+      *tile_count = over ? 0u : it;
+      if (over && status) atomicOr(status, kStatusCapacityExceeded);
+    }
+  }
+  __syncthreads();
+  if (tiles == nullptr || poff_s[E] > sf_row_cap || toff_s[E] > max_tiles) return;
+  for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
+    const uint32_t c = cnt_s[e];
+    for (uint32_t j = 0; j * nt < c; ++j) {
+      NTile tl;
+      tl.expert = e;
+      tl.row_start = off_s[e] + j * nt;
+      tl.sf_row_start = poff_s[e] + j * nt;
+      tl.rows = min(nt, c - j * nt);
+      tiles[toff_s[e] + j] = tl;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FC1 input: NVFP4-quantise x[t] once (per-row global scale = amax/2688,
+// per-16 E4M3 scales, nvfp4.rs:170-273 arithmetic) and write it to each of the
+// token's K assignment rows.  One CTA per token, thread = one 64-wide k-block.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float r = lane < (blockDim.x + 31) / 32 ? red[lane] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) r = fmaxf(r, __shfl_xor_sync(0xffffffffu, r, off));
+    if (lane == 0) red[32] = r;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__global__ void __launch_bounds__(1024) quant_scatter_kernel(QuantScatterArgs a) {
+  __shared__ float red[33];
+  const uint32_t t = blockIdx.x, kb = threadIdx.x;
+  const uint32_t KB = a.H / 64;
+  const bool active = kb < KB;
+  float v[64];
+  float amax = 0.f;
+  bool finite = true;
+  if (active) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + uint64_t(t) * a.H + kb * 64);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = src[q];
+      const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[q * 8 + h * 2] = __uint_as_float(wds[h] << 16);
+        v[q * 8 + h * 2 + 1] = __uint_as_float(wds[h] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      finite = finite && isfinite(v[i]);
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+  if (!finite) atomicOr(a.status, kStatusNonFiniteInput);
+  amax = block_max(amax, red);
+  if (!active) return;
+  const float gscale = global_scale_of(amax);
+  uint2 packed[4];
+  uint32_t sfw = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
+  const uint32_t W = (a.T + 31) / 32;
+  for (uint32_t slot = 0; slot < a.top_k; ++slot) {
+    const uint32_t i = t * a.top_k + slot;
+    const uint32_t e = a.route_experts[i];
+    if (e >= a.E) continue;
+    const uint32_t word = a.bitmap[uint64_t(e) * W + t / 32];
+    const uint32_t rank = a.wprefix[uint64_t(e) * W + t / 32] + __popc(word & ((1u << (t % 32)) - 1u));
+    const uint32_t prow = a.poffs[e] + rank;  // scale-factor row
+    const uint32_t row = a.offsets[e] + rank;  // compacted row
+    if (prow >= a.sf_row_cap || row >= a.T * a.top_k) continue;
+    uint4* dst = reinterpret_cast<uint4*>(a.xq + uint64_t(row) * (a.H / 2) + kb * 32);
+    dst[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
+    dst[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
+    *reinterpret_cast<uint32_t*>(a.xsf + sf_offset(prow, kb, 0, KB)) = sfw;
+    if (kb == 0) {
+      a.row_token[row] = t;
+      a.row_slot[row] = slot;
+      a.row_weight[row] = a.route_weights[i];
+      a.row_gscale[row] = gscale;
+      a.row_prow[row] = prow;
+      a.route_row[i] = row;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FC2 input: NVFP4-quantise each assignment's h row (K = I).  Threads of one
+// row are KB2 = I/64 consecutive lanes (I <= 2048), amax by a segmented
+// butterfly.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) fc2_quant_kernel(Fc2QuantArgs a) {
+  const uint32_t KB2 = a.I / 64;
+  const uint32_t rows_per_block = 256 / KB2;
+  const uint32_t r_local = threadIdx.x / KB2, kb = threadIdx.x % KB2;
+  const uint32_t row = blockIdx.x * rows_per_block + r_local;
+  const uint32_t count = a.count_ptr ? min(*a.count_ptr, a.count) : a.count;
+  const bool active = row < count;
+  float v[64];
+  float amax = 0.f;
+  bool finite = true;
+  if (active) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.h + uint64_t(row) * a.I + kb * 64);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = src[q];
+      const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[q * 8 + h * 2] = __uint_as_float(wds[h] << 16);
+        v[q * 8 + h * 2 + 1] = __uint_as_float(wds[h] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      finite = finite && isfinite(v[i]);
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+  for (uint32_t off = 1; off < KB2; off <<= 1)
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if (!active) return;
+  if (!finite && a.status) atomicOr(a.status, kStatusNonFiniteInput);
+  const uint32_t prow = a.row_prow[row];
+  if (prow >= a.sf_row_cap) return;
+  const float gscale = global_scale_of(amax);
+  uint2 packed[4];
+  uint32_t sfw = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
+  uint4* dst = reinterpret_cast<uint4*>(a.hq + uint64_t(row) * (a.I / 2) + kb * 32);
+  dst[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
+  dst[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
+  *reinterpret_cast<uint32_t*>(a.hsf + sf_offset(prow, kb, 0, KB2)) = sfw;
+  if (kb == 0) a.gscale[row] = gscale;
+}
+
+// Compacted-order route arrays (reference ABI) from the device compaction.
+__global__ void compact_write_kernel(CompactWriteArgs a) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.T * a.top_k) return;
+  const uint32_t t = i / a.top_k, slot = i % a.top_k;
+  const uint32_t e = a.route_experts[i];
+  if (e >= a.E) return;
+  const uint32_t W = (a.T + 31) / 32;
+  const uint32_t word = a.bitmap[uint64_t(e) * W + t / 32];
+  const uint32_t rank = a.wprefix[uint64_t(e) * W + t / 32] + __popc(word & ((1u << (t % 32)) - 1u));
+  const uint32_t c = a.offsets[e] + rank;
+  a.comp_token[c] = t;
+  a.comp_expert[c] = static_cast<uint16_t>(e);
+  a.comp_slot[c] = static_cast<uint8_t>(slot);
+  a.comp_weight[c] = a.route_weights[i];
+}
+
+// Reference-ABI compacted routes -> padded offsets, per-row padded row, tiles.
+// Single CTA; expert_offsets must be non-decreasing with offsets[E] == A.
+__global__ void __launch_bounds__(1024) compat_prepare_kernel(CompatPrepareArgs a) {
+  __shared__ uint32_t poff_s[257], toff_s[257];
+  if (threadIdx.x < 32) {
+    const uint32_t lane = threadIdx.x;
+    const uint32_t per = (a.E + 31) / 32;
+    uint32_t sp = 0, st = 0;
+    bool bad = false;
+    for (uint32_t q = 0; q < per; ++q) {
+      const uint32_t e = lane * per + q;
+      if (e < a.E) {
+        const uint32_t b0 = a.offsets[e], b1 = a.offsets[e + 1];
+        if (b1 < b0 || b1 > a.A) bad = true;
+        const uint32_t c = b1 >= b0 ? b1 - b0 : 0;
+        sp += (c + 127) / 128 * 128;
+        st += (c + a.nt - 1) / a.nt;
+      }
+    }
+    uint32_t ip = sp, it = st;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t b = __shfl_up_sync(0xffffffffu, ip, off);
+      const uint32_t c = __shfl_up_sync(0xffffffffu, it, off);
+      if (lane >= off) {
+        ip += b;
+        it += c;
+      }
+    }
+    uint32_t op = ip - sp, ot = it - st;
+    for (uint32_t q = 0; q < per; ++q) {
+      const uint32_t e = lane * per + q;
+      if (e < a.E) {
+        const uint32_t b0 = a.offsets[e], b1 = a.offsets[e + 1];
+        const uint32_t c = b1 >= b0 ? b1 - b0 : 0;
+        a.poffs[e] = op;
+        poff_s[e] = op;
+        toff_s[e] = ot;
+        op += (c + 127) / 128 * 128;
+        ot += (c + a.nt - 1) / a.nt;
+      }
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 31) {
+      a.poffs[a.E] = ip;
+      poff_s[a.E] = ip;
+      toff_s[a.E] = it;
+      const bool over = bad || ip > a.sf_row_cap || it > a.max_tiles || a.offsets[0] != 0 ||
+                        a.offsets[a.E] != a.A;
+      *a.tile_count = over ? 0u : it;
+      if (over && a.status) atomicOr(a.status, kStatusCapacityExceeded);
+    }
+  }
+  __syncthreads();
+  if (*a.tile_count == 0) return;
+  for (uint32_t e = threadIdx.x; e < a.E; e += blockDim.x) {
+    const uint32_t b0 = a.offsets[e], c = a.offsets[e + 1] - b0;
+    const bool on = (a.expert_mask[e / 32] >> (e % 32)) & 1u;
+    for (uint32_t j = 0; j * a.nt < c; ++j) {
+      NTile tl;
+      tl.expert = e;
+      tl.row_start = b0 + j * a.nt;
+      tl.sf_row_start = poff_s[e] + j * a.nt;
+      tl.rows = on ? min(a.nt, c - j * a.nt) : 0;
+      a.tiles[toff_s[e] + j] = tl;
+    }
+  }
+  for (uint32_t r = threadIdx.x; r < a.A; r += blockDim.x) {
+    const uint32_t e = a.route_experts[r];
+    if (e < a.E && r >= a.offsets[e] && r < a.offsets[e + 1])
+      a.row_prow[r] = poff_s[e] + (r - a.offsets[e]);
+    else {
+      a.row_prow[r] = 0xffffffffu;
+      if (a.status) atomicOr(a.status, kStatusExpertOutOfRange);
+    }
+  }
+}
+
+// Reference-ABI quantiser, one CTA per compacted row, one thread per 64-wide
+// k-block (nvfp4_routed_fc1.cu:76-147 semantics, expert-local scale layout).
+__global__ void __launch_bounds__(1024) quant_rows_kernel(QuantRowsArgs a) {
+  __shared__ float red[33];
+  const uint32_t r = blockIdx.x, kb = threadIdx.x;
+  const uint32_t KB = a.K / 64;
+  const bool active = kb < KB;
+  const uint32_t sr = a.src_row ? a.src_row[r] : r;
+  const bool in_range = sr < a.src_rows;
+  float v[64];
+  float amax = 0.f;
+  bool finite = true;
+  if (active && in_range) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.src + uint64_t(sr) * a.K + kb * 64);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = src[q];
+      const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[q * 8 + h * 2] = __uint_as_float(wds[h] << 16);
+        v[q * 8 + h * 2 + 1] = __uint_as_float(wds[h] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      finite = finite && isfinite(v[i]);
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+  }
+  if (!finite && a.status) atomicOr(a.status, kStatusNonFiniteInput);
+  amax = block_max(amax, red);
+  if (!active || !in_range) return;
+  const uint32_t prow = a.row_prow[r];
+  if (prow >= a.sf_row_cap) return;
+  const float gscale = global_scale_of(amax);
+  uint2 packed[4];
+  uint32_t sfw = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
+  uint4* dst = reinterpret_cast<uint4*>(a.values + uint64_t(r) * (a.K / 2) + kb * 32);
+  dst[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
+  dst[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
+  *reinterpret_cast<uint32_t*>(a.scales + sf_offset(prow, kb, 0, KB)) = sfw;
+  if (kb == 0) a.gscale[r] = gscale;
+}
+
+__global__ void slot_table_kernel(SlotArgs a) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.A) return;
+  const uint32_t token = a.route_tokens[i], slot = a.route_slots[i];
+  uint32_t err = 0;
+  if (token >= a.rows) err |= kStatusRouteTokenOutOfRange;
+  if (slot >= a.top_k) err |= kStatusRouteSlotOutOfRange;
+  if (a.route_experts[i] >= a.E) err |= kStatusExpertOutOfRange;
+  if (!isfinite(a.route_weights[i])) err |= kStatusRouteWeightNotFinite;
+  if (err) {
+    atomicOr(a.status, err);
+    return;
+  }
+  if (atomicCAS(a.slot_assignment + uint64_t(token) * a.top_k + slot, 0xffffffffu, i) != 0xffffffffu)
+    atomicOr(a.status, kStatusDuplicateTokenSlot);
+}
+
+__global__ void slot_reduce_kernel(SlotArgs a) {
+  const uint64_t total = uint64_t(a.rows) * a.H;
+  for (uint64_t lin = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; lin < total;
+       lin += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t token = static_cast<uint32_t>(lin / a.H), col = static_cast<uint32_t>(lin % a.H);
+    float acc = 0.f;
+    for (uint32_t slot = 0; slot < a.top_k; ++slot) {
+      const uint32_t asg = a.slot_assignment[uint64_t(token) * a.top_k + slot];
+      if (asg != 0xffffffffu && asg < a.A)
+        acc = fmaf(a.route_weights[asg], a.assignment_down[uint64_t(asg) * a.H + col], acc);
+    }
+    a.token_output[lin] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Deterministic combine: out[t][c] = (sum over the token's slots in ascending
+// expert order of plane[t][slot][c]) + shared[t][c].  The ascending-expert
+// order is the reference oracle's compacted accumulation order
+// (routed_fc2.rs:63-86); routed + shared follows routed_fc2.rs:250-256.
+// ---------------------------------------------------------------------------
+__global__ void combine_kernel(const float* __restrict__ plane, const uint16_t* __restrict__ experts,
+                               const float* __restrict__ shared, float* __restrict__ out, uint32_t T,
+                               uint32_t H, uint32_t top_k) {
+  const uint32_t t = blockIdx.y;
+  const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (t >= T || c >= H) return;
+  uint32_t order[8];
+  uint32_t ex[8];
+  for (uint32_t s = 0; s < top_k; ++s) {
+    ex[s] = experts[uint64_t(t) * top_k + s];
+    order[s] = s;
+  }
+  for (uint32_t i = 1; i < top_k; ++i) {
+    const uint32_t o = order[i];
+    uint32_t j = i;
+    while (j > 0 && ex[order[j - 1]] > ex[o]) {
+      order[j] = order[j - 1];
+      --j;
+    }
+    order[j] = o;
+  }
+  float4 acc = *reinterpret_cast<const float4*>(plane + (uint64_t(t) * top_k + order[0]) * H + c);
+  for (uint32_t k = 1; k < top_k; ++k) {
+    const float4 v = *reinterpret_cast<const float4*>(plane + (uint64_t(t) * top_k + order[k]) * H + c);
+    acc.x = __fadd_rn(acc.x, v.x);
+    acc.y = __fadd_rn(acc.y, v.y);
+    acc.z = __fadd_rn(acc.z, v.z);
+    acc.w = __fadd_rn(acc.w, v.w);
+  }
+  if (shared) {
+    const float4 s = *reinterpret_cast<const float4*>(shared + uint64_t(t) * H + c);
+    acc.x = __fadd_rn(acc.x, s.x);
+    acc.y = __fadd_rn(acc.y, s.y);
+    acc.z = __fadd_rn(acc.z, s.z);
+    acc.w = __fadd_rn(acc.w, s.w);
+  }
+  *reinterpret_cast<float4*>(out + uint64_t(t) * H + c) = acc;
+}
+
+// ---------------------------------------------------------------------------
+// NVFP4 packer for weights (PackedNvfp4::pack, 1-D codec, nvfp4.rs:170-273) on
+// [batch][N][K] f32 or bf16 tensors with N % 128 == 0 and K % 64 == 0: pass 1
+// takes each tensor's amax, pass 2 encodes one 64-wide k-block per thread.
+// ---------------------------------------------------------------------------
+__global__ void pack_amax_kernel(const void* __restrict__ src, int src_bf16, uint64_t per_tensor,
+                                 uint32_t* __restrict__ amax_bits, uint32_t* __restrict__ status) {
+  const uint32_t b = blockIdx.y;
+  float m = 0.f;
+  bool finite = true;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < per_tensor;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const uint64_t j = uint64_t(b) * per_tensor + i;
+    const float v = src_bf16 ? bf16_to_f32(reinterpret_cast<const uint16_t*>(src)[j])
+                             : reinterpret_cast<const float*>(src)[j];
+    finite = finite && isfinite(v);
+    m = fmaxf(m, fabsf(v));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) atomicMax(&amax_bits[b], __float_as_uint(m));
+  if (!finite) atomicOr(status, kStatusNonFiniteInput);
+}
+
+__global__ void pack_encode_kernel(const void* __restrict__ src, int src_bf16, uint32_t N,
+                                   uint32_t K, const uint32_t* __restrict__ amax_bits,
+                                   uint8_t* __restrict__ values, uint8_t* __restrict__ scales,
+                                   float* __restrict__ global_scale,
+                                   float* __restrict__ global_amax) {
+  const uint32_t b = blockIdx.y;
+  const uint32_t KB = K / 64;
+  const uint64_t idx = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;
+  if (idx >= uint64_t(N) * KB) return;
+  const uint32_t row = static_cast<uint32_t>(idx / KB), kb = static_cast<uint32_t>(idx % KB);
+  const float amax = __uint_as_float(amax_bits[b]);
+  const float gscale = global_scale_of(amax);
+  float v[64];
+  const uint64_t base = (uint64_t(b) * N + row) * K + uint64_t(kb) * 64;
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    v[i] = src_bf16 ? bf16_to_f32(reinterpret_cast<const uint16_t*>(src)[base + i])
+                    : reinterpret_cast<const float*>(src)[base + i];
+  uint2 packed[4];
+  uint32_t sfw = 0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
+  uint8_t* vdst = values + uint64_t(b) * N * (K / 2) + uint64_t(row) * (K / 2) + kb * 32;
+  uint4* d4 = reinterpret_cast<uint4*>(vdst);
+  d4[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
+  d4[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
+  *reinterpret_cast<uint32_t*>(scales + uint64_t(b) * N * (K / 16) + sf_offset(row, kb, 0, KB)) = sfw;
+  if (idx == 0) {
+    global_scale[b] = gscale;
+    if (global_amax) global_amax[b] = amax;
+  }
+}
+
+// ------------------------------------------------------------- host launchers
+cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
+                                 uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,
+                                 cudaStream_t stream) {
+  const size_t smem = 2ull * 32 * (H / 16 + 1) * 4;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t st = cudaFuncSetAttribute(router_logits_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (st != cudaSuccess) return st;
+    configured = true;
+  }
+  dim3 grid((E + 31) / 32, (T + 31) / 32, 8);
+  router_logits_kernel<<<grid, 256, smem, stream>>>(x, w, partial, T, H, E, bitmap, bitmap_words);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_router_select(const float* partial, const float* bias, uint32_t T, uint32_t E,
+                                 uint32_t groups, uint32_t topk_groups, uint32_t top_k,
+                                 float route_scale, uint16_t* experts, float* weights,
+                                 uint32_t* bitmap, uint32_t bitmap_stride, uint32_t* status,
+                                 cudaStream_t stream) {
+  router_select_kernel<<<(T + 7) / 8, 256, 0, stream>>>(partial, bias, T, E, groups, topk_groups,
+                                                        top_k, route_scale, experts, weights,
+                                                        bitmap, bitmap_stride, status);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_routes_to_bitmap(const uint16_t* experts, const float* weights, uint32_t T,
+                                    uint32_t E, uint32_t top_k, uint32_t* bitmap,
+                                    uint32_t bitmap_words, uint32_t* status, cudaStream_t stream) {
+  zero_words_kernel<<<64, 256, 0, stream>>>(bitmap, bitmap_words);
+  const uint32_t n = T * top_k;
+  routes_to_bitmap_kernel<<<(n + 255) / 256, 256, 0, stream>>>(experts, weights, T, E, top_k,
+                                                               bitmap, (T + 31) / 32, status);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_compact(const uint32_t* bitmap, uint32_t T, uint32_t E, uint32_t nt,
+                           uint32_t sf_row_cap, uint32_t max_tiles, uint32_t* wprefix,
+                           uint32_t* counts, uint32_t* offsets, uint32_t* poffs, NTile* tiles,
+                           uint32_t* tile_count, uint32_t* status, cudaStream_t stream) {
+  compact_kernel<<<1, 1024, 0, stream>>>(bitmap, (T + 31) / 32, E, nt, sf_row_cap, max_tiles,
+                                         wprefix, counts, offsets, poffs, tiles, tile_count, status);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_compact_write(const CompactWriteArgs& a, cudaStream_t stream) {
+  const uint32_t n = a.T * a.top_k;
+  compact_write_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_compat_prepare(const CompatPrepareArgs& a, cudaStream_t stream) {
+  compat_prepare_kernel<<<1, 1024, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_quant_scatter(const QuantScatterArgs& a, cudaStream_t stream) {
+  const uint32_t threads = (a.H / 64 + 31) / 32 * 32;
+  quant_scatter_kernel<<<a.T, threads, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_fc2_quant(const Fc2QuantArgs& a, cudaStream_t stream) {
+  const uint32_t rows_per_block = 256 / (a.I / 64);
+  const uint32_t blocks = (a.count + rows_per_block - 1) / rows_per_block;
+  if (blocks == 0) return cudaSuccess;
+  fc2_quant_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_quant_rows(const QuantRowsArgs& a, cudaStream_t stream) {
+  if (a.A == 0) return cudaSuccess;
+  const uint32_t threads = (a.K / 64 + 31) / 32 * 32;
+  quant_rows_kernel<<<a.A, threads, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_slot_table(const SlotArgs& a, cudaStream_t stream) {
+  cudaError_t st = cudaMemsetAsync(a.slot_assignment, 0xff, uint64_t(a.rows) * a.top_k * 4, stream);
+  if (st != cudaSuccess) return st;
+  slot_table_kernel<<<(a.A + 255) / 256, 256, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_slot_reduce(const SlotArgs& a, cudaStream_t stream) {
+  const uint64_t total = uint64_t(a.rows) * a.H;
+  const uint64_t want = (total + 255) / 256;
+  const uint32_t blocks = static_cast<uint32_t>(want < 148 * 8 ? want : 148 * 8);
+  slot_reduce_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_combine(const float* plane, const uint16_t* experts, const float* shared,
+                           float* out, uint32_t T, uint32_t H, uint32_t top_k,
+                           cudaStream_t stream) {
+  dim3 grid((H / 4 + 255) / 256, T);
+  combine_kernel<<<grid, 256, 0, stream>>>(plane, experts, shared, out, T, H, top_k);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_pack(const void* src, int src_bf16, uint32_t batch, uint32_t N, uint32_t K,
+                        uint8_t* values, uint8_t* scales, float* global_scale, float* global_amax,
+                        uint32_t* amax_scratch, uint32_t* status, cudaStream_t stream) {
+  zero_words_kernel<<<1, 256, 0, stream>>>(amax_scratch, batch);
+  dim3 g1(64, batch);
+  pack_amax_kernel<<<g1, 256, 0, stream>>>(src, src_bf16, uint64_t(N) * K, amax_scratch, status);
+  const uint64_t work = uint64_t(N) * (K / 64);
+  dim3 g2(static_cast<uint32_t>((work + 127) / 128), batch);
+  pack_encode_kernel<<<g2, 128, 0, stream>>>(src, src_bf16, N, K, amax_scratch, values, scales,
+                                             global_scale, global_amax);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace glmaxx

@@ -1,0 +1,28 @@
+// Device properties cache and the architecture gate shared by the entry points.
+#pragma once
+
+#include <cstdint>
+
+struct glmaxx_moe_layer_descriptor;
+struct glmaxx_router_descriptor;
+
+namespace glmaxx {
+
+struct DeviceInfo {
+  int device;
+  int sms;
+  int major;
+  int minor;
+};
+
+// Fills `info` for the current device.  Returns 0, GLMAXX_ERR_WRONG_ARCH when
+// the device is not compute capability 10.x (B200 / sm_100a), or a cudaError_t.
+int32_t current_device_info(DeviceInfo* info);
+
+uint64_t layer_workspace_bytes(const glmaxx_moe_layer_descriptor& d);
+int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* stream, int32_t* async_err);
+uint64_t router_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k);
+int32_t router_compact_launch(const glmaxx_router_descriptor* desc, void* stream,
+                              int32_t* async_err);
+
+}  // namespace glmaxx

@@ -1,0 +1,416 @@
+/*
+ * glmaxx routed-MoE kernel library for NVIDIA B200 (sm_100a): C ABI.
+ *
+ * Drop-in replacement for the reference's kernel library
+ * (yatesdr/glmaxx kernels/include/glmaxx_kernel.h, bound from Rust in
+ * crates/glm-cuda/src/ffi.rs:21-151), shipped as libglmaxx_sm100.so.
+ *
+ *  - Descriptor structs keep the reference layouts byte for byte
+ *    (glmaxx_kernel.h:22-121; 224/224/144 bytes, 16-byte aligned, POSIX
+ *    ownership: the caller owns every buffer, pointers are device addresses
+ *    as uint64_t, launches are asynchronous on the caller's stream).
+ *  - Geometry fields (hidden, local_intermediate, experts, top_k) are honoured
+ *    instead of being pinned to the TP4 constants, so TP = 1/2/4/8 shards and
+ *    the 16-expert reduced layer run through the same entry points.
+ *  - Status convention (reference nvfp4_routed_fc1.cu:542-566): 0 success,
+ *    -1 null argument, -2 invalid descriptor or short workspace, -120 device is
+ *    not the supported architecture (here: compute capability 10.x), a positive
+ *    cudaError_t otherwise.  Device-detected problems are reported as bit flags
+ *    in the caller's validation word (bits 0..4 as the reference's FC2 word,
+ *    nvfp4_routed_fc2.cu:33-39; see GLMAXX_STATUS_* below).
+ *
+ * New in this library (ABI string "glmaxx.sm100.nvfp4.routed_moe.v3"):
+ *  - glmaxx_router_compact_launch: the protected router (manifest.rs:188-194)
+ *    and the stable (expert, token, slot) compaction (routed_fc1.rs:20-58) on
+ *    the device.
+ *  - glmaxx_moe_layer_launch: the full rank-local routed-MoE step (router,
+ *    compaction, NVFP4 quantisation, grouped FC1+SwiGLU, FC2 + weighted
+ *    combine, bf16 shared expert) producing the fp32 partial that the TP
+ *    all-reduce sums (manifest.rs:223-229).
+ *  - glmaxx_nvfp4_pack_launch: PackedNvfp4::pack (nvfp4.rs:170-273) on the GPU.
+ */
+#ifndef GLMAXX_KERNEL_H_
+#define GLMAXX_KERNEL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__cplusplus)
+extern "C" {
+#endif
+
+enum {
+  GLMAXX_FC1_ABI_VERSION = 1,
+  GLMAXX_FC2_ABI_VERSION = 1,
+  GLMAXX_EXL3_ABI_VERSION = 1,
+  GLMAXX_ROUTER_ABI_VERSION = 3,
+  GLMAXX_MOE_LAYER_ABI_VERSION = 3,
+  GLMAXX_FC1_DECODE_PERSISTENT = 1,
+  GLMAXX_FC1_PREFILL_GROUPED = 2,
+  GLMAXX_EXL3_GATE = 1,
+  GLMAXX_EXL3_UP = 2,
+  GLMAXX_EXL3_DOWN = 3,
+};
+
+/* Status codes returned by the launch functions. */
+enum {
+  GLMAXX_OK = 0,
+  GLMAXX_ERR_NULL = -1,
+  GLMAXX_ERR_DESCRIPTOR = -2,
+  GLMAXX_ERR_WRONG_ARCH = -120,
+};
+
+/* Bits of the device validation word. */
+enum {
+  GLMAXX_STATUS_ROUTE_TOKEN_OUT_OF_RANGE = 1u << 0,
+  GLMAXX_STATUS_ROUTE_SLOT_OUT_OF_RANGE = 1u << 1,
+  GLMAXX_STATUS_DUPLICATE_TOKEN_SLOT = 1u << 2,
+  GLMAXX_STATUS_EXPERT_OUT_OF_RANGE = 1u << 3,
+  GLMAXX_STATUS_ROUTE_WEIGHT_NOT_FINITE = 1u << 4,
+  GLMAXX_STATUS_NON_FINITE_INPUT = 1u << 5,
+  GLMAXX_STATUS_CAPACITY_EXCEEDED = 1u << 6,
+  GLMAXX_STATUS_WAIT_TIMEOUT = 1u << 8,
+  GLMAXX_STATUS_TMEM_TIMEOUT = 1u << 9,
+};
+
+/* Flags of glmaxx_moe_layer_descriptor.flags. */
+enum {
+  GLMAXX_MOE_ROUTES_GIVEN = 1u << 0,   /* route_experts/route_weights are inputs */
+  GLMAXX_MOE_SHARED_EXPERT = 1u << 1,  /* add the bf16 shared expert            */
+};
+
+/* glmaxx_kernel.h:22-57 (unchanged layout). */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_fc1_descriptor {
+#else
+struct glmaxx_fc1_descriptor {
+#endif
+  uint32_t abi_version;
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t path;
+  uint32_t rows;
+  uint32_t assignments;
+  uint32_t hidden;
+  uint32_t local_gate_up;
+  uint32_t local_intermediate;
+  uint32_t experts;
+  uint32_t top_k;
+  uint32_t reserved0;
+  uint64_t input_bf16;
+  uint64_t expert_value_base;
+  uint64_t expert_scale_base;
+  uint64_t expert_global_scales;
+  uint64_t route_experts_u16;
+  uint64_t route_tokens_u32;
+  uint64_t route_slots_u8;
+  uint64_t route_weights_f32;
+  uint64_t expert_offsets_u32;
+  uint64_t compacted_input_bf16;
+  uint64_t activation_values;
+  uint64_t activation_scales;
+  uint64_t activation_global_scales;
+  uint64_t gate_up_accum_f32;
+  uint64_t output_bf16;
+  uint64_t workspace_bytes;
+  uint64_t sequence;
+  uint64_t reserved[4];
+};
+
+/* glmaxx_kernel.h:59-95 (unchanged layout). */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_fc2_descriptor {
+#else
+struct glmaxx_fc2_descriptor {
+#endif
+  uint32_t abi_version;
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t path;
+  uint32_t rows;
+  uint32_t assignments;
+  uint32_t hidden;
+  uint32_t local_intermediate;
+  uint32_t experts;
+  uint32_t top_k;
+  uint32_t reserved0;
+  uint32_t reserved1;
+  uint64_t input_bf16;
+  uint64_t expert_value_base;
+  uint64_t expert_scale_base;
+  uint64_t expert_global_scales;
+  uint64_t route_experts_u16;
+  uint64_t route_tokens_u32;
+  uint64_t route_slots_u8;
+  uint64_t route_weights_f32;
+  uint64_t expert_offsets_u32;
+  uint64_t activation_values;
+  uint64_t activation_scales;
+  uint64_t activation_global_scales;
+  uint64_t assignment_down_f32;
+  uint64_t token_output_f32;
+  uint64_t slot_assignment_u32;
+  uint64_t validation_error_u32;
+  uint64_t workspace_bytes;
+  uint64_t sequence;
+  uint64_t reserved[4];
+};
+
+/* glmaxx_kernel.h:97-121 (unchanged layout). */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_exl3_descriptor {
+#else
+struct glmaxx_exl3_descriptor {
+#endif
+  uint32_t abi_version;
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t projection;
+  uint32_t rows;
+  uint32_t logical_k;
+  uint32_t logical_n;
+  uint32_t bits;
+  uint64_t input_f16;
+  uint64_t trellis_u16;
+  uint64_t suh_f16;
+  uint64_t svh_f16;
+  uint64_t rotated_input_f16;
+  uint64_t projected_f16;
+  uint64_t output_f16;
+  uint64_t validation_error_u32;
+  uint64_t workspace_bytes;
+  uint64_t sequence;
+  uint64_t reserved[4];
+};
+
+/*
+ * Router + compaction (new).  Replaces the host-side route preparation of the
+ * reference (crates/glm-cuda/src/ffi.rs:1692-1750 validate_case, which builds
+ * expert_offsets on the CPU) and the unbuilt router of manifest.rs:188-194.
+ * Outputs: dense routes [tokens][top_k] (slot order = descending choice
+ * score) and the compacted arrays in (expert, token, slot) order with
+ * expert_offsets[experts + 1], exactly the inputs of the FC1/FC2 descriptors.
+ */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_router_descriptor {
+#else
+struct glmaxx_router_descriptor {
+#endif
+  uint32_t abi_version;
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t tokens;
+  uint32_t hidden;
+  uint32_t experts;
+  uint32_t top_k;
+  uint32_t groups;
+  uint32_t topk_groups;
+  float route_scale;
+  uint32_t reserved0[2];
+  uint64_t input_bf16;          /* [tokens][hidden]                      */
+  uint64_t router_weight_bf16;  /* [experts][hidden]                     */
+  uint64_t router_bias_f32;     /* [experts] e_score_correction_bias      */
+  uint64_t route_experts_u16;   /* out [tokens][top_k]                    */
+  uint64_t route_weights_f32;   /* out [tokens][top_k]                    */
+  uint64_t compacted_tokens_u32;   /* out [tokens*top_k]                  */
+  uint64_t compacted_experts_u16;  /* out [tokens*top_k]                  */
+  uint64_t compacted_slots_u8;     /* out [tokens*top_k]                  */
+  uint64_t compacted_weights_f32;  /* out [tokens*top_k]                  */
+  uint64_t expert_offsets_u32;  /* out [experts + 1]                      */
+  uint64_t validation_error_u32;
+  uint64_t workspace;
+  uint64_t workspace_bytes;
+  uint64_t sequence;
+  uint64_t reserved[4];
+};
+
+/*
+ * Full rank-local routed-MoE step (new).  Weights are in the reference's
+ * packed rank layout: per expert, gate/up NVFP4 [2*local_intermediate][hidden]
+ * (rank-local gate rows, then up rows: nvfp4-physical-abi.md:18-28) and down
+ * NVFP4 [hidden][local_intermediate]; values row-major, two codes per byte
+ * (even element in the low nibble), scales in the 128x4 atom layout of
+ * nvfp4.rs:493-521, one fp32 global scale per tensor.  Experts are contiguous:
+ * expert e's gate/up values start at w13_values + e * 2*I*H/2, and so on.
+ * Shared expert (optional): bf16 gate/up [2*shared_intermediate][hidden] and
+ * down [hidden][shared_intermediate] rank shards (checkpoint.rs:1408-1436).
+ * Output: fp32 partial [tokens][hidden] = routed + shared (routed_fc2.rs:
+ * 250-256), the operand of the TP all-reduce.
+ */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_moe_layer_descriptor {
+#else
+struct glmaxx_moe_layer_descriptor {
+#endif
+  uint32_t abi_version;
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t path; /* 0 = auto, GLMAXX_FC1_DECODE_PERSISTENT, GLMAXX_FC1_PREFILL_GROUPED */
+  uint32_t tokens;
+  uint32_t hidden;
+  uint32_t experts;
+  uint32_t local_intermediate;
+  uint32_t top_k;
+  uint32_t groups;
+  uint32_t topk_groups;
+  float route_scale;
+  uint32_t shared_intermediate;
+  uint32_t reserved0[3];
+  uint64_t input_bf16;
+  uint64_t router_weight_bf16;
+  uint64_t router_bias_f32;
+  uint64_t w13_values;
+  uint64_t w13_scales;
+  uint64_t w13_global_f32;
+  uint64_t w2_values;
+  uint64_t w2_scales;
+  uint64_t w2_global_f32;
+  uint64_t shared13_bf16;
+  uint64_t shared2_bf16;
+  uint64_t route_experts_u16;
+  uint64_t route_weights_f32;
+  uint64_t output_f32;
+  uint64_t validation_error_u32;
+  uint64_t workspace;
+  uint64_t workspace_bytes;
+  uint64_t sequence;
+  uint64_t reserved[4];
+};
+
+/* ---- reference entry points (glmaxx_kernel.h:123-250) ---- */
+int32_t glmaxx_nvfp4_routed_fc1_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                       void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_routed_fc1_graph_instantiate(const struct glmaxx_fc1_descriptor* descriptor,
+                                                  void* cuda_stream, uint64_t* graph_exec);
+int32_t glmaxx_nvfp4_quantize_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                     void* cuda_stream);
+int32_t glmaxx_nvfp4_grouped_quantize_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                             void* cuda_stream);
+int32_t glmaxx_nvfp4_core_swiglu_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                        void* cuda_stream);
+int32_t glmaxx_nvfp4_dense_control_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                          uint32_t expert, void* cuda_stream,
+                                          int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_grouped_control_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                            const uint16_t* active_experts,
+                                            uint32_t active_expert_count, void* cuda_stream,
+                                            int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_grouped_core_swiglu_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                                const uint16_t* active_experts,
+                                                uint32_t active_expert_count, void* cuda_stream,
+                                                int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_grouped_prepare_launch(const struct glmaxx_fc1_descriptor* descriptor,
+                                            const uint16_t* active_experts,
+                                            uint32_t active_expert_count, void* cuda_stream);
+int32_t glmaxx_nvfp4_grouped_prepared_control_launch(
+    const struct glmaxx_fc1_descriptor* descriptor, uint32_t active_expert_count,
+    void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_grouped_prepared_core_swiglu_launch(
+    const struct glmaxx_fc1_descriptor* descriptor, uint32_t active_expert_count,
+    void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_routed_fc2_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                       void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_fc2_quantize_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                         void* cuda_stream);
+int32_t glmaxx_nvfp4_fc2_grouped_quantize_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                                 void* cuda_stream);
+int32_t glmaxx_nvfp4_fc2_core_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                     void* cuda_stream);
+int32_t glmaxx_nvfp4_fc2_reduce_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                       void* cuda_stream);
+int32_t glmaxx_nvfp4_fc2_dense_control_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                              uint32_t expert, void* cuda_stream,
+                                              int32_t* asynchronous_error);
+int32_t glmaxx_nvfp4_fc2_grouped_control_launch(const struct glmaxx_fc2_descriptor* descriptor,
+                                                const uint16_t* active_experts,
+                                                uint32_t active_expert_count, void* cuda_stream,
+                                                int32_t* asynchronous_error);
+int32_t glmaxx_exl3_projection_launch(const struct glmaxx_exl3_descriptor* descriptor,
+                                      void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_graph_exec_launch(uint64_t graph_exec, uint64_t stream);
+int32_t glmaxx_graph_exec_destroy(uint64_t graph_exec);
+int32_t glmaxx_event_create(uint64_t* event);
+int32_t glmaxx_event_record(uint64_t event, uint64_t stream);
+int32_t glmaxx_event_synchronize(uint64_t event);
+int32_t glmaxx_event_elapsed_ms(uint64_t start, uint64_t end, float* milliseconds);
+int32_t glmaxx_event_destroy(uint64_t event);
+int32_t glmaxx_profiler_start(void);
+int32_t glmaxx_profiler_stop(void);
+int32_t glmaxx_nvtx_range_push(const char* message);
+int32_t glmaxx_nvtx_range_pop(void);
+
+/* Workspace sizes for the reference GLM-5.2 TP4 geometry (hidden 6144, local
+ * intermediate 512, 256 experts), as the reference defines them
+ * (nvfp4_routed_fc1.cu:346-368, nvfp4_routed_fc2.cu:512-544). */
+uint64_t glmaxx_nvfp4_routed_fc1_workspace_bytes(uint32_t assignments);
+uint64_t glmaxx_nvfp4_grouped_workspace_bytes(uint32_t assignments);
+uint64_t glmaxx_nvfp4_routed_fc2_workspace_bytes(uint32_t rows, uint32_t assignments);
+uint64_t glmaxx_nvfp4_grouped_fc2_workspace_bytes(uint32_t rows, uint32_t assignments);
+uint64_t glmaxx_exl3_projection_workspace_bytes(uint32_t rows, uint32_t logical_k,
+                                                uint32_t logical_n);
+const char* glmaxx_kernel_abi(void);
+const char* glmaxx_exl3_kernel_abi(void);
+
+/* Runtime helpers (glmaxx_kernel.h:221-250, same signatures). */
+int32_t glmaxx_device_count(int32_t* count);
+int32_t glmaxx_device_bind(int32_t device_index, int32_t* compute_capability,
+                           int32_t* multiprocessor_count, uint64_t* total_memory_bytes,
+                           uint8_t device_uuid[16]);
+int32_t glmaxx_device_memory_info(uint64_t* free_memory_bytes, uint64_t* total_memory_bytes);
+int32_t glmaxx_device_alloc(uint64_t bytes, uint64_t* pointer);
+int32_t glmaxx_device_free(uint64_t pointer);
+int32_t glmaxx_pinned_alloc(uint64_t bytes, uint64_t* pointer);
+int32_t glmaxx_pinned_free(uint64_t pointer);
+int32_t glmaxx_stream_create(uint64_t* stream);
+int32_t glmaxx_stream_destroy(uint64_t stream);
+int32_t glmaxx_stream_query(uint64_t stream, int32_t* complete);
+int32_t glmaxx_stream_synchronize(uint64_t stream);
+int32_t glmaxx_memcpy_h2d(uint64_t destination, const void* source, uint64_t bytes,
+                          uint64_t stream);
+int32_t glmaxx_memcpy_d2d(uint64_t destination, uint64_t source, uint64_t bytes, uint64_t stream);
+int32_t glmaxx_memcpy_d2h(void* destination, uint64_t source, uint64_t bytes, uint64_t stream);
+int32_t glmaxx_memset_zero(uint64_t destination, uint64_t bytes, uint64_t stream);
+
+/* ---- new entry points ---- */
+
+/* Geometry-aware workspace sizes (replace the fixed-geometry formulas above
+ * for TP != 4 and for the 16-expert reduced layer). */
+uint64_t glmaxx_nvfp4_routed_fc1_workspace_bytes_v3(uint32_t rows, uint32_t assignments,
+                                                    uint32_t hidden, uint32_t local_intermediate,
+                                                    uint32_t experts, uint32_t top_k);
+uint64_t glmaxx_nvfp4_routed_fc2_workspace_bytes_v3(uint32_t rows, uint32_t assignments,
+                                                    uint32_t hidden, uint32_t local_intermediate,
+                                                    uint32_t experts, uint32_t top_k);
+uint64_t glmaxx_router_workspace_bytes(uint32_t tokens, uint32_t hidden, uint32_t experts,
+                                       uint32_t top_k);
+uint64_t glmaxx_moe_layer_workspace_bytes(const struct glmaxx_moe_layer_descriptor* descriptor);
+
+int32_t glmaxx_router_compact_launch(const struct glmaxx_router_descriptor* descriptor,
+                                     void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_moe_layer_launch(const struct glmaxx_moe_layer_descriptor* descriptor,
+                                void* cuda_stream, int32_t* asynchronous_error);
+
+/* PackedNvfp4::pack (1-D codec) of `batch` row-major [n][k] tensors (f32 when
+ * src_is_bf16 == 0, else bf16), n % 128 == 0, k % 64 == 0.  Tensor b writes
+ * values + b*n*k/2, scales + b*n*k/16, global_scale[b], global_amax[b]
+ * (global_amax may be 0).  scratch: >= 4*batch bytes of device memory. */
+int32_t glmaxx_nvfp4_pack_launch(uint64_t src, int32_t src_is_bf16, uint32_t batch, uint32_t n,
+                                 uint32_t k, uint64_t values, uint64_t scales,
+                                 uint64_t global_scale_f32, uint64_t global_amax_f32,
+                                 uint64_t scratch, uint64_t validation_error_u32,
+                                 void* cuda_stream);
+
+#if defined(__cplusplus)
+}
+
+static_assert(sizeof(glmaxx_fc1_descriptor) == 224, "Rust/C descriptor size mismatch");
+static_assert(alignof(glmaxx_fc1_descriptor) == 16, "Rust/C descriptor alignment mismatch");
+static_assert(sizeof(glmaxx_fc2_descriptor) == 224, "Rust/C FC2 descriptor size mismatch");
+static_assert(alignof(glmaxx_fc2_descriptor) == 16, "Rust/C FC2 descriptor alignment mismatch");
+static_assert(sizeof(glmaxx_exl3_descriptor) == 144, "Rust/C EXL3 descriptor size mismatch");
+static_assert(alignof(glmaxx_exl3_descriptor) == 16, "Rust/C EXL3 descriptor alignment mismatch");
+static_assert(sizeof(glmaxx_router_descriptor) == 192, "router descriptor size");
+static_assert(sizeof(glmaxx_moe_layer_descriptor) == 240, "layer descriptor size");
+#endif
+
+#endif /* GLMAXX_KERNEL_H_ */

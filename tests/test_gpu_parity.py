@@ -1,0 +1,209 @@
+"""GPU parity of the sm_100a path against the CPU oracle (calls go through the C ABI).
+
+Bit-exact: NVFP4 packing (against the reference golden hashes and the oracle),
+routing indices/weights and compaction.  Layer outputs: rel-L2 <= 1e-3 and
+max-abs <= 4 bf16 ulp of the output scale (tests/gpu_util.py).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from glmaxx_b200 import abi, synth
+from glmaxx_b200.moe import MoEConfig, RoutedMoE, pack_nvfp4
+
+from gpu_util import assert_layer_close, cuda, rel_l2, to_np_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _packed_to_oracle(p, b=0):
+    return O.Packed(p.values[b].cpu().numpy().ravel(), p.scales[b].cpu().numpy().ravel(),
+                    float(p.global_scale[b]), float(p.global_amax[b]), p.n, p.k, "1d")
+
+
+def test_gpu_packer_actual_shape_golden(golden):
+    g = golden["actual_shape"]
+    w = torch.from_numpy(O.actual_shape_values(g["n"], g["k"])).to(cuda())
+    p = pack_nvfp4(w)
+    torch.cuda.synchronize()
+    assert _packed_to_oracle(p).sha256() == g["packed_sha256"]
+
+
+@pytest.mark.parametrize("case", O.NUMERICAL_CASES)
+def test_gpu_packer_matrix_golden(golden, case):
+    mp = golden["matrix_proof"]
+    n, k, _ = mp["model_shape"]
+    entry = next(e for e in mp["numerical"] if e["case"] == case)
+    _, w = O.generate_numerical_fixture(case, 1, n, k)
+    p = pack_nvfp4(torch.from_numpy(w).to(cuda()))
+    assert _packed_to_oracle(p).sha256() == entry["packed_weight_sha256"]
+
+
+def test_gpu_packer_random_bf16_matches_oracle():
+    rng = np.random.default_rng(7)
+    w = (rng.standard_normal((3, 256, 512)) * rng.choice([1e-3, 1.0, 300.0], (3, 1, 1)))
+    wb = O.bf16_round(w.astype(np.float32))
+    t = torch.from_numpy(wb).to(cuda()).to(torch.bfloat16)
+    p = pack_nvfp4(t)
+    for b in range(3):
+        ref = O.pack(wb[b])
+        got = _packed_to_oracle(p, b)
+        assert np.array_equal(got.values, ref.values)
+        assert np.array_equal(got.scales, ref.scales)
+        assert got.global_scale == ref.global_scale
+
+
+def _router_case(T, H, E, groups, topk_groups, seed):
+    rng = np.random.default_rng(seed)
+    x = O.f32_to_bf16_bits(rng.standard_normal((T, H)).astype(np.float32))
+    w = O.f32_to_bf16_bits((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
+    bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+    return x, w, bias
+
+
+@pytest.mark.parametrize("T,E,groups,topk_groups", [(64, 256, 8, 4), (8, 16, 1, 1), (333, 256, 8, 4)])
+def test_gpu_router_compact_bit_exact(T, E, groups, topk_groups):
+    H, K = 6144, 8
+    dev = cuda()
+    x, w, bias = _router_case(T, H, E, groups, topk_groups, seed=T + E)
+    ref_e, ref_w = O.router(x, w, bias, groups, topk_groups, K, 2.5)
+    xd = torch.from_numpy(x.view(np.int16)).to(dev)
+    wd = torch.from_numpy(w.view(np.int16)).to(dev)
+    bd = torch.from_numpy(bias).to(dev)
+    re = torch.empty((T, K), dtype=torch.int16, device=dev)
+    rw = torch.empty((T, K), dtype=torch.float32, device=dev)
+    ct = torch.empty(T * K, dtype=torch.int32, device=dev)
+    ce = torch.empty(T * K, dtype=torch.int16, device=dev)
+    cs = torch.empty(T * K, dtype=torch.uint8, device=dev)
+    cw = torch.empty(T * K, dtype=torch.float32, device=dev)
+    off = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = abi.load()
+    wsb = int(L.glmaxx_router_workspace_bytes(T, H, E, K))
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    d = abi.RouterDescriptor.new(
+        abi_version=abi.ROUTER_ABI_VERSION, tokens=T, hidden=H, experts=E, top_k=K, groups=groups,
+        topk_groups=topk_groups, route_scale=2.5, input_bf16=xd.data_ptr(),
+        router_weight_bf16=wd.data_ptr(), router_bias_f32=bd.data_ptr(),
+        route_experts_u16=re.data_ptr(), route_weights_f32=rw.data_ptr(),
+        compacted_tokens_u32=ct.data_ptr(), compacted_experts_u16=ce.data_ptr(),
+        compacted_slots_u8=cs.data_ptr(), compacted_weights_f32=cw.data_ptr(),
+        expert_offsets_u32=off.data_ptr(), validation_error_u32=st.data_ptr(),
+        workspace=ws.data_ptr(), workspace_bytes=wsb)
+    err = ctypes.c_int32(0)
+    abi.check(L.glmaxx_router_compact_launch(
+        ctypes.byref(d), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+        ctypes.byref(err)), "router")
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    got_e = re.cpu().numpy().view(np.uint16)
+    got_w = rw.cpu().numpy()
+    assert np.array_equal(got_e, ref_e)
+    assert np.array_equal(got_w.view(np.uint32), ref_w.view(np.uint32))
+    routes = O.routes_array([(t, int(ref_e[t, s]), s, float(ref_w[t, s]))
+                             for t in range(T) for s in range(K)])
+    comp = O.compact_routes(routes, T)
+    assert np.array_equal(ct.cpu().numpy().view(np.uint32), comp["token"])
+    assert np.array_equal(ce.cpu().numpy().view(np.uint16), comp["expert"])
+    assert np.array_equal(cs.cpu().numpy(), comp["slot"])
+    counts = np.bincount(comp["expert"], minlength=E)
+    assert np.array_equal(off.cpu().numpy().view(np.uint32), np.concatenate([[0], np.cumsum(counts)]))
+
+
+def _oracle_layer(layer: RoutedMoE, x: torch.Tensor, cfg: MoEConfig, subset=None):
+    w = layer.w
+    xb = to_np_bf16_bits(x)
+    re, rw = layer.routes(x.shape[0])
+    re = re.cpu().numpy().view(np.uint16)
+    rw = rw.cpu().numpy()
+    routed, shared = O.moe_layer(
+        xb, re, rw, w.w13.values.cpu().numpy(), w.w13.scales.cpu().numpy(),
+        w.w13.global_scale.cpu().numpy(), w.w2.values.cpu().numpy(), w.w2.scales.cpu().numpy(),
+        w.w2.global_scale.cpu().numpy(), cfg.local_intermediate,
+        None if w.shared13 is None else to_np_bf16_bits(w.shared13),
+        None if w.shared2 is None else to_np_bf16_bits(w.shared2), token_subset=subset)
+    return O.finish_sparse_layer(None, None, routed[None], shared[None])
+
+
+def _check_routes(layer, x, cfg):
+    xb = to_np_bf16_bits(x)
+    ref_e, ref_w = O.router(xb, to_np_bf16_bits(layer.w.router_weight),
+                            layer.w.router_bias.cpu().numpy(), cfg.groups, cfg.topk_groups,
+                            cfg.top_k, cfg.route_scale)
+    got_e, got_w = layer.routes(x.shape[0])
+    assert np.array_equal(got_e.cpu().numpy().view(np.uint16), ref_e)
+    assert np.array_equal(got_w.cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
+
+
+def test_gpu_layer_reduced_config0():
+    """T=8, E=16, top-8 (no groups), I=2048, NVFP4 W4A4."""
+    cfg = MoEConfig(experts=16, groups=1, topk_groups=1, shared_intermediate=0)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=3, device=dev)
+    x = synth.make_input(8, cfg.hidden, seed=3, device=dev)
+    layer = RoutedMoE(cfg, w, 8)
+    out = layer(x)
+    torch.cuda.synchronize()
+    assert layer.device_status() == []
+    _check_routes(layer, x, cfg)
+    ref = _oracle_layer(layer, x, cfg)
+    assert_layer_close(out.cpu().numpy(), ref, "config0")
+
+
+@pytest.mark.parametrize("tp,rank", [(1, 0), (4, 3)])
+def test_gpu_layer_decode_config1(tp, rank):
+    """BASELINE configs[1] shapes: T=64, E=256, 8 groups/top-4, shared expert, TP shard."""
+    cfg = MoEConfig(tp=tp, rank=rank)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=11, device=dev)
+    x = synth.make_input(64, cfg.hidden, seed=11, device=dev)
+    layer = RoutedMoE(cfg, w, 64)
+    out = layer(x)
+    torch.cuda.synchronize()
+    assert layer.device_status() == []
+    _check_routes(layer, x, cfg)
+    ref = _oracle_layer(layer, x, cfg)
+    assert_layer_close(out.cpu().numpy(), ref, f"decode tp{tp} r{rank}")
+
+
+def test_gpu_layer_prefill_path_subset():
+    """Prefill path (N tile 128, atomic combine) on T=1024, checked on a token subset."""
+    cfg = MoEConfig(tp=2, rank=1)
+    dev = cuda()
+    T = 1024
+    w = synth.make_rank_weights(cfg, seed=5, device=dev)
+    x = synth.make_input(T, cfg.hidden, seed=5, device=dev)
+    layer = RoutedMoE(cfg, w, T)
+    out = layer(x, path=abi.PREFILL_GROUPED)
+    torch.cuda.synchronize()
+    assert layer.device_status() == []
+    subset = np.arange(0, T, 37, dtype=np.uint32)
+    ref = _oracle_layer(layer, x, cfg, subset=subset)
+    assert_layer_close(out.cpu().numpy()[subset], ref, "prefill subset")
+
+
+def test_gpu_layer_decode_and_prefill_paths_agree():
+    cfg = MoEConfig(tp=8, rank=0)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=9, device=dev)
+    x = synth.make_input(96, cfg.hidden, seed=9, device=dev)
+    layer = RoutedMoE(cfg, w, 96)
+    a = layer(x, path=abi.DECODE_PERSISTENT).clone()
+    b = layer(x, path=abi.PREFILL_GROUPED).clone()
+    torch.cuda.synchronize()
+    assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
+
+
+def test_gpu_layer_deterministic_decode():
+    cfg = MoEConfig(tp=4, rank=0)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=2, device=dev)
+    x = synth.make_input(64, cfg.hidden, seed=2, device=dev)
+    layer = RoutedMoE(cfg, w, 64)
+    outs = [layer(x).clone() for _ in range(5)]
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
