@@ -22,6 +22,9 @@ MOE_LAYER_ABI_VERSION = 3
 DECODE_PERSISTENT = 1
 PREFILL_GROUPED = 2
 EXL3_GATE, EXL3_UP, EXL3_DOWN = 1, 2, 3
+PLANES = {"fc1_output_bf16": 0, "row_token_u32": 1, "row_slot_u32": 2, "row_weight_f32": 3,
+          "expert_offsets_u32": 4, "shared_f32": 5}
+LAYER_STAGES = ["router", "compact", "quant", "fc1", "fc2_quant", "shared", "fc2", "combine"]
 MOE_ROUTES_GIVEN = 1 << 0
 MOE_SHARED_EXPERT = 1 << 1
 
@@ -192,6 +195,8 @@ SIGNATURES = {
     "glmaxx_moe_layer_workspace_bytes": (u64, [_P]),
     "glmaxx_router_compact_launch": (ctypes.c_int32, [_P, _P, _I32P]),
     "glmaxx_moe_layer_launch": (ctypes.c_int32, [_P, _P, _I32P]),
+    "glmaxx_moe_layer_set_stage_events": (ctypes.c_int32, [_U64P, u32]),
+    "glmaxx_moe_layer_plane": (ctypes.c_int32, [_P, u32, _U64P, _U64P]),
     "glmaxx_nvfp4_pack_launch": (ctypes.c_int32, [u64, ctypes.c_int32, u32, u32, u32, u64, u64,
                                                   u64, u64, u64, u64, _P]),
 }

@@ -137,8 +137,10 @@ struct Fc1Plan {
   GemmVariant variant;
   uint64_t sf_rows;
   bool build(const glmaxx_fc1_descriptor& d) {
-    nt = d.path == GLMAXX_FC1_DECODE_PERSISTENT ? 32 : 128;
-    variant = nt == 32 ? kFc1DecodeFp4 : kFc1PrefillFp4;
+    // 128-row tiles keep the scale plane within the reference's grouped SFA
+    // capacity (A + 127 * min(A, E) rows) for any per-expert count.
+    nt = 128;
+    variant = kFc1PrefillFp4;
     sf_rows = round128(grouped_sf_rows(d.assignments, d.experts));
     s.carve(d.compacted_input_bf16 + kFc1ScratchOffset, d.assignments, d.experts, nt);
     const uint64_t plane = uint64_t(d.assignments) * d.hidden * 2;
@@ -353,6 +355,15 @@ int32_t glmaxx_moe_layer_launch(const glmaxx_moe_layer_descriptor* descriptor, v
   return moe_layer_launch(descriptor, cuda_stream, asynchronous_error);
 }
 
+int32_t glmaxx_moe_layer_set_stage_events(uint64_t* events, uint32_t count) {
+  return set_stage_events(events, count);
+}
+
+int32_t glmaxx_moe_layer_plane(const glmaxx_moe_layer_descriptor* descriptor, uint32_t which,
+                               uint64_t* address, uint64_t* bytes) {
+  return layer_plane(descriptor, which, address, bytes);
+}
+
 int32_t glmaxx_nvfp4_routed_fc1_launch(const glmaxx_fc1_descriptor* descriptor, void* cuda_stream,
                                        int32_t* asynchronous_error) {
   if (asynchronous_error == nullptr) return GLMAXX_ERR_NULL;
@@ -479,7 +490,7 @@ struct Fc2Plan {
   uint32_t nt;
   uint64_t sf_rows;
   bool build(const glmaxx_fc2_descriptor& d) {
-    nt = d.path == GLMAXX_FC1_DECODE_PERSISTENT ? 32 : 128;
+    nt = 128;
     sf_rows = round128(grouped_sf_rows(d.assignments, d.experts));
     s.carve(d.token_output_f32, d.assignments, d.experts, nt);
     return s.bytes + 256 <= uint64_t(d.rows) * d.hidden * 4;

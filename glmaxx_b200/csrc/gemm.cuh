@@ -28,9 +28,11 @@ namespace glmaxx {
 
 // One N tile of a grouped GEMM: up to NT consecutive B rows of one expert.
 // B values and per-row metadata are in compacted (expert, token, slot) row
-// order; B scale factors live in the expert-local 128-padded row space of the
-// reference's grouped SFA plan (crates/glm-cuda/src/abi.rs:44-91), where every
-// expert's rows start on a 128-row atom boundary.
+// order.  B scale factors live in a padded row space in which every N tile
+// owns whole 128-row scale atoms starting at sf_row_start (a multiple of 128),
+// so the tile's scales enter TMEM at column 0 of the atom.  With NT = 128 this
+// is exactly the reference's expert-local grouped SFA plan
+// (crates/glm-cuda/src/abi.rs:44-91).
 struct NTile {
   uint32_t expert;        // expert index (A operand slab)
   uint32_t row_start;     // first B row (compacted row space)
@@ -232,9 +234,6 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
       for (uint32_t item = blockIdx.x; ok && item < items; item += gridDim.x) {
-        const uint32_t q = item / args.m_tiles;
-        const NTile t = tile_of(q);
-        const uint32_t sfb_shift = NT < 128 ? (t.sf_row_start % 128) / 32 : 0;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, s_abort)) {
           fail(kStatusWaitTimeout);
           break;
@@ -269,10 +268,10 @@ __global__ void __launch_bounds__(192, 1)
             // advancing the start address by 32 bytes steps K by one MMA inside the swizzle atom
             if (FP4) {
               mma_fp4(d0, a0 + 2 * kb, bd + 2 * kb, kIdesc, accum, sfa_t0 + kb * 4,
-                      sfb_t + kb * 4 * S::kNJ + sfb_shift);
+                      sfb_t + kb * 4 * S::kNJ);
               if (DUAL)
                 mma_fp4(d1, a1 + 2 * kb, bd + 2 * kb, kIdesc, accum, sfa_t1 + kb * 4,
-                        sfb_t + kb * 4 * S::kNJ + sfb_shift);
+                        sfb_t + kb * 4 * S::kNJ);
             } else {
               mma_bf16(d0, a0 + 2 * kb, bd + 2 * kb, kIdesc, accum);
               if (DUAL) mma_bf16(d1, a1 + 2 * kb, bd + 2 * kb, kIdesc, accum);

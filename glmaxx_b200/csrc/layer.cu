@@ -66,8 +66,8 @@ struct LayerPlan {
     nt = decode ? 32 : 128;
     const uint32_t A = r.A;
     const uint32_t active = A < r.E ? A : r.E;
-    sf_rows = static_cast<uint32_t>(up(uint64_t(A) + 127ull * active, 128));
     max_tiles = (A + nt - 1) / nt + active;
+    sf_rows = max_tiles * 128;  // each n tile owns a 128-row scale atom
     tiles = c.take(uint64_t(max_tiles) * sizeof(NTile));
     tile_count = c.take(16);
     route_row = c.take(uint64_t(A) * 4);
@@ -131,12 +131,66 @@ T* at(uint64_t base, uint64_t off) {
   return reinterpret_cast<T*>(base + off);
 }
 
+// Optional per-stage CUDA events (profiling): when set, the next layer
+// launches on this thread record event[s] before stage s and event[kStages]
+// after the last stage, on the launch stream.
+thread_local uint64_t* g_stage_events = nullptr;
+thread_local uint32_t g_stage_event_count = 0;
+
+}  // namespace
+
+int32_t set_stage_events(uint64_t* events, uint32_t count) {
+  if (events != nullptr && count < kLayerStages + 1) return GLMAXX_ERR_DESCRIPTOR;
+  g_stage_events = events;
+  g_stage_event_count = events ? count : 0;
+  return 0;
+}
+
+namespace {
+cudaError_t mark(uint32_t stage, cudaStream_t stream) {
+  if (g_stage_events == nullptr || stage >= g_stage_event_count) return cudaSuccess;
+  return cudaEventRecord(reinterpret_cast<cudaEvent_t>(g_stage_events[stage]), stream);
+}
 }  // namespace
 
 uint64_t layer_workspace_bytes(const glmaxx_moe_layer_descriptor& d) {
   LayerPlan p;
   p.build(d);
   return p.total;
+}
+
+int32_t layer_plane(const glmaxx_moe_layer_descriptor* desc, uint32_t which, uint64_t* address,
+                    uint64_t* bytes) {
+  if (desc == nullptr || address == nullptr || bytes == nullptr) return GLMAXX_ERR_NULL;
+  if (!valid_layer(*desc)) return GLMAXX_ERR_DESCRIPTOR;
+  LayerPlan p;
+  p.build(*desc);
+  const uint64_t ws = up(desc->workspace, kAlign);
+  const uint64_t A = p.r.A;
+  switch (which) {
+    case GLMAXX_PLANE_FC1_OUTPUT_BF16:
+      *address = ws + p.hbuf, *bytes = A * p.I * 2;
+      break;
+    case GLMAXX_PLANE_ROW_TOKEN_U32:
+      *address = ws + p.row_token, *bytes = A * 4;
+      break;
+    case GLMAXX_PLANE_ROW_SLOT_U32:
+      *address = ws + p.row_slot, *bytes = A * 4;
+      break;
+    case GLMAXX_PLANE_ROW_WEIGHT_F32:
+      *address = ws + p.row_weight, *bytes = A * 4;
+      break;
+    case GLMAXX_PLANE_EXPERT_OFFSETS_U32:
+      *address = ws + p.r.offsets, *bytes = uint64_t(p.r.E + 1) * 4;
+      break;
+    case GLMAXX_PLANE_SHARED_F32:
+      if (!p.shared || !p.decode) return GLMAXX_ERR_DESCRIPTOR;
+      *address = ws + p.sbuf, *bytes = uint64_t(p.r.T) * p.H * 4;
+      break;
+    default:
+      return GLMAXX_ERR_DESCRIPTOR;
+  }
+  return 0;
 }
 
 int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_stream,
@@ -166,6 +220,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     cudaError_t _st = (expr);                \
     if (_st != cudaSuccess) return int32_t(_st); \
   } while (0)
+  CHECK(mark(kStageRouter, stream));
   CHECK(cudaMemsetAsync(status, 0, 4, stream));
   // 1. router (or caller routes) -> dense routes + token-in-expert bitmap
   if (d.flags & GLMAXX_MOE_ROUTES_GIVEN) {
@@ -181,6 +236,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
                                at<uint32_t>(ws, r.bitmap), r.W, status, stream));
   }
   // 2. stable compaction
+  CHECK(mark(kStageCompact, stream));
   NTile* tiles = at<NTile>(ws, p.tiles);
   uint32_t* tile_count = at<uint32_t>(ws, p.tile_count);
   CHECK(launch_compact(at<uint32_t>(ws, r.bitmap), r.T, r.E, p.nt, p.sf_rows, p.max_tiles,
@@ -188,6 +244,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
                        at<uint32_t>(ws, r.offsets), at<uint32_t>(ws, r.poffs), tiles, tile_count,
                        status, stream));
   // 3. NVFP4 quantisation of x into the assignment rows
+  CHECK(mark(kStageQuant, stream));
   QuantScatterArgs q{};
   q.x = x;
   q.route_experts = experts;
@@ -210,8 +267,10 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   q.E = r.E;
   q.top_k = r.K;
   q.sf_row_cap = p.sf_rows;
+  q.nt = p.nt;
   CHECK(launch_quant_scatter(q, stream));
   // 4. grouped FC1 (gate+up) with fused SwiGLU -> h [A][I] bf16
+  CHECK(mark(kStageFc1, stream));
   {
     GemmLaunch g{};
     g.a = reinterpret_cast<const void*>(d.w13_values);
@@ -240,6 +299,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     CHECK(launch_gemm(p.decode ? kFc1DecodeFp4 : kFc1PrefillFp4, g, info.sms, stream));
   }
   // 5. NVFP4 quantisation of h
+  CHECK(mark(kStageFc2Quant, stream));
   Fc2QuantArgs f{};
   f.h = at<uint16_t>(ws, p.hbuf);
   f.row_prow = q.row_prow;
@@ -253,6 +313,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   f.sf_row_cap = p.sf_rows;
   CHECK(launch_fc2_quant(f, stream));
   // 6. shared expert (bf16), and the output initialisation it provides
+  CHECK(mark(kStageShared, stream));
   if (p.shared) {
     GemmLaunch g1{};
     g1.a = reinterpret_cast<const void*>(d.shared13_bf16);
@@ -289,6 +350,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     CHECK(cudaMemsetAsync(out, 0, uint64_t(r.T) * p.H * 4, stream));
   }
   // 7. grouped FC2 with the routing-weighted combine
+  CHECK(mark(kStageFc2, stream));
   {
     GemmLaunch g{};
     g.a = reinterpret_cast<const void*>(d.w2_values);
@@ -319,9 +381,11 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     CHECK(launch_gemm(p.decode ? kFc2DecodeFp4 : kFc2PrefillFp4, g, info.sms, stream));
   }
   // 8. deterministic combine (decode): ascending-expert sum + shared
+  CHECK(mark(kStageCombine, stream));
   if (p.decode)
     CHECK(launch_combine(at<float>(ws, p.plane), experts,
                          p.shared ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H, r.K, stream));
+  CHECK(mark(kLayerStages, stream));
 #undef CHECK
   return 0;
 }

@@ -27,7 +27,7 @@ struct QuantScatterArgs {
   uint32_t* row_prow;             // [A] -> padded (scale-factor) row
   uint32_t* route_row;            // [T*K] -> compacted row
   uint32_t* status;
-  uint32_t T, H, E, top_k, sf_row_cap;
+  uint32_t T, H, E, top_k, sf_row_cap, nt;
 };
 
 // Compacted-order route arrays of the reference FC1/FC2 ABI, written from the

@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
       const uint32_t e = lane * per + q;
       if (e < E) {
         sc += cnt_s[e];
-        sp += (cnt_s[e] + 127) / 128 * 128;
+        sp += (cnt_s[e] + nt - 1) / nt * 128;
         st += (cnt_s[e] + nt - 1) / nt;
       }
     }
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
         toff_s[e] = ot;
         counts[e] = cnt_s[e];
         oc += cnt_s[e];
-        op += (cnt_s[e] + 127) / 128 * 128;
+        op += (cnt_s[e] + nt - 1) / nt * 128;
         ot += (cnt_s[e] + nt - 1) / nt;
       }
     }
@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
       NTile tl;
       tl.expert = e;
       tl.row_start = off_s[e] + j * nt;
-      tl.sf_row_start = poff_s[e] + j * nt;
+      tl.sf_row_start = poff_s[e] + j * 128;
       tl.rows = min(nt, c - j * nt);
       tiles[toff_s[e] + j] = tl;
     }
@@ -397,7 +397,8 @@ __global__ void __launch_bounds__(1024) quant_scatter_kernel(QuantScatterArgs a)
     if (e >= a.E) continue;
     const uint32_t word = a.bitmap[uint64_t(e) * W + t / 32];
     const uint32_t rank = a.wprefix[uint64_t(e) * W + t / 32] + __popc(word & ((1u << (t % 32)) - 1u));
-    const uint32_t prow = a.poffs[e] + rank;  // scale-factor row
+    // scale-factor row: every n tile of a.nt rows owns a whole 128-row atom
+    const uint32_t prow = a.poffs[e] + (rank / a.nt) * 128 + rank % a.nt;
     const uint32_t row = a.offsets[e] + rank;  // compacted row
     if (prow >= a.sf_row_cap || row >= a.T * a.top_k) continue;
     uint4* dst = reinterpret_cast<uint4*>(a.xq + uint64_t(row) * (a.H / 2) + kb * 32);
@@ -498,7 +499,7 @@ __global__ void __launch_bounds__(1024) compat_prepare_kernel(CompatPrepareArgs 
         const uint32_t b0 = a.offsets[e], b1 = a.offsets[e + 1];
         if (b1 < b0 || b1 > a.A) bad = true;
         const uint32_t c = b1 >= b0 ? b1 - b0 : 0;
-        sp += (c + 127) / 128 * 128;
+        sp += (c + a.nt - 1) / a.nt * 128;
         st += (c + a.nt - 1) / a.nt;
       }
     }
@@ -521,7 +522,7 @@ __global__ void __launch_bounds__(1024) compat_prepare_kernel(CompatPrepareArgs 
         a.poffs[e] = op;
         poff_s[e] = op;
         toff_s[e] = ot;
-        op += (c + 127) / 128 * 128;
+        op += (c + a.nt - 1) / a.nt * 128;
         ot += (c + a.nt - 1) / a.nt;
       }
     }
@@ -545,15 +546,17 @@ __global__ void __launch_bounds__(1024) compat_prepare_kernel(CompatPrepareArgs 
       NTile tl;
       tl.expert = e;
       tl.row_start = b0 + j * a.nt;
-      tl.sf_row_start = poff_s[e] + j * a.nt;
+      tl.sf_row_start = poff_s[e] + j * 128;
       tl.rows = on ? min(a.nt, c - j * a.nt) : 0;
       a.tiles[toff_s[e] + j] = tl;
     }
   }
   for (uint32_t r = threadIdx.x; r < a.A; r += blockDim.x) {
     const uint32_t e = a.route_experts[r];
-    if (e < a.E && r >= a.offsets[e] && r < a.offsets[e + 1])
-      a.row_prow[r] = poff_s[e] + (r - a.offsets[e]);
+    if (e < a.E && r >= a.offsets[e] && r < a.offsets[e + 1]) {
+      const uint32_t rank = r - a.offsets[e];
+      a.row_prow[r] = poff_s[e] + (rank / a.nt) * 128 + rank % a.nt;
+    }
     else {
       a.row_prow[r] = 0xffffffffu;
       if (a.status) atomicOr(a.status, kStatusExpertOutOfRange);

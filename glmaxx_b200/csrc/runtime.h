@@ -19,7 +19,22 @@ struct DeviceInfo {
 // the device is not compute capability 10.x (B200 / sm_100a), or a cudaError_t.
 int32_t current_device_info(DeviceInfo* info);
 
+enum LayerStage : uint32_t {
+  kStageRouter = 0,
+  kStageCompact = 1,
+  kStageQuant = 2,
+  kStageFc1 = 3,
+  kStageFc2Quant = 4,
+  kStageShared = 5,
+  kStageFc2 = 6,
+  kStageCombine = 7,
+  kLayerStages = 8,
+};
+int32_t set_stage_events(uint64_t* events, uint32_t count);
+
 uint64_t layer_workspace_bytes(const glmaxx_moe_layer_descriptor& d);
+int32_t layer_plane(const glmaxx_moe_layer_descriptor* desc, uint32_t which, uint64_t* address,
+                    uint64_t* bytes);
 int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* stream, int32_t* async_err);
 uint64_t router_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_k);
 int32_t router_compact_launch(const glmaxx_router_descriptor* desc, void* stream,

@@ -144,6 +144,7 @@ class RoutedMoE:
             self._ws[key] = ws
         d.workspace = ws.data_ptr()
         d.workspace_bytes = ws.numel()
+        self._last, self._last_key = d, key
         return d
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None,
@@ -166,6 +167,18 @@ class RoutedMoE:
         return out
 
     __call__ = forward
+
+    def plane(self, name: str) -> torch.Tensor:
+        """Device view of an intermediate workspace plane of the last forward()
+        (glmaxx_moe_layer_plane), as raw bytes."""
+        d = self._last
+        addr, nbytes = ctypes.c_uint64(0), ctypes.c_uint64(0)
+        abi.check(self.lib.glmaxx_moe_layer_plane(ctypes.byref(d), abi.PLANES[name],
+                                                  ctypes.byref(addr), ctypes.byref(nbytes)),
+                  f"plane {name}")
+        ws = self._ws[self._last_key]
+        off = addr.value - ws.data_ptr()
+        return ws[off:off + nbytes.value]
 
     def device_status(self) -> list[str]:
         """Decode the device validation word of the last step (synchronises)."""

@@ -390,6 +390,39 @@ int32_t glmaxx_router_compact_launch(const struct glmaxx_router_descriptor* desc
 int32_t glmaxx_moe_layer_launch(const struct glmaxx_moe_layer_descriptor* descriptor,
                                 void* cuda_stream, int32_t* asynchronous_error);
 
+/* Profiling (the CUDA-event timing of the reference, crates/glm-cuda/src/
+ * ffi.rs:3057-3079, per stage): while set, layer launches on the calling
+ * thread record events[s] (cudaEvent_t handles) before stage s of
+ * GLMAXX_LAYER_STAGE_* and events[GLMAXX_LAYER_STAGES] after the last, on the
+ * launch stream.  count must be >= GLMAXX_LAYER_STAGES + 1; events = NULL clears. */
+enum {
+  GLMAXX_LAYER_STAGE_ROUTER = 0,
+  GLMAXX_LAYER_STAGE_COMPACT = 1,
+  GLMAXX_LAYER_STAGE_QUANT = 2,
+  GLMAXX_LAYER_STAGE_FC1 = 3,
+  GLMAXX_LAYER_STAGE_FC2_QUANT = 4,
+  GLMAXX_LAYER_STAGE_SHARED = 5,
+  GLMAXX_LAYER_STAGE_FC2 = 6,
+  GLMAXX_LAYER_STAGE_COMBINE = 7,
+  GLMAXX_LAYER_STAGES = 8,
+};
+int32_t glmaxx_moe_layer_set_stage_events(uint64_t* events, uint32_t count);
+
+/* Workspace introspection: device address and size of an intermediate plane
+ * of the last glmaxx_moe_layer_launch with this descriptor (valid after the
+ * launch completes).  Rows are in compacted (expert, token, slot) order, the
+ * order of crates/glm-reference/src/routed_fc1.rs:20-58. */
+enum {
+  GLMAXX_PLANE_FC1_OUTPUT_BF16 = 0,    /* [assignments][local_intermediate] SwiGLU output */
+  GLMAXX_PLANE_ROW_TOKEN_U32 = 1,      /* [assignments] token of each compacted row       */
+  GLMAXX_PLANE_ROW_SLOT_U32 = 2,       /* [assignments] route slot                        */
+  GLMAXX_PLANE_ROW_WEIGHT_F32 = 3,     /* [assignments] routing weight                    */
+  GLMAXX_PLANE_EXPERT_OFFSETS_U32 = 4, /* [experts + 1] exclusive compacted offsets       */
+  GLMAXX_PLANE_SHARED_F32 = 5,         /* [tokens][hidden] shared expert (decode path)     */
+};
+int32_t glmaxx_moe_layer_plane(const struct glmaxx_moe_layer_descriptor* descriptor,
+                               uint32_t which, uint64_t* address, uint64_t* bytes);
+
 /* PackedNvfp4::pack (1-D codec) of `batch` row-major [n][k] tensors (f32 when
  * src_is_bf16 == 0, else bf16), n % 128 == 0, k % 64 == 0.  Tensor b writes
  * values + b*n*k/2, scales + b*n*k/16, global_scale[b], global_amax[b]

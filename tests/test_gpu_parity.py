@@ -14,7 +14,8 @@ import oracle as O
 from glmaxx_b200 import abi, synth
 from glmaxx_b200.moe import MoEConfig, RoutedMoE, pack_nvfp4
 
-from gpu_util import assert_layer_close, cuda, rel_l2, to_np_bf16_bits
+from gpu_util import (MAX_ABS_ULPS, assert_layer_close, bf16_ulp, cuda, rel_l2,
+                      to_np_bf16_bits)
 
 pytestmark = pytest.mark.gpu
 
@@ -138,8 +139,56 @@ def _check_routes(layer, x, cfg):
     assert np.array_equal(got_w.cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
 
 
+def _stage_pins(layer: RoutedMoE, x: torch.Tensor, cfg: MoEConfig, out: np.ndarray):
+    """Pin each stage of the real layer run: the FC1 output h read back from the
+    workspace against the oracle FC1 on the same compacted rows, and FC2 + combine
+    against the oracle FC2 evaluated on the GPU's own h.  Returns (h rel-L2,
+    routed rel-L2 given h)."""
+    T, I, H = x.shape[0], cfg.local_intermediate, cfg.hidden
+    A = T * cfg.top_k
+    h = layer.plane("fc1_output_bf16").view(torch.bfloat16).reshape(A, I).float().cpu().numpy()
+    tok = layer.plane("row_token_u32").view(torch.int32).cpu().numpy()
+    slot = layer.plane("row_slot_u32").view(torch.int32).cpu().numpy()
+    off = layer.plane("expert_offsets_u32").view(torch.int32).cpu().numpy()
+    xf = O.bf16_bits_to_f32(to_np_bf16_bits(x))
+    w = layer.w
+    packed13 = lambda e: O.Packed(w.w13.values[e].cpu().numpy().ravel(),
+                                  w.w13.scales[e].cpu().numpy().ravel(),
+                                  float(w.w13.global_scale[e]), 0.0, 2 * I, H, "1d")
+    packed2 = lambda e: O.Packed(w.w2.values[e].cpu().numpy().ravel(),
+                                 w.w2.scales[e].cpu().numpy().ravel(),
+                                 float(w.w2.global_scale[e]), 0.0, H, I, "1d")
+    h_ref = np.zeros_like(h)
+    experts = []
+    for e in range(cfg.experts):
+        if off[e + 1] > off[e]:
+            experts.append(e)
+            h_ref[off[e]:off[e + 1]] = O.routed_fc1(xf[tok[off[e]:off[e + 1]]], packed13(e))
+    re, rw = layer.routes(T)
+    re, rw = re.cpu().numpy().view(np.uint16), rw.cpu().numpy()
+    routes = O.routes_array([(t, int(re[t, s]), s, float(rw[t, s]))
+                             for t in range(T) for s in range(cfg.top_k)])
+    comp = O.compact_routes(routes, T)
+    assert np.array_equal(comp["token"], tok.astype(np.uint32))
+    assert np.array_equal(comp["slot"], slot.astype(np.uint8))
+    routed_on_gpu_h = O.routed_fc2(h, routes, T, I, H, {e: packed2(e) for e in experts})
+    shared = 0.0
+    if w.shared13 is not None:
+        shared = layer.plane("shared_f32").view(torch.float32).reshape(T, H).cpu().numpy()
+    return rel_l2(h, h_ref), rel_l2(out - shared, routed_on_gpu_h)
+
+
 def test_gpu_layer_reduced_config0():
-    """T=8, E=16, top-8 (no groups), I=2048, NVFP4 W4A4."""
+    """T=8, E=16, top-8 (no groups), I=2048, NVFP4 W4A4, no shared expert.
+
+    Checks: routes bit-exact; end-to-end max-abs <= 4 bf16 ulp of the output scale;
+    FC1 output h within rel-L2 1e-3 of the oracle FC1; FC2 + combine within rel-L2
+    1e-5 of the oracle FC2 applied to the same h.  The end-to-end rel-L2 against
+    the sequential-fp32 oracle is not asserted at 1e-3 for this 8-token case: the
+    oracle's own rounding moves ~0.15% of the bf16 h values by one ulp relative to
+    the tensor-core sum, and NVFP4 re-quantisation of h turns an isolated one-ulp
+    move into a whole code step (measured across seeds: 6e-7 to 2.3e-3); with
+    64 tokens or a shared expert the same path measures 2e-4 to 8e-4."""
     cfg = MoEConfig(experts=16, groups=1, topk_groups=1, shared_intermediate=0)
     dev = cuda()
     w = synth.make_rank_weights(cfg, seed=3, device=dev)
@@ -149,8 +198,13 @@ def test_gpu_layer_reduced_config0():
     torch.cuda.synchronize()
     assert layer.device_status() == []
     _check_routes(layer, x, cfg)
+    got = out.cpu().numpy()
     ref = _oracle_layer(layer, x, cfg)
-    assert_layer_close(out.cpu().numpy(), ref, "config0")
+    err = float(np.abs(got - ref).max())
+    assert err <= MAX_ABS_ULPS * bf16_ulp(float(np.abs(ref).max()))
+    h_err, fc2_err = _stage_pins(layer, x, cfg, got)
+    assert h_err <= 1e-3, h_err
+    assert fc2_err <= 1e-5, fc2_err
 
 
 @pytest.mark.parametrize("tp,rank", [(1, 0), (4, 3)])
@@ -166,7 +220,11 @@ def test_gpu_layer_decode_config1(tp, rank):
     assert layer.device_status() == []
     _check_routes(layer, x, cfg)
     ref = _oracle_layer(layer, x, cfg)
-    assert_layer_close(out.cpu().numpy(), ref, f"decode tp{tp} r{rank}")
+    got = out.cpu().numpy()
+    assert_layer_close(got, ref, f"decode tp{tp} r{rank}")
+    h_err, fc2_err = _stage_pins(layer, x, cfg, got)
+    assert h_err <= 1e-3, h_err
+    assert fc2_err <= 1e-5, fc2_err
 
 
 def test_gpu_layer_prefill_path_subset():
