@@ -99,7 +99,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_router_logits": (None, [vp, u64, u64, vp, u64, vp, i32]),
         "orc_router_select": (i32, [vp, u64, u64, vp, u32, u32, u32, f32, vp, vp]),
         "orc_moe_layer": (i32, [u32, u32, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp, vp, vp,
-                                vp, vp, vp, u32, vp, vp, i32]),
+                                vp, vp, u32, vp, u32, vp, vp, i32]),
         "orc_f32_to_f16_bits": (u16, [f32]),
         "orc_f16_bits_to_f32": (f32, [u16]),
         "orc_exl3_xorshift_trellis": (None, [u64, u64, vp]),
@@ -368,8 +368,9 @@ def moe_layer(x_bf16, route_experts, route_weights, w13_values, w13_scales, w13_
                                                w2_scales, w2_global)]
     s13 = None if shared13_bf16 is None else np.ascontiguousarray(shared13_bf16, np.uint16)
     s2 = None if shared2_bf16 is None else np.ascontiguousarray(shared2_bf16, np.uint16)
+    shared_inter = 0 if s2 is None else s2.shape[1]
     _check(lib().orc_moe_layer(t, h, experts, local_inter, topk, _p(x), _p(re), _p(rw),
-                               *[_p(a) for a in arrs], _p(s13), _p(s2), _p(subset),
+                               *[_p(a) for a in arrs], _p(s13), _p(s2), shared_inter, _p(subset),
                                0 if subset is None else subset.size, _p(routed), _p(shared),
                                threads()), "moe_layer")
     return routed.reshape(nsel, h), shared.reshape(nsel, h)

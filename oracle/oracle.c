@@ -844,8 +844,8 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
                   const uint8_t* w13_scales, const float* w13_global, const uint8_t* w2_values,
                   const uint8_t* w2_scales, const float* w2_global,
                   const uint16_t* shared13_bf16, const uint16_t* shared2_bf16,
-                  const uint32_t* token_subset, uint32_t subset_count, float* routed_out,
-                  float* shared_out, int threads) {
+                  uint32_t shared_inter, const uint32_t* token_subset, uint32_t subset_count,
+                  float* routed_out, float* shared_out, int threads) {
 #ifdef _OPENMP
   if (threads > 0) omp_set_num_threads(threads);
 #else
@@ -862,7 +862,8 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
   float* w2 = malloc(sizeof(float) * H * I);
   float* xrow = malloc(sizeof(float) * H);
   float* act = malloc(sizeof(float) * H);
-  float* hrow = malloc(sizeof(float) * I);
+  const uint64_t IS = shared_inter;
+  float* hrow = malloc(sizeof(float) * (I > IS ? I : IS));
   float* src = malloc(sizeof(float) * I);
   if (!out_row || !routes || !comp || !w13 || !w2 || !xrow || !act || !hrow || !src) {
     free(out_row), free(routes), free(comp), free(w13), free(w2), free(xrow), free(act);
@@ -934,10 +935,10 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
         continue;
       }
 #pragma omp parallel for schedule(static)
-      for (int64_t c = 0; c < (int64_t)I; ++c) {
+      for (int64_t c = 0; c < (int64_t)IS; ++c) {
         float gate = 0.0f, up = 0.0f;
         const uint16_t* wg = shared13_bf16 + (uint64_t)c * H;
-        const uint16_t* wu = shared13_bf16 + (I + (uint64_t)c) * H;
+        const uint16_t* wu = shared13_bf16 + (IS + (uint64_t)c) * H;
         for (uint64_t k = 0; k < H; ++k) {
           const float xv = bf16_bits_to_f32(x_bf16[(uint64_t)t * H + k]);
           gate += xv * bf16_bits_to_f32(wg[k]);
@@ -948,8 +949,8 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
 #pragma omp parallel for schedule(static)
       for (int64_t c = 0; c < (int64_t)H; ++c) {
         float acc = 0.0f;
-        const uint16_t* wr = shared2_bf16 + (uint64_t)c * I;
-        for (uint64_t k = 0; k < I; ++k) acc += hrow[k] * bf16_bits_to_f32(wr[k]);
+        const uint16_t* wr = shared2_bf16 + (uint64_t)c * IS;
+        for (uint64_t k = 0; k < IS; ++k) acc += hrow[k] * bf16_bits_to_f32(wr[k]);
         out[c] = acc;
       }
     }

@@ -102,8 +102,8 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
                   const uint8_t* w13_scales, const float* w13_global, const uint8_t* w2_values,
                   const uint8_t* w2_scales, const float* w2_global,
                   const uint16_t* shared13_bf16, const uint16_t* shared2_bf16,
-                  const uint32_t* token_subset, uint32_t subset_count, float* routed_out,
-                  float* shared_out, int threads);
+                  uint32_t shared_inter, const uint32_t* token_subset, uint32_t subset_count,
+                  float* routed_out, float* shared_out, int threads);
 
 /* crates/glm-format/src/exl3.rs */
 uint16_t orc_f32_to_f16_bits(float value);
