@@ -25,6 +25,7 @@ EXL3_GATE, EXL3_UP, EXL3_DOWN = 1, 2, 3
 PLANES = {"fc1_output_bf16": 0, "row_token_u32": 1, "row_slot_u32": 2, "row_weight_f32": 3,
           "expert_offsets_u32": 4, "shared_f32": 5}
 LAYER_STAGES = ["router", "compact", "quant", "fc1", "fc2_quant", "shared", "fc2", "combine"]
+ROUTER_STATIC_SCRATCH_BYTES = 4 << 20
 MOE_ROUTES_GIVEN = 1 << 0
 MOE_SHARED_EXPERT = 1 << 1
 
@@ -194,6 +195,7 @@ SIGNATURES = {
     "glmaxx_router_workspace_bytes": (u64, [u32] * 4),
     "glmaxx_moe_layer_workspace_bytes": (u64, [_P]),
     "glmaxx_router_compact_launch": (ctypes.c_int32, [_P, _P, _I32P]),
+    "glmaxx_router_compact_launch_static": (ctypes.c_int32, [_P, _P, _I32P]),
     "glmaxx_moe_layer_launch": (ctypes.c_int32, [_P, _P, _I32P]),
     "glmaxx_moe_layer_set_stage_events": (ctypes.c_int32, [_U64P, u32]),
     "glmaxx_moe_layer_plane": (ctypes.c_int32, [_P, u32, _U64P, _U64P]),

@@ -387,6 +387,22 @@ uint64_t glmaxx_moe_layer_workspace_bytes(const struct glmaxx_moe_layer_descript
 
 int32_t glmaxx_router_compact_launch(const struct glmaxx_router_descriptor* descriptor,
                                      void* cuda_stream, int32_t* asynchronous_error);
+
+/* Allocation-free variant of glmaxx_router_compact_launch (no counterpart in the
+ * reference library).  For callers that cannot provide or allocate scratch
+ * memory -- an engine whose HBM is planned up front with no per-call
+ * workspace, or code running under stream capture where cudaMalloc is not
+ * allowed -- the router's scratch lives in a device array of
+ * GLMAXX_ROUTER_STATIC_SCRATCH_BYTES inside this library, held by every GPU
+ * that loads it until exit.  The descriptor's workspace fields are ignored;
+ * inputs and outputs are the caller's.  Shapes needing more scratch than the
+ * array (glmaxx_router_workspace_bytes) return GLMAXX_ERR_DESCRIPTOR.  The
+ * first call on a device looks up the array's address and should be made
+ * outside stream capture.  All calls share the array: calls whose GPU work
+ * overlaps race and must be serialised by the caller. */
+#define GLMAXX_ROUTER_STATIC_SCRATCH_BYTES (4ull << 20)
+int32_t glmaxx_router_compact_launch_static(const struct glmaxx_router_descriptor* descriptor,
+                                            void* cuda_stream, int32_t* asynchronous_error);
 int32_t glmaxx_moe_layer_launch(const struct glmaxx_moe_layer_descriptor* descriptor,
                                 void* cuda_stream, int32_t* asynchronous_error);
 
