@@ -268,6 +268,9 @@ def run_ours(args):
         handles = (ctypes.c_uint64 * nst)(*[e.cuda_event for e in evs])
         abi.check(L.glmaxx_moe_layer_set_stage_events(handles, nst), "stage events")
         for _ in range(min(args.steps, 50)):
+            # a short device spin first, so that every launch of the step is queued
+            # before the GPU reaches it and the stage events time the GPU alone
+            torch.cuda._sleep(2_000_000)
             layer(x, out)
             stream.synchronize()
             for i, s in enumerate(abi.LAYER_STAGES):

@@ -62,11 +62,13 @@ cudaError_t run(const GemmLaunch& g, int num_sms, cudaStream_t stream) {
   static_assert(gemm_smem_bytes<FP4, DUAL, NT, STAGES>() <= 227 * 1024, "smem budget");
   auto kernel = grouped_gemm_kernel<FP4, DUAL, NT, STAGES, EPI>;
   constexpr int smem = gemm_smem_bytes<FP4, DUAL, NT, STAGES>();
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
     cudaError_t st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (st != cudaSuccess) return st;
-    configured = true;
+    configured[dev] = true;
   }
   if (g.a_row_bytes % 128 != 0 || g.b_row_bytes != g.a_row_bytes) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
@@ -80,14 +82,28 @@ cudaError_t run(const GemmLaunch& g, int num_sms, cudaStream_t stream) {
 
 }  // namespace
 
+void choose_k_splits(uint32_t tiles, uint32_t k_chunks, int sms, uint32_t max_splits,
+                     uint32_t* splits, uint32_t* kc_per) {
+  uint32_t want = tiles >= uint32_t(sms) ? 1u : uint32_t(sms) / (tiles ? tiles : 1);
+  if (want > max_splits) want = max_splits;
+  if (want > k_chunks) want = k_chunks;
+  if (want < 1) want = 1;
+  const uint32_t per = (k_chunks + want - 1) / want;
+  *kc_per = per;
+  *splits = (k_chunks + per - 1) / per;  // every slice has at least one chunk
+}
+
 int gemm_tile_rows(GemmVariant v) {
   switch (v) {
     case kFc1DecodeFp4:
     case kFc2DecodeFp4:
+    case kFc2DecodeFp4Pair:
     case kFc2DecodeFp4Store:
       return 32;
     case kShared1Bf16N64:
     case kShared2Bf16N64:
+    case kShared1Bf16N64Split:
+    case kShared2Bf16N64Split:
       return 64;
     default:
       return 128;
@@ -100,6 +116,8 @@ cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStr
       return run<true, true, 32, 5, kEpiSwiGLU>(g, num_sms, stream);
     case kFc2DecodeFp4:
       return run<true, false, 32, 8, kEpiRoutedPlane>(g, num_sms, stream);
+    case kFc2DecodeFp4Pair:
+      return run<true, true, 32, 5, kEpiRoutedPlane>(g, num_sms, stream);
     case kFc2DecodeFp4Store:
       return run<true, false, 32, 8, kEpiStoreF32>(g, num_sms, stream);
     case kFc1PrefillFp4:
@@ -116,6 +134,10 @@ cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStr
       return run<false, true, 128, 4, kEpiSwiGLU>(g, num_sms, stream);
     case kShared2Bf16N128:
       return run<false, false, 128, 6, kEpiStoreF32>(g, num_sms, stream);
+    case kShared1Bf16N64Split:
+      return run<false, true, 64, 5, kEpiStorePartial>(g, num_sms, stream);
+    case kShared2Bf16N64Split:
+      return run<false, false, 64, 8, kEpiStorePartial>(g, num_sms, stream);
   }
   return cudaErrorInvalidValue;
 }

@@ -45,19 +45,24 @@ enum EpilogueKind : int {
   kEpiRoutedPlane = 1,  // plane[token][slot][col] = w * acc (deterministic combine later)
   kEpiRoutedAtomic = 2, // out_f32[token][col] += w * acc
   kEpiStoreF32 = 3,     // out_f32[row][col] = acc
+  kEpiStorePartial = 4, // split-K partial: out_f32[ks][row][col] (+ up half at ldo_up)
 };
 
 struct GemmArgs {
   const NTile* tiles;         // explicit n-tile list, or null for implicit tiles
   const uint32_t* tile_count; // device count for explicit lists
   uint32_t implicit_rows;     // implicit tiles: q -> rows [q*NT, min(+NT, implicit_rows))
-  uint32_t m_tiles;           // 128-row output tiles (per half in dual mode)
+  uint32_t m_tiles;           // M tiles per n tile (pairs of 128-row tiles in dual mode)
   uint32_t k_chunks;          // K bytes / 128
-  uint32_t up_row_offset;     // dual: first up row inside an expert's A rows
+  uint32_t up_row_offset;     // dual: A rows of the second accumulator = first + this
+  uint32_t m_stride;          // A rows between consecutive M tiles (0 = 128)
   uint32_t kblocks;           // K / 64: scale atoms along K
   uint32_t ldo;               // output row stride (elements)
   uint32_t top_k;
-  uint32_t pad0;
+  uint32_t k_splits;          // K slices per output tile (split-K; kEpiStorePartial only)
+  uint32_t kc_per_split;      // k chunks per slice
+  uint32_t ldo_up;            // dual split-K: column offset of the up half in out rows
+  uint64_t split_stride;      // elements between consecutive K-slice partial planes
   const uint8_t* sfa;         // A scale atoms, expert-major
   uint64_t sfa_expert_bytes;
   const uint8_t* sfb;         // B scale atoms (padded row space, 128-row tiles)
@@ -75,7 +80,9 @@ struct GemmShape {
   static constexpr int kAcc = DUAL ? 2 : 1;
   static constexpr int kNJ = NT >= 128 ? NT / 128 : 1;              // SFB atoms along N
   static constexpr int kSfCols = FP4 ? (kAcc * 16 + 16 * kNJ) : 0;  // TMEM columns for scales
-  static constexpr int kAccBufs = (2 * kAcc * NT + kSfCols) <= 512 ? 2 : 1;
+  // Accumulator buffers (up to 4) let the MMA warp run items ahead of the epilogue.
+  static constexpr int kAccBufsFit = (512 - kSfCols) / (kAcc * NT);
+  static constexpr int kAccBufs = kAccBufsFit >= 4 ? 4 : (kAccBufsFit >= 1 ? kAccBufsFit : 1);
   static constexpr int kUsedCols = kAccBufs * kAcc * NT + kSfCols;
   static constexpr int kTmemCols = kUsedCols <= 32    ? 32
                                    : kUsedCols <= 64  ? 64
@@ -110,9 +117,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
   uint64_t* tfull_bar = bars + 2 * STAGES;
-  uint64_t* tempty_bar = bars + 2 * STAGES + 2;
-  uint64_t* drain_bar = bars + 2 * STAGES + 4;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  uint64_t* tempty_bar = bars + 2 * STAGES + 4;
+  uint64_t* drain_bar = bars + 2 * STAGES + 8;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -123,7 +130,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < S::kAccBufs; ++b) {
       mbar_init(&tfull_bar[b], 1);
       mbar_init(&tempty_bar[b], 4);
     }
@@ -145,7 +152,19 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *s_tmem;
 
   const uint32_t tiles_total = args.tiles ? *args.tile_count : (args.implicit_rows + NT - 1) / NT;
-  const uint32_t items = tiles_total * args.m_tiles;
+  const uint32_t splits = args.k_splits ? args.k_splits : 1;
+  const uint32_t kc_per = splits > 1 ? args.kc_per_split : args.k_chunks;
+  const uint32_t items = tiles_total * args.m_tiles * splits;
+  // item -> (n tile q, m tile i, K slice ks); K slice ks covers chunks [ks*kc_per, ...)
+  auto item_q = [&](uint32_t item) { return item / splits / args.m_tiles; };
+  auto item_i = [&](uint32_t item) { return (item / splits) % args.m_tiles; };
+  auto item_kc0 = [&](uint32_t item) { return (item % splits) * kc_per; };
+  auto item_kc1 = [&](uint32_t item) { return min(args.k_chunks, (item % splits) * kc_per + kc_per); };
+  // Dual mode either pairs gate/up rows for the SwiGLU epilogue (m_stride 128,
+  // second tile = up rows) or streams two adjacent 128-row tiles that share the
+  // B tile (m_stride 256, up_row_offset 128), which doubles the weight bytes per
+  // pipeline stage.
+  const uint32_t m_stride = args.m_stride ? args.m_stride : 128;
 
   auto stage_a = [&](int s, int h) { return stage_base + s * S::kStageBytes + h * S::kABytes; };
   auto stage_b = [&](int s) { return stage_base + s * S::kStageBytes + S::kAcc * S::kABytes; };
@@ -177,11 +196,17 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
+      // The next item's tile descriptor is loaded one item ahead so that its
+      // global-memory latency overlaps the current item's copies.
+      NTile t_next = blockIdx.x < items ? tile_of(item_q(blockIdx.x)) : NTile{};
       for (uint32_t item = blockIdx.x; ok && item < items; item += gridDim.x) {
-        const uint32_t q = item / args.m_tiles, i = item % args.m_tiles;
-        const NTile t = tile_of(q);
+        const uint32_t i = item_i(item);
+        const NTile t = t_next;
+        const uint32_t next = item + gridDim.x;
+        if (next < items) t_next = tile_of(item_q(next));
         const uint8_t* sfa_e = FP4 ? args.sfa + uint64_t(t.expert) * args.sfa_expert_bytes : nullptr;
-        for (uint32_t kc = 0; kc < args.k_chunks; ++kc) {
+        const uint32_t kc1 = item_kc1(item);
+        for (uint32_t kc = item_kc0(item); kc < kc1; ++kc) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) {
             fail(kStatusWaitTimeout);
             ok = false;
@@ -189,18 +214,20 @@ __global__ void __launch_bounds__(192, 1)
           }
           mbar_arrive_expect_tx(&full_bar[stage], kTx);
           const int32_t kx = static_cast<int32_t>(kc * 128);
-          tma_load_3d(stage_a(stage, 0), &tmap_a, &full_bar[stage], kx, int32_t(i * 128),
+          tma_load_3d(stage_a(stage, 0), &tmap_a, &full_bar[stage], kx, int32_t(i * m_stride),
                       int32_t(t.expert));
           if (DUAL)
             tma_load_3d(stage_a(stage, 1), &tmap_a, &full_bar[stage], kx,
-                        int32_t(args.up_row_offset + i * 128), int32_t(t.expert));
+                        int32_t(i * m_stride + args.up_row_offset), int32_t(t.expert));
           tma_load_2d(stage_b(stage), &tmap_b, &full_bar[stage], kx, int32_t(t.row_start));
           if (FP4) {
-            bulk_load(stage_sfa(stage, 0), sfa_e + 512ull * (uint64_t(i) * args.kblocks + kc * 4),
-                      2048, &full_bar[stage]);
+            bulk_load(stage_sfa(stage, 0),
+                      sfa_e + 512ull * (uint64_t(i * m_stride / 128) * args.kblocks + kc * 4), 2048,
+                      &full_bar[stage]);
             if (DUAL)
               bulk_load(stage_sfa(stage, 1),
-                        sfa_e + 512ull * (uint64_t(args.up_row_offset / 128 + i) * args.kblocks +
+                        sfa_e + 512ull * (uint64_t((i * m_stride + args.up_row_offset) / 128) *
+                                              args.kblocks +
                                           kc * 4),
                         2048, &full_bar[stage]);
 #pragma unroll
@@ -241,7 +268,8 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t d0 = tmem + acc * (S::kAcc * NT);
         const uint32_t d1 = d0 + NT;
-        for (uint32_t kc = 0; kc < args.k_chunks; ++kc) {
+        const uint32_t kc0 = item_kc0(item), kc1 = item_kc1(item);
+        for (uint32_t kc = kc0; kc < kc1; ++kc) {
           if (!mbar_wait(&full_bar[stage], phase, s_abort)) {
             fail(kStatusWaitTimeout);
             ok = false;
@@ -264,7 +292,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t bd = smem_desc_sw128(stage_b(stage));
 #pragma unroll
           for (int kb = 0; kb < 4; ++kb) {
-            const uint32_t accum = (kc > 0 || kb > 0) ? 1u : 0u;
+            const uint32_t accum = (kc > kc0 || kb > 0) ? 1u : 0u;
             // advancing the start address by 32 bytes steps K by one MMA inside the swizzle atom
             if (FP4) {
               mma_fp4(d0, a0 + 2 * kb, bd + 2 * kb, kIdesc, accum, sfa_t0 + kb * 4,
@@ -285,10 +313,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (!ok) break;
         tc_commit(&tfull_bar[acc]);
-        if (S::kAccBufs == 2) {
-          acc ^= 1;
-          if (acc == 0) acc_phase ^= 1;
-        } else {
+        if (++acc == S::kAccBufs) {
+          acc = 0;
           acc_phase ^= 1;
         }
       }
@@ -298,60 +324,102 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each lane loads the per-row metadata of rows lane, lane+32, ... of the
+    // tile before waiting for the accumulator, so those global loads overlap
+    // the MMAs; rows are then broadcast with shuffles.
+    constexpr int kRowRegs = NT / 32;
     const int quarter = warp & 3;
     const uint32_t m = quarter * 32 + lane;
     uint32_t acc = 0, acc_phase = 0;
     for (uint32_t item = blockIdx.x; item < items; item += gridDim.x) {
-      const uint32_t q = item / args.m_tiles, i = item % args.m_tiles;
-      const NTile t = tile_of(q);
+      const uint32_t i = item_i(item);
+      const NTile t = tile_of(item_q(item));
+      const uint64_t split_base = uint64_t(item % splits) * args.split_stride;
+      float scale_a = 1.0f;
+      if (FP4 && args.a_global) scale_a = args.a_global[t.expert];
+      float r_scale[kRowRegs], r_weight[kRowRegs];
+      uint32_t r_dst[kRowRegs];
+#pragma unroll
+      for (int r = 0; r < kRowRegs; ++r) {
+        const uint32_t n = r * 32 + lane;
+        const uint32_t row = t.row_start + n;
+        r_scale[r] = 1.0f;
+        r_weight[r] = 0.0f;
+        r_dst[r] = row;
+        if (n < t.rows) {
+          if (FP4 && args.b_global) r_scale[r] = args.b_global[row];
+          if (EPI == kEpiRoutedPlane) {
+            r_weight[r] = args.row_weight[row];
+            r_dst[r] = args.row_token[row] * args.top_k + args.row_slot[row];
+          } else if (EPI == kEpiRoutedAtomic) {
+            r_weight[r] = args.row_weight[row];
+            r_dst[r] = args.row_token[row];
+          }
+        }
+      }
       if (!mbar_wait(&tfull_bar[acc], acc_phase, s_abort)) {
         fail(kStatusWaitTimeout);
         break;
       }
       tc_fence_after();
-      const uint32_t col = i * 128 + m;
+      const uint32_t col = (EPI == kEpiSwiGLU ? i * 128 : i * m_stride) + m;
+      const uint32_t col1 = i * m_stride + args.up_row_offset + m;  // second tile (non-SwiGLU dual)
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       const uint32_t c_acc = acc * (S::kAcc * NT);
-      float scale_a = 1.0f;
-      if (FP4 && args.a_global) scale_a = args.a_global[t.expert];
       for (uint32_t c0 = 0; c0 < t.rows; c0 += 16) {
+        // rows c0..c0+15 all live in register slot c0/32 (c0 is a multiple of 16)
+        const int rr = static_cast<int>(c0 / 32);
+        float src_s = r_scale[0], src_w = r_weight[0];
+        uint32_t src_d = r_dst[0];
+#pragma unroll
+        for (int r = 1; r < kRowRegs; ++r) {
+          if (r == rr) {
+            src_s = r_scale[r];
+            src_w = r_weight[r];
+            src_d = r_dst[r];
+          }
+        }
         float g[16], u[16];
         tmem_ld16(lane_base + c_acc + c0, g);
         if (DUAL) tmem_ld16(lane_base + c_acc + NT + c0, u);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const uint32_t n = c0 + j;
-          if (n >= t.rows) break;
-          const uint32_t row = t.row_start + n;
-          float s = scale_a;
-          if (FP4 && args.b_global) s = __fmul_rn(s, args.b_global[row]);
+          const float rs = __shfl_sync(0xffffffffu, src_s, n % 32);
+          const float rw = __shfl_sync(0xffffffffu, src_w, n % 32);
+          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, n % 32);
+          if (n >= t.rows) continue;
+          const float s = __fmul_rn(scale_a, rs);
           if (EPI == kEpiSwiGLU) {
             const float gv = __fmul_rn(g[j], s);
             const float uv = DUAL ? __fmul_rn(u[j], s) : 1.0f;
             const float h = __fmul_rn(silu(gv), uv);
-            reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(row) * args.ldo + col] =
+            reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(rd) * args.ldo + col] =
                 __float2bfloat16_rn(h);
           } else if (EPI == kEpiRoutedPlane) {
-            const float v = __fmul_rn(args.row_weight[row], __fmul_rn(g[j], s));
-            const uint64_t dst =
-                (uint64_t(args.row_token[row]) * args.top_k + args.row_slot[row]) * args.ldo + col;
-            reinterpret_cast<float*>(args.out)[dst] = v;
+            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
+            o[col] = __fmul_rn(rw, __fmul_rn(g[j], s));
+            if (DUAL) o[col1] = __fmul_rn(rw, __fmul_rn(u[j], s));
           } else if (EPI == kEpiRoutedAtomic) {
-            const float v = __fmul_rn(args.row_weight[row], __fmul_rn(g[j], s));
-            atomicAdd(reinterpret_cast<float*>(args.out) + uint64_t(args.row_token[row]) * args.ldo + col,
-                      v);
+            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
+            atomicAdd(o + col, __fmul_rn(rw, __fmul_rn(g[j], s)));
+            if (DUAL) atomicAdd(o + col1, __fmul_rn(rw, __fmul_rn(u[j], s)));
+          } else if (EPI == kEpiStorePartial) {
+            float* o = reinterpret_cast<float*>(args.out) + split_base + uint64_t(rd) * args.ldo;
+            o[col] = __fmul_rn(g[j], s);
+            if (DUAL) o[args.ldo_up + col] = __fmul_rn(u[j], s);
           } else {
-            reinterpret_cast<float*>(args.out)[uint64_t(row) * args.ldo + col] = __fmul_rn(g[j], s);
+            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
+            o[col] = __fmul_rn(g[j], s);
+            if (DUAL) o[col1] = __fmul_rn(u[j], s);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (S::kAccBufs == 2) {
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
-      } else {
+      if (++acc == S::kAccBufs) {
+        acc = 0;
         acc_phase ^= 1;
       }
     }

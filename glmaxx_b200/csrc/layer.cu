@@ -51,9 +51,10 @@ struct RoutePlan {
 struct LayerPlan {
   RoutePlan r;
   uint32_t H, I, Is, nt, sf_rows, max_tiles;
+  uint32_t s1_splits, s1_kc, s2_splits, s2_kc;  // shared-expert split-K (decode)
   bool decode, shared;
   uint64_t tiles, tile_count, route_row, row_token, row_slot, row_weight, gx, gh, row_prow;
-  uint64_t xq, xsf, hbuf, hq, hsf, plane, hs, sbuf, total;
+  uint64_t xq, xsf, hbuf, hq, hsf, plane, hs, sbuf, sparts1, sparts2, total;
 
   void build(const glmaxx_moe_layer_descriptor& d) {
     Carve c;
@@ -85,6 +86,16 @@ struct LayerPlan {
     plane = decode ? c.take(uint64_t(A) * H * 4) : c.take(0);
     hs = shared ? c.take(uint64_t(r.T) * Is * 2) : c.take(0);
     sbuf = (shared && decode) ? c.take(uint64_t(r.T) * H * 4) : c.take(0);
+    // Decode runs the shared expert as split-K GEMMs so that its few output
+    // tiles still cover every SM (sized for up to 148 SMs).
+    s1_splits = s1_kc = s2_splits = s2_kc = 1;
+    if (shared && decode) {
+      const uint32_t nt_tiles = (r.T + 63) / 64;
+      choose_k_splits(nt_tiles * (Is / 128), 2 * H / 128, 148, 16, &s1_splits, &s1_kc);
+      choose_k_splits(nt_tiles * (H / 128), 2 * Is / 128, 148, 16, &s2_splits, &s2_kc);
+    }
+    sparts1 = (shared && decode) ? c.take(uint64_t(s1_splits) * r.T * 2 * Is * 4) : c.take(0);
+    sparts2 = (shared && decode) ? c.take(uint64_t(s2_splits) * r.T * H * 4) : c.take(0);
     total = c.cursor + kAlign;  // slack so the caller's base need only be 16-byte aligned
   }
 };
@@ -100,7 +111,7 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
   if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT)) return false;
   if (d.path > GLMAXX_FC1_PREFILL_GROUPED) return false;
   if (d.tokens == 0 || d.tokens > 65536) return false;
-  if (d.hidden == 0 || d.hidden % 256 != 0 || d.hidden > 16384) return false;
+  if (d.hidden == 0 || d.hidden % 256 != 0 || d.hidden > 16384) return false;  // <= 256 k-blocks
   if (d.experts == 0 || d.experts > 256) return false;
   if (d.top_k == 0 || d.top_k > 8 || d.top_k > d.experts) return false;
   if (uint64_t(d.tokens) * d.top_k > (1u << 20)) return false;
@@ -327,10 +338,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     g1.args.m_tiles = p.Is / 128;
     g1.args.k_chunks = 2 * p.H / 128;
     g1.args.up_row_offset = p.Is;
-    g1.args.ldo = p.Is;
-    g1.args.out = at<void>(ws, p.hs);
     g1.args.status = status;
-    CHECK(launch_gemm(p.decode ? kShared1Bf16N64 : kShared1Bf16N128, g1, info.sms, stream));
     GemmLaunch g2{};
     g2.a = reinterpret_cast<const void*>(d.shared2_bf16);
     g2.a_experts = 1;
@@ -343,9 +351,30 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     g2.args.m_tiles = p.H / 128;
     g2.args.k_chunks = 2 * p.Is / 128;
     g2.args.ldo = p.H;
-    g2.args.out = p.decode ? at<void>(ws, p.sbuf) : static_cast<void*>(out);
     g2.args.status = status;
-    CHECK(launch_gemm(p.decode ? kShared2Bf16N64 : kShared2Bf16N128, g2, info.sms, stream));
+    if (p.decode) {
+      // split-K partial planes, reduced in slice order by the finish / combine kernels
+      g1.args.k_splits = p.s1_splits;
+      g1.args.kc_per_split = p.s1_kc;
+      g1.args.ldo = 2 * p.Is;
+      g1.args.ldo_up = p.Is;
+      g1.args.split_stride = uint64_t(r.T) * 2 * p.Is;
+      g1.args.out = at<void>(ws, p.sparts1);
+      CHECK(launch_gemm(kShared1Bf16N64Split, g1, info.sms, stream));
+      CHECK(launch_swiglu_finish(at<float>(ws, p.sparts1), p.s1_splits, r.T, p.Is,
+                                 at<uint16_t>(ws, p.hs), stream));
+      g2.args.k_splits = p.s2_splits;
+      g2.args.kc_per_split = p.s2_kc;
+      g2.args.split_stride = uint64_t(r.T) * p.H;
+      g2.args.out = at<void>(ws, p.sparts2);
+      CHECK(launch_gemm(kShared2Bf16N64Split, g2, info.sms, stream));
+    } else {
+      g1.args.ldo = p.Is;
+      g1.args.out = at<void>(ws, p.hs);
+      CHECK(launch_gemm(kShared1Bf16N128, g1, info.sms, stream));
+      g2.args.out = static_cast<void*>(out);
+      CHECK(launch_gemm(kShared2Bf16N128, g2, info.sms, stream));
+    }
   } else if (!p.decode) {
     CHECK(cudaMemsetAsync(out, 0, uint64_t(r.T) * p.H * 4, stream));
   }
@@ -363,7 +392,10 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     GemmArgs& a = g.args;
     a.tiles = tiles;
     a.tile_count = tile_count;
-    a.m_tiles = p.H / 128;
+    // decode: two adjacent 128-row M tiles per item (shared B tile)
+    a.m_tiles = p.decode ? p.H / 256 : p.H / 128;
+    a.m_stride = p.decode ? 256 : 128;
+    a.up_row_offset = p.decode ? 128 : 0;
     a.k_chunks = p.I / 256;
     a.kblocks = p.I / 64;
     a.ldo = p.H;
@@ -378,12 +410,13 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     a.row_slot = q.row_slot;
     a.row_weight = q.row_weight;
     a.status = status;
-    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4 : kFc2PrefillFp4, g, info.sms, stream));
+    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair : kFc2PrefillFp4, g, info.sms, stream));
   }
   // 8. deterministic combine (decode): ascending-expert sum + shared
   CHECK(mark(kStageCombine, stream));
   if (p.decode)
     CHECK(launch_combine(at<float>(ws, p.plane), experts,
+                         p.shared ? at<float>(ws, p.sparts2) : nullptr, p.s2_splits,
                          p.shared ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H, r.K, stream));
   CHECK(mark(kLayerStages, stream));
 #undef CHECK

@@ -120,7 +120,10 @@ cudaError_t launch_quant_rows(const QuantRowsArgs& a, cudaStream_t stream);
 cudaError_t launch_slot_table(const SlotArgs& a, cudaStream_t stream);
 cudaError_t launch_slot_reduce(const SlotArgs& a, cudaStream_t stream);
 cudaError_t launch_combine(const float* plane, const uint16_t* experts, const float* shared,
-                           float* out, uint32_t T, uint32_t H, uint32_t top_k, cudaStream_t stream);
+                           uint32_t shared_splits, float* shared_out, float* out, uint32_t T,
+                           uint32_t H, uint32_t top_k, cudaStream_t stream);
+cudaError_t launch_swiglu_finish(const float* parts, uint32_t splits, uint32_t T, uint32_t I,
+                                 uint16_t* h, cudaStream_t stream);
 cudaError_t launch_pack(const void* src, int src_bf16, uint32_t batch, uint32_t N, uint32_t K,
                         uint8_t* values, uint8_t* scales, float* global_scale, float* global_amax,
                         uint32_t* amax_scratch, uint32_t* status, cudaStream_t stream);
@@ -147,7 +150,15 @@ enum GemmVariant : int {
   kShared2Bf16N128 = 7,
   kFc2DecodeFp4Store = 8,  // NVFP4, N tile 32, store f32 (reference FC2 assignment plane)
   kFc2PrefillFp4Store = 9, // NVFP4, N tile 128, store f32
+  kShared1Bf16N64Split = 10,  // BF16, gate+up, N tile 64, split-K partials
+  kShared2Bf16N64Split = 11,  // BF16, N tile 64, split-K partials
+  kFc2DecodeFp4Pair = 12,     // NVFP4, two adjacent M tiles per item, N tile 32, routed plane
 };
+
+// Number of K slices (and chunks per slice) that spread `tiles` output tiles of
+// k_chunks chunks over about `sms` CTAs, every slice non-empty.
+void choose_k_splits(uint32_t tiles, uint32_t k_chunks, int sms, uint32_t max_splits,
+                     uint32_t* splits, uint32_t* kc_per);
 
 int gemm_tile_rows(GemmVariant v);
 cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStream_t stream);

@@ -33,17 +33,22 @@ namespace glmaxx {
 //   logit[t][e] = ((s_0 + s_1) + ...) + s_7,  s_c = fma-chain over the c-th
 //   eighth of H in ascending k from 0.
 // grid (E/32, ceil(T/32), 8), 256 threads: warp w -> experts e0+4w..e0+4w+3,
-// lane -> token t0+lane; both tiles staged in shared memory (padded pitch).
-// The first kernel of a step also clears the token-in-expert bitmap.
+// lane -> token t0+lane.  The first kernel of a step also clears the
+// token-in-expert bitmap.
 // ---------------------------------------------------------------------------
+// K is staged through shared memory in fp32 sub-tiles of 256 (pitch 260 keeps
+// the 128-bit loads of one warp phase on distinct banks); each thread keeps four
+// independent fma-chains (4 experts of one token) in ascending k.
+constexpr uint32_t kRouterSub = 256;
+constexpr uint32_t kRouterPitch = kRouterSub + 4;
+
 __global__ void __launch_bounds__(256) router_logits_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
     uint32_t T, uint32_t H, uint32_t E, uint32_t* __restrict__ bitmap, uint32_t bitmap_words) {
-  extern __shared__ uint32_t rsm[];
-  const uint32_t chunk_w = H / 16;  // 32-bit words (bf16 pairs) per chunk
-  const uint32_t pitch = chunk_w + 1;
-  uint32_t* xs = rsm;
-  uint32_t* ws = rsm + 32 * pitch;
+  extern __shared__ float rsm[];
+  float* xs = rsm;                        // [32 tokens][kRouterPitch]
+  float* ws = rsm + 32 * kRouterPitch;    // [32 experts][kRouterPitch]
+  const uint32_t chunk = H / 8;
   const uint32_t e0 = blockIdx.x * 32, t0 = blockIdx.y * 32, c = blockIdx.z;
   const uint32_t tid = threadIdx.x;
   {
@@ -51,28 +56,44 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
     const uint64_t nthreads = uint64_t(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
     for (uint64_t i = lin * blockDim.x + tid; i < bitmap_words; i += nthreads) bitmap[i] = 0;
   }
-  const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x);
-  const uint32_t* w32 = reinterpret_cast<const uint32_t*>(w);
-  for (uint32_t i = tid; i < 32 * chunk_w; i += 256) {
-    const uint32_t r = i / chunk_w, k = i % chunk_w;
-    const uint32_t tt = t0 + r, ee = e0 + r;
-    xs[r * pitch + k] = tt < T ? x32[uint64_t(tt) * (H / 2) + c * chunk_w + k] : 0u;
-    ws[r * pitch + k] = ee < E ? w32[uint64_t(ee) * (H / 2) + c * chunk_w + k] : 0u;
-  }
-  __syncthreads();
   const uint32_t warp = tid >> 5, lane = tid & 31;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint32_t* xr = xs + lane * pitch;
-  const uint32_t* wr = ws + (warp * 4) * pitch;
-#pragma unroll 4
-  for (uint32_t k = 0; k < chunk_w; ++k) {
-    const uint32_t xv = xr[k];
-    const float xl = __uint_as_float(xv << 16), xh = __uint_as_float(xv & 0xffff0000u);
+  for (uint32_t k0 = 0; k0 < chunk; k0 += kRouterSub) {
+    const uint32_t kn = min(kRouterSub, chunk - k0);  // multiple of 8 (H % 256 == 0)
+    __syncthreads();
+    // fill: 32 rows x kn bf16 of x and of w, 8 elements (16 bytes) per load
+    for (uint32_t v = tid; v < 32 * (kn / 8); v += 256) {
+      const uint32_t r = v / (kn / 8), kk = (v % (kn / 8)) * 8;
+      const uint64_t col = uint64_t(c) * chunk + k0 + kk;
+      uint4 xv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+      if (t0 + r < T) xv = *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + col);
+      if (e0 + r < E) wv = *reinterpret_cast<const uint4*>(w + uint64_t(e0 + r) * H + col);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, wwv[4] = {wv.x, wv.y, wv.z, wv.w};
+      float4* xd = reinterpret_cast<float4*>(xs + r * kRouterPitch + kk);
+      float4* wd = reinterpret_cast<float4*>(ws + r * kRouterPitch + kk);
+      xd[0] = make_float4(__uint_as_float(xw[0] << 16), __uint_as_float(xw[0] & 0xffff0000u),
+                          __uint_as_float(xw[1] << 16), __uint_as_float(xw[1] & 0xffff0000u));
+      xd[1] = make_float4(__uint_as_float(xw[2] << 16), __uint_as_float(xw[2] & 0xffff0000u),
+                          __uint_as_float(xw[3] << 16), __uint_as_float(xw[3] & 0xffff0000u));
+      wd[0] = make_float4(__uint_as_float(wwv[0] << 16), __uint_as_float(wwv[0] & 0xffff0000u),
+                          __uint_as_float(wwv[1] << 16), __uint_as_float(wwv[1] & 0xffff0000u));
+      wd[1] = make_float4(__uint_as_float(wwv[2] << 16), __uint_as_float(wwv[2] & 0xffff0000u),
+                          __uint_as_float(wwv[3] << 16), __uint_as_float(wwv[3] & 0xffff0000u));
+    }
+    __syncthreads();
+    const float* xr = xs + lane * kRouterPitch;
+    const float* wr = ws + (warp * 4) * kRouterPitch;
+#pragma unroll 2
+    for (uint32_t k = 0; k < kn; k += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t wv = wr[j * pitch + k];
-      acc[j] = fmaf(xl, __uint_as_float(wv << 16), acc[j]);
-      acc[j] = fmaf(xh, __uint_as_float(wv & 0xffff0000u), acc[j]);
+      for (int j = 0; j < 4; ++j) {
+        const float4 wv = *reinterpret_cast<const float4*>(wr + j * kRouterPitch + k);
+        acc[j] = fmaf(xv.x, wv.x, acc[j]);
+        acc[j] = fmaf(xv.y, wv.y, acc[j]);
+        acc[j] = fmaf(xv.z, wv.z, acc[j]);
+        acc[j] = fmaf(xv.w, wv.w, acc[j]);
+      }
     }
   }
   const uint32_t t = t0 + lane;
@@ -92,8 +113,13 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
 //   them (slot order = descending choice, ties -> lower index);
 //   weight = (s / sum_slots s) * route_scale, the sum taken in slot order.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ bool better(float v, uint32_t e, float ov, uint32_t oe) {
-  return v > ov || (v == ov && e < oe);
+// Order-preserving 32-bit key of a non-NaN float (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
 __global__ void __launch_bounds__(256) router_select_kernel(
@@ -101,109 +127,92 @@ __global__ void __launch_bounds__(256) router_select_kernel(
     uint32_t groups, uint32_t topk_groups, uint32_t top_k, float route_scale,
     uint16_t* __restrict__ experts_out, float* __restrict__ weights_out,
     uint32_t* __restrict__ bitmap, uint32_t bitmap_stride, uint32_t* __restrict__ status) {
-  __shared__ float gsm[8][32];
+  constexpr uint32_t kFull = 0xffffffffu;
+  constexpr uint32_t kNone = 0u;  // key below every finite choice (fkey(-inf) > 0)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t t = blockIdx.x * 8 + warp;
   if (t >= T) return;
   const uint32_t nj = (E + 31) / 32;
-  float s[8], ch[8];
+  const uint32_t gs = E / groups;
+  float s[8];
+  uint32_t key[8], gid[8];
   bool bad = false;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    s[j] = 0.f;
-    ch[j] = -INFINITY;
     const uint32_t e = lane + 32 * j;
-    if (j < nj && e < E) {
-      float L = partial[uint64_t(t) * E + e];
+    float L = 0.f;
+    const bool valid = j < nj && e < E;
+    if (valid) {
+      L = partial[uint64_t(t) * E + e];
 #pragma unroll
       for (int c = 1; c < 8; ++c) L = __fadd_rn(L, partial[(uint64_t(c) * T + t) * E + e]);
+    }
+    s[j] = 0.f;
+    key[j] = kNone;
+    gid[j] = 0xffffffffu;
+    if (valid) {
       if (!isfinite(L)) bad = true;
       s[j] = router_sigmoid(L);
-      ch[j] = __fadd_rn(s[j], bias[e]);
+      key[j] = fkey(__fadd_rn(s[j], bias[e]));
+      gid[j] = e / gs;
     }
   }
-  const uint32_t gs = E / groups;
+  // group score = top1 + top2 of the group's choices
+  float gscore[32];
   for (uint32_t g = 0; g < groups; ++g) {
-    float t1 = -INFINITY, t2 = -INFINITY;
+    uint32_t l1 = kNone, l2 = kNone;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t e = lane + 32 * j;
-      if (j < nj && e < E && e / gs == g) {
-        const float v = ch[j];
-        if (v > t1) {
-          t2 = t1;
-          t1 = v;
-        } else if (v > t2) {
-          t2 = v;
+      if (gid[j] == g) {
+        if (key[j] > l1) {
+          l2 = l1;
+          l1 = key[j];
+        } else if (key[j] > l2) {
+          l2 = key[j];
         }
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float o1 = __shfl_xor_sync(0xffffffffu, t1, off);
-      const float o2 = __shfl_xor_sync(0xffffffffu, t2, off);
-      if (o1 > t1) {
-        t2 = fmaxf(t1, o2);
-        t1 = o1;
-      } else {
-        t2 = fmaxf(t2, o1);
-      }
-    }
-    if (lane == 0) gsm[warp][g] = gs >= 2 ? __fadd_rn(t1, t2) : t1;
+    const uint32_t m1 = __reduce_max_sync(kFull, l1);
+    const uint32_t owner = __reduce_min_sync(kFull, l1 == m1 ? lane : 32u);
+    const uint32_t m2 = __reduce_max_sync(kFull, lane == owner ? l2 : l1);
+    gscore[g] = gs >= 2 ? __fadd_rn(fkey_inv(m1), fkey_inv(m2)) : fkey_inv(m1);
   }
-  __syncwarp();
+  // keep the best topk_groups groups (ties -> lower group index)
   uint32_t gmask = 0;
   for (uint32_t r = 0; r < topk_groups; ++r) {
-    float v = (lane < groups && !((gmask >> lane) & 1u)) ? gsm[warp][lane] : -INFINITY;
-    uint32_t gi = lane < groups && !((gmask >> lane) & 1u) ? lane : 0xffffffffu;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, v, off);
-      const uint32_t oi = __shfl_xor_sync(0xffffffffu, gi, off);
-      if (better(ov, oi, v, gi)) {
-        v = ov;
-        gi = oi;
-      }
-    }
-    if (gi < groups) gmask |= 1u << gi;
+    int best = -1;
+    for (uint32_t g = 0; g < groups; ++g)
+      if (!((gmask >> g) & 1u) && (best < 0 || gscore[g] > gscore[best])) best = static_cast<int>(g);
+    gmask |= 1u << best;
   }
+  // top_k experts by choice among the kept groups (ties -> lower expert index)
   uint32_t taken = 0;
-  uint32_t my_e = 0xffffffffu;
-  float my_s = 0.f;
-  float denom = 0.f;
+  uint32_t my_e = 0;
+  float my_s = 0.f, denom = 0.f;
   for (uint32_t k = 0; k < top_k; ++k) {
-    float bv = -INFINITY, bs = 0.f;
-    uint32_t be = 0xffffffffu;
+    uint32_t bk = kNone, be = 0xffffu;
+    float bs = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t e = lane + 32 * j;
-      if (j < nj && e < E && ((gmask >> (e / gs)) & 1u) && !((taken >> j) & 1u) &&
-          (be == 0xffffffffu || ch[j] > bv)) {
-        bv = ch[j];
+      if (gid[j] != 0xffffffffu && ((gmask >> gid[j]) & 1u) && !((taken >> j) & 1u) &&
+          (be == 0xffffu || key[j] > bk)) {
+        bk = key[j];
+        be = lane + 32 * j;
         bs = s[j];
-        be = e;
       }
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
-      const uint32_t oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (oe != 0xffffffffu && (be == 0xffffffffu || better(ov, oe, bv, be))) {
-        bv = ov;
-        bs = os;
-        be = oe;
-      }
-    }
-    if (be == 0xffffffffu) {
+    const uint32_t mk = __reduce_max_sync(kFull, bk);
+    const uint32_t we = __reduce_min_sync(kFull, (be != 0xffffu && bk == mk) ? be : 0xffffu);
+    if (we == 0xffffu) {
       bad = true;
-      be = 0;
+      continue;
     }
-    if ((be & 31u) == lane) taken |= 1u << (be >> 5);
-    denom = k == 0 ? bs : __fadd_rn(denom, bs);
+    const float ws_ = __shfl_sync(kFull, bs, we & 31u);
+    if ((we & 31u) == lane) taken |= 1u << (we >> 5);
+    denom = k == 0 ? ws_ : __fadd_rn(denom, ws_);
     if (lane == k) {
-      my_e = be;
-      my_s = bs;
+      my_e = we;
+      my_s = ws_;
     }
   }
   if (lane < top_k) {
@@ -356,7 +365,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
-__global__ void __launch_bounds__(1024) quant_scatter_kernel(QuantScatterArgs a) {
+__global__ void __launch_bounds__(256) quant_scatter_kernel(QuantScatterArgs a) {
   __shared__ float red[33];
   const uint32_t t = blockIdx.x, kb = threadIdx.x;
   const uint32_t KB = a.H / 64;
@@ -566,7 +575,7 @@ __global__ void __launch_bounds__(1024) compat_prepare_kernel(CompatPrepareArgs 
 
 // Reference-ABI quantiser, one CTA per compacted row, one thread per 64-wide
 // k-block (nvfp4_routed_fc1.cu:76-147 semantics, expert-local scale layout).
-__global__ void __launch_bounds__(1024) quant_rows_kernel(QuantRowsArgs a) {
+__global__ void __launch_bounds__(256) quant_rows_kernel(QuantRowsArgs a) {
   __shared__ float red[33];
   const uint32_t r = blockIdx.x, kb = threadIdx.x;
   const uint32_t KB = a.K / 64;
@@ -650,7 +659,8 @@ __global__ void slot_reduce_kernel(SlotArgs a) {
 // (routed_fc2.rs:63-86); routed + shared follows routed_fc2.rs:250-256.
 // ---------------------------------------------------------------------------
 __global__ void combine_kernel(const float* __restrict__ plane, const uint16_t* __restrict__ experts,
-                               const float* __restrict__ shared, float* __restrict__ out, uint32_t T,
+                               const float* __restrict__ shared, uint32_t shared_splits,
+                               float* __restrict__ shared_out, float* __restrict__ out, uint32_t T,
                                uint32_t H, uint32_t top_k) {
   const uint32_t t = blockIdx.y;
   const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
@@ -679,13 +689,40 @@ __global__ void combine_kernel(const float* __restrict__ plane, const uint16_t* 
     acc.w = __fadd_rn(acc.w, v.w);
   }
   if (shared) {
-    const float4 s = *reinterpret_cast<const float4*>(shared + uint64_t(t) * H + c);
+    // shared expert = sum of its split-K partial planes in slice order
+    const uint64_t stride = uint64_t(T) * H;
+    float4 s = *reinterpret_cast<const float4*>(shared + uint64_t(t) * H + c);
+    for (uint32_t k = 1; k < shared_splits; ++k) {
+      const float4 v = *reinterpret_cast<const float4*>(shared + k * stride + uint64_t(t) * H + c);
+      s.x = __fadd_rn(s.x, v.x);
+      s.y = __fadd_rn(s.y, v.y);
+      s.z = __fadd_rn(s.z, v.z);
+      s.w = __fadd_rn(s.w, v.w);
+    }
+    if (shared_out) *reinterpret_cast<float4*>(shared_out + uint64_t(t) * H + c) = s;
     acc.x = __fadd_rn(acc.x, s.x);
     acc.y = __fadd_rn(acc.y, s.y);
     acc.z = __fadd_rn(acc.z, s.z);
     acc.w = __fadd_rn(acc.w, s.w);
   }
   *reinterpret_cast<float4*>(out + uint64_t(t) * H + c) = acc;
+}
+
+// Shared-expert FC1 finish after split-K: gate/up = sums of the slice partials
+// (parts[s][t][0..I) gate, [I..2I) up, slice order), h = bf16(silu(gate) * up).
+__global__ void swiglu_finish_kernel(const float* __restrict__ parts, uint32_t splits, uint32_t T,
+                                     uint32_t I, uint16_t* __restrict__ h) {
+  const uint64_t idx = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x;
+  if (idx >= uint64_t(T) * I) return;
+  const uint64_t t = idx / I, c = idx % I;
+  const uint64_t stride = uint64_t(T) * 2 * I;
+  float g = parts[t * 2 * I + c], u = parts[t * 2 * I + I + c];
+  for (uint32_t s = 1; s < splits; ++s) {
+    g = __fadd_rn(g, parts[s * stride + t * 2 * I + c]);
+    u = __fadd_rn(u, parts[s * stride + t * 2 * I + I + c]);
+  }
+  const __nv_bfloat16 b = __float2bfloat16_rn(__fmul_rn(silu(g), u));
+  h[idx] = *reinterpret_cast<const uint16_t*>(&b);
 }
 
 // ---------------------------------------------------------------------------
@@ -749,13 +786,16 @@ __global__ void pack_encode_kernel(const void* __restrict__ src, int src_bf16, u
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
                                  uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,
                                  cudaStream_t stream) {
-  const size_t smem = 2ull * 32 * (H / 16 + 1) * 4;
-  static bool configured = false;
-  if (!configured) {
+  const size_t smem = 2ull * 32 * kRouterPitch * 4;
+  static bool configured[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
     cudaError_t st = cudaFuncSetAttribute(router_logits_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
     if (st != cudaSuccess) return st;
-    configured = true;
+    configured[dev] = true;
   }
   dim3 grid((E + 31) / 32, (T + 31) / 32, 8);
   router_logits_kernel<<<grid, 256, smem, stream>>>(x, w, partial, T, H, E, bitmap, bitmap_words);
@@ -840,10 +880,19 @@ cudaError_t launch_slot_reduce(const SlotArgs& a, cudaStream_t stream) {
 }
 
 cudaError_t launch_combine(const float* plane, const uint16_t* experts, const float* shared,
-                           float* out, uint32_t T, uint32_t H, uint32_t top_k,
-                           cudaStream_t stream) {
+                           uint32_t shared_splits, float* shared_out, float* out, uint32_t T,
+                           uint32_t H, uint32_t top_k, cudaStream_t stream) {
   dim3 grid((H / 4 + 255) / 256, T);
-  combine_kernel<<<grid, 256, 0, stream>>>(plane, experts, shared, out, T, H, top_k);
+  combine_kernel<<<grid, 256, 0, stream>>>(plane, experts, shared, shared_splits, shared_out, out,
+                                           T, H, top_k);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_swiglu_finish(const float* parts, uint32_t splits, uint32_t T, uint32_t I,
+                                 uint16_t* h, cudaStream_t stream) {
+  const uint64_t n = uint64_t(T) * I;
+  swiglu_finish_kernel<<<static_cast<uint32_t>((n + 255) / 256), 256, 0, stream>>>(parts, splits,
+                                                                                  T, I, h);
   return cudaPeekAtLastError();
 }
 

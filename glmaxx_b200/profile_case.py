@@ -1,0 +1,54 @@
+"""Run a few routed-MoE layer steps of a chosen shape (the target of ncu captures).
+
+    python -m glmaxx_b200.profile_case --experts 64 --tokens 64 --steps 3 [--tp 1] [--path 1]
+
+Per step the layer launches, in order: router_logits, router_select, compact,
+quant_scatter, FC1 grouped GEMM, fc2_quant, shared FC1 GEMM, shared FC2 GEMM,
+FC2 grouped GEMM, combine.  With --experts < 256 the expert weights of one
+step stay a few GB, which keeps an `ncu --set full` capture small.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from . import abi, synth
+from .moe import MoEConfig, RoutedMoE
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--experts", type=int, default=64)
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--path", type=int, default=0)
+    p.add_argument("--shared", type=int, default=2048)
+    p.add_argument("--seed", type=int, default=7)
+    a = p.parse_args()
+    groups = 8 if a.experts % 8 == 0 and a.experts >= 64 else 1
+    cfg = MoEConfig(experts=a.experts, groups=groups, topk_groups=min(4, groups),
+                    shared_intermediate=a.shared, tp=a.tp)
+    dev = torch.device("cuda:0")
+    w = synth.make_rank_weights(cfg, seed=a.seed, device=dev)
+    x = synth.make_input(a.tokens, cfg.hidden, seed=a.seed, device=dev)
+    layer = RoutedMoE(cfg, w, a.tokens)
+    out = torch.empty((a.tokens, cfg.hidden), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(a.steps):
+            layer(x, out, path=a.path)
+    torch.cuda.synchronize()
+    status = layer.device_status()
+    touched = int(torch.unique(layer.routes(a.tokens)[0].long()).numel())
+    print(json.dumps({"experts": a.experts, "tokens": a.tokens, "tp": a.tp, "steps": a.steps,
+                      "touched_experts": touched, "status": status,
+                      "abi": abi.abi_string()}))
+    if status:
+        raise SystemExit(1)
+
+
+if __name__ == "__main__":
+    main()

@@ -244,15 +244,24 @@ def test_gpu_layer_prefill_path_subset():
 
 
 def test_gpu_layer_decode_and_prefill_paths_agree():
+    """The routed experts compute the same rows on both paths (only the order of the
+    prefill path's atomic combine differs).  The shared expert is split along K on the
+    decode path and not on the prefill path, so with it the two paths agree to the
+    layer tolerance rather than to fp32 reassociation."""
     cfg = MoEConfig(tp=8, rank=0)
     dev = cuda()
     w = synth.make_rank_weights(cfg, seed=9, device=dev)
     x = synth.make_input(96, cfg.hidden, seed=9, device=dev)
+    routed_only = RoutedMoE(MoEConfig(**{**cfg.__dict__, "shared_intermediate": 0}), w, 96)
+    a = routed_only(x, path=abi.DECODE_PERSISTENT).clone()
+    b = routed_only(x, path=abi.PREFILL_GROUPED).clone()
+    torch.cuda.synchronize()
+    assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
     layer = RoutedMoE(cfg, w, 96)
     a = layer(x, path=abi.DECODE_PERSISTENT).clone()
     b = layer(x, path=abi.PREFILL_GROUPED).clone()
     torch.cuda.synchronize()
-    assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) < 1e-5
+    assert_layer_close(a.cpu().numpy(), b.cpu().numpy(), "decode vs prefill")
 
 
 def test_gpu_layer_deterministic_decode():
