@@ -34,8 +34,25 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 HIDDEN, EXPERTS, INTER, TOPK = 6144, 256, 2048, 8
-METRIC = "routed-MoE layer tokens/s (decode T=64, 256 experts, top-8, NVFP4 W4A4)"
 UNIT = "tokens/s"
+WORKLOADS = {
+    "decode": {"tokens": 64, "zipf": False, "bound": "hbm",
+               "metric": "routed-MoE layer tokens/s (decode T=64, 256 experts, top-8, NVFP4 W4A4)",
+               "name": "decode T=64 (BASELINE configs[1])"},
+    "prefill": {"tokens": 8192, "zipf": True, "bound": "tensor",
+                "metric": "routed-MoE layer tokens/s (prefill T=8192, Zipf(1.1) routing, 256 "
+                          "experts, top-8, NVFP4 W4A4)",
+                "name": "prefill T=8192, Zipf(s=1.1) expert counts (BASELINE configs[2])"},
+}
+# NVFP4 dense tensor rate / bf16 dense tensor rate on B200 (9 / 2.25 PFLOP/s nominal):
+# the NVFP4 roofline is the measured cuBLAS bf16 rate scaled by this ratio.
+NVFP4_PER_BF16 = 4.0
+NVFP4_NOMINAL_TFLOPS = 9000.0
+# Zipf skew of the reference arm's own seeded router (bisection value of
+# glmaxx_b200.synth.fit_zipf_beta at the default seed); the arm times a token sample,
+# whose per-token cost does not depend on the skew.
+REF_ZIPF_BETA = 0.04
+REF_TIME_BUDGET_S = 90.0
 
 
 def parse():
@@ -44,11 +61,15 @@ def parse():
     p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-sample-tokens", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.tokens is None:
+        a.tokens = WORKLOADS[a.workload]["tokens"]
+    return a
 
 
 def routed_bytes_per_expert(local_inter: int) -> dict:
@@ -59,11 +80,12 @@ def routed_bytes_per_expert(local_inter: int) -> dict:
 
 
 def measured_peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, kind) from MEASURED_PEAKS.json, else the fallback."""
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
 class ClockSampler:
@@ -173,6 +195,19 @@ def cpu_baseline_from_device(layer, x, cfg, n_tokens: int):
                       f"NVFP4 dequant, {dt:.2f} s"}
 
 
+# FC1 DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
+# of the decode FC1 at 64 experts, T=64, TP1, divided by the touched experts of that
+# capture; FC1 traffic grows with the touched experts (weights dominate), so a
+# full launch is estimated as this figure x touched experts.
+FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 = None
+
+
+def fc1_traffic_estimate(touched: int, world: int):
+    if FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 is None:
+        return None
+    return FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 * touched / world
+
+
 def torch_index(used):
     import torch
     return torch.as_tensor(used.astype("int64"))
@@ -199,8 +234,14 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     T = args.tokens
+    wl = WORKLOADS[args.workload]
     cfg = MoEConfig(tp=world, rank=rank)
-    weights = synth.make_rank_weights(cfg, seed=args.seed, device=dev)
+    zipf = None
+    if wl["zipf"]:
+        # same beta on every rank: the fit is deterministic in (seed, router, input)
+        zipf = synth.fit_zipf_beta(cfg, T, args.seed, dev)
+    weights = synth.make_rank_weights(cfg, seed=args.seed, device=dev,
+                                      zipf_beta=None if zipf is None else zipf[0])
     x = synth.make_input(T, HIDDEN, seed=args.seed, device=dev)
     layer = RoutedMoE(cfg, weights, T)
     out = torch.empty((T, HIDDEN), dtype=torch.float32, device=dev)
@@ -303,22 +344,47 @@ def run_ours(args):
     # ---------------------------------------------------------- roofline
     re, _ = layer.routes(T)
     touched = int(torch.unique(re.long()).numel())
+    counts = torch.bincount(re.long().flatten(), minlength=EXPERTS)
     per = routed_bytes_per_expert(cfg.local_intermediate)
     A = T * TOPK
-    fc1_bytes = touched * per["fc1"] + A * (HIDDEN // 2 + HIDDEN // 16 + 4) + \
-        A * cfg.local_intermediate * 2
-    fc1_gbs = fc1_bytes / (stage_avg["fc1"] * 1e-3) / 1e9
-    peak, peak_kind = measured_peaks()
+    Ir = cfg.local_intermediate
+    hbm_peak, bf16_peak, peak_kind = measured_peaks()
     shared_bytes = 3 * cfg.local_shared * HIDDEN * 2
     layer_bytes = touched * (per["fc1"] + per["fc2"]) + shared_bytes + EXPERTS * HIDDEN * 2 + \
         T * HIDDEN * (2 + 4)
-    traffic = None
-    tf = ROOT / "profiles" / "fc1_decode_traffic.json"
-    if tf.exists():
-        try:
-            traffic = json.loads(tf.read_text()).get(f"tp{world}", {}).get("dram_bytes_per_launch")
-        except (ValueError, AttributeError):
-            traffic = None
+    fc1_ms = stage_avg["fc1"]
+    if wl["bound"] == "hbm":
+        # FC1 weights of every touched expert, the NVFP4 activation rows (values,
+        # scales, global) and the bf16 SwiGLU output rows
+        fc1_bytes = touched * per["fc1"] + A * (HIDDEN // 2 + HIDDEN // 16 + 4) + A * Ir * 2
+        achieved = fc1_bytes / (fc1_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "fc1 grouped GEMM (tcgen05 NVFP4, N tile 32)",
+                "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} HBM copy",
+                "traffic": fc1_traffic_estimate(touched, world),
+                "algorithmic_bytes_per_launch": fc1_bytes}
+    else:
+        fc1_flops = 2.0 * A * HIDDEN * (2 * Ir)
+        fc2_flops = 2.0 * A * Ir * HIDDEN
+        peak = NVFP4_PER_BF16 * bf16_peak
+        achieved = fc1_flops / (fc1_ms * 1e-3) / 1e12
+        fc2_tf = fc2_flops / (stage_avg["fc2"] * 1e-3) / 1e12
+        roof = {"bound": "tensor", "kernel": "fc1 grouped GEMM (tcgen05 NVFP4, N tile 128)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} cuBLAS bf16 burst x {NVFP4_PER_BF16:g} (NVFP4:bf16 "
+                             "dense rate)",
+                "frac_of_nominal_9pf": achieved / NVFP4_NOMINAL_TFLOPS,
+                "traffic": None, "algorithmic_flops_per_launch": fc1_flops,
+                "fc2_tflops": fc2_tf, "fc2_frac": fc2_tf / peak,
+                "routed_tflops": (fc1_flops + fc2_flops) / (ms * 1e-3) / 1e12,
+                "expert_counts": {"max": int(counts.max()), "min": int(counts.min()),
+                                  "zero": int((counts == 0).sum())}}
+        if zipf is not None:
+            roof["zipf_beta"], roof["zipf_slope"] = zipf
+    roof.update({"touched_experts": touched, "fc1_ms": fc1_ms, "layer_weight_bytes": layer_bytes,
+                 "layer_achieved_gbs": layer_bytes / (ms * 1e-3) / 1e9,
+                 "layer_frac_hbm": layer_bytes / (ms * 1e-3) / 1e9 / hbm_peak})
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -329,25 +395,19 @@ def run_ours(args):
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "metric": wl["metric"], "value": T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "nvfp4",
-            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) bias)",
-            "config": {"workload": "decode T=64 (BASELINE configs[1])", "tokens": T,
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(0,0.01) bias"
+                    + (", Zipf-skewed bias)" if zipf is not None else ")"),
+            "config": {"workload": wl["name"], "tokens": T,
                        "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOPK, "groups": 8,
                        "topk_groups": 4, "intermediate": INTER, "shared_intermediate": INTER,
                        "parallelism": f"tp{world} (expert intermediate sharded, NCCL all-reduce)",
                        "l2": "weights per step >> 126 MB L2 (no flush needed)",
                        "timing": "CUDA-graph replay of the layer + eager NCCL all-reduce, "
                                  "CUDA events on the launch stream, max over ranks"},
-            "roofline": {"bound": "hbm", "kernel": "fc1 grouped GEMM (tcgen05 NVFP4, N tile 32)",
-                         "achieved": fc1_gbs, "peak": peak, "unit": "GB/s",
-                         "frac": fc1_gbs / peak, "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": fc1_bytes, "touched_experts": touched,
-                         "fc1_ms": stage_avg["fc1"],
-                         "layer_weight_bytes": layer_bytes,
-                         "layer_achieved_gbs": layer_bytes / (ms * 1e-3) / 1e9,
-                         "layer_frac": layer_bytes / (ms * 1e-3) / 1e9 / peak},
+            "roofline": roof,
             "stage_ms": stage_avg,
             "cpu_baseline": cpu,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
@@ -375,17 +435,21 @@ def run_reference(args):
 
     import oracle as O
 
+    wl = WORKLOADS[args.workload]
     rng = np.random.default_rng(args.seed)
-    T, S = args.tokens, max(1, args.cpu_sample_tokens)
+    T = args.tokens
+    S = min(T, max(1, args.cpu_sample_tokens))
     Ir = INTER // world
-    x = O.f32_to_bf16_bits(rng.standard_normal((T, HIDDEN)).astype(np.float32))
+    # every token costs the same on this path (router + 8 expert rows), so only the
+    # sampled tokens are generated and each step runs router + layer on them
+    x = O.f32_to_bf16_bits(rng.standard_normal((S, HIDDEN)).astype(np.float32))
     wr = O.f32_to_bf16_bits((rng.standard_normal((EXPERTS, HIDDEN)) * 0.02).astype(np.float32))
     bias = (rng.standard_normal(EXPERTS) * 0.01).astype(np.float32)
-    t0 = time.perf_counter()
+    if wl["zipf"]:
+        perm = rng.permutation(EXPERTS).astype(np.float32)
+        bias = (bias + REF_ZIPF_BETA * (-1.1 * np.log1p(perm))).astype(np.float32)
     experts, weights = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
-    router_s = time.perf_counter() - t0
-    sel = np.arange(S)
-    used = np.unique(experts[sel])
+    used = np.unique(experts)
     remap = {int(e): i for i, e in enumerate(used)}
     v13, s13, g13, v2, s2, g2 = [], [], [], [], [], []
     for e in used:
@@ -396,28 +460,38 @@ def run_reference(args):
         v2.append(p2.values), s2.append(p2.scales), g2.append(p2.global_scale)
     sh13 = O.f32_to_bf16_bits((rng.standard_normal((2 * Ir, HIDDEN)) * 0.02).astype(np.float32))
     sh2 = O.f32_to_bf16_bits((rng.standard_normal((HIDDEN, Ir)) * 0.02).astype(np.float32))
-    re_m = np.vectorize(lambda e: remap[int(e)])(experts[sel]).astype(np.uint16)
-    a = (x[sel], re_m, weights[sel], np.stack(v13), np.stack(s13), np.array(g13, np.float32),
-         np.stack(v2), np.stack(s2), np.array(g2, np.float32), Ir, sh13, sh2)
-    times = []
-    for i in range(args.warmup + args.steps):
+    packed = (np.stack(v13), np.stack(s13), np.array(g13, np.float32), np.stack(v2),
+              np.stack(s2), np.array(g2, np.float32), Ir, sh13, sh2)
+
+    def step():
         t0 = time.perf_counter()
-        O.moe_layer(*a)
-        dt = time.perf_counter() - t0
-        if i >= args.warmup:
-            times.append(dt)
-    per_step = statistics.mean(times) + router_s * S / T
+        ex, wt = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
+        re_m = np.vectorize(lambda e: remap[int(e)])(ex).astype(np.uint16)
+        O.moe_layer(x, re_m, wt, *packed)
+        return time.perf_counter() - t0
+
+    # warm-up and timed steps stop early once REF_TIME_BUDGET_S is spent, so that the
+    # arm ends within a few minutes whatever K and W are; "steps" reports the count run
+    for _ in range(min(args.warmup, 2)):
+        step()
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < args.steps and (not times or
+                                       time.perf_counter() - t_start < REF_TIME_BUDGET_S):
+        times.append(step())
+    per_step = statistics.mean(times)
     value = S / per_step
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "impl": "reference", "metric": wl["metric"], "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": len(times), "steps_requested": args.steps,
+        "warmup": min(args.warmup, 2), "ms_per_step": per_step * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded, same shapes and distributions)",
-        "config": {"workload": "decode T=64 (BASELINE configs[1])", "tokens": T,
+        "config": {"workload": wl["name"], "tokens": T,
                    "parallelism": f"tp{world} shard on one host process"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
-                         "sample": f"{S} tokens of {T} per step ({len(used)} experts), "
-                                   "full layer incl. per-call NVFP4 dequant"},
+                         "sample": f"{S} tokens of {T} per step ({len(used)} experts), router "
+                                   "+ full layer incl. per-call NVFP4 dequant"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

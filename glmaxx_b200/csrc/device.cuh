@@ -206,6 +206,25 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 
 // 32 lanes x 32 bits, 16 consecutive columns.
+// Asynchronous 32-column TMEM load (32 lanes x 32 columns of 32 bits): the
+// registers are valid only after tmem_wait_ld() and reg_fence() on them.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Orders every later use of r after the preceding tmem_wait_ld() (the compiler
+// does not know that the load above writes r asynchronously).
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
@@ -247,8 +266,10 @@ __device__ __forceinline__ float router_sigmoid(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, cw_exp(-x)));
 }
 
+// SiLU of the FC1 epilogue, v / (1 + exp(-v)) with the fast exponential and
+// division intrinsics (a few ulp of fp32, far inside the bf16 rounding of h).
 __device__ __forceinline__ float silu(float v) {
-  return __fdiv_rn(v, __fadd_rn(1.0f, cw_exp(-v)));
+  return __fdividef(v, 1.0f + __expf(-v));
 }
 
 // ------------------------------------------------------------ NVFP4 encode

@@ -366,53 +366,76 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t col1 = i * m_stride + args.up_row_offset + m;  // second tile (non-SwiGLU dual)
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
       const uint32_t c_acc = acc * (S::kAcc * NT);
-      for (uint32_t c0 = 0; c0 < t.rows; c0 += 16) {
-        // rows c0..c0+15 all live in register slot c0/32 (c0 is a multiple of 16)
-        const int rr = static_cast<int>(c0 / 32);
+      // 32-column chunks; the TMEM load of chunk ch+1 is in flight while chunk ch
+      // is processed.  Chunk ch covers rows 32*ch.. of the tile: register slot ch.
+      const uint32_t nch = (t.rows + 31) / 32;
+      const uint32_t tbase = lane_base + c_acc;
+      auto process = [&](uint32_t ch, const uint32_t (&g)[32], const uint32_t (&u)[32]) {
         float src_s = r_scale[0], src_w = r_weight[0];
         uint32_t src_d = r_dst[0];
 #pragma unroll
         for (int r = 1; r < kRowRegs; ++r) {
-          if (r == rr) {
+          if (r == static_cast<int>(ch)) {
             src_s = r_scale[r];
             src_w = r_weight[r];
             src_d = r_dst[r];
           }
         }
-        float g[16], u[16];
-        tmem_ld16(lane_base + c_acc + c0, g);
-        if (DUAL) tmem_ld16(lane_base + c_acc + NT + c0, u);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t n = c0 + j;
-          const float rs = __shfl_sync(0xffffffffu, src_s, n % 32);
-          const float rw = __shfl_sync(0xffffffffu, src_w, n % 32);
-          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, n % 32);
+        for (int j = 0; j < 32; ++j) {
+          const uint32_t n = ch * 32 + j;
+          const float rs = __shfl_sync(0xffffffffu, src_s, j);
+          const float rw = __shfl_sync(0xffffffffu, src_w, j);
+          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
           if (n >= t.rows) continue;
           const float s = __fmul_rn(scale_a, rs);
+          const float gj = __uint_as_float(g[j]);
+          const float uj = DUAL ? __uint_as_float(u[j]) : 0.0f;
           if (EPI == kEpiSwiGLU) {
-            const float gv = __fmul_rn(g[j], s);
-            const float uv = DUAL ? __fmul_rn(u[j], s) : 1.0f;
+            const float gv = __fmul_rn(gj, s);
+            const float uv = DUAL ? __fmul_rn(uj, s) : 1.0f;
             const float h = __fmul_rn(silu(gv), uv);
             reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(rd) * args.ldo + col] =
                 __float2bfloat16_rn(h);
           } else if (EPI == kEpiRoutedPlane) {
             float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(rw, __fmul_rn(g[j], s));
-            if (DUAL) o[col1] = __fmul_rn(rw, __fmul_rn(u[j], s));
+            o[col] = __fmul_rn(rw, __fmul_rn(gj, s));
+            if (DUAL) o[col1] = __fmul_rn(rw, __fmul_rn(uj, s));
           } else if (EPI == kEpiRoutedAtomic) {
             float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            atomicAdd(o + col, __fmul_rn(rw, __fmul_rn(g[j], s)));
-            if (DUAL) atomicAdd(o + col1, __fmul_rn(rw, __fmul_rn(u[j], s)));
+            atomicAdd(o + col, __fmul_rn(rw, __fmul_rn(gj, s)));
+            if (DUAL) atomicAdd(o + col1, __fmul_rn(rw, __fmul_rn(uj, s)));
           } else if (EPI == kEpiStorePartial) {
             float* o = reinterpret_cast<float*>(args.out) + split_base + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(g[j], s);
-            if (DUAL) o[args.ldo_up + col] = __fmul_rn(u[j], s);
+            o[col] = __fmul_rn(gj, s);
+            if (DUAL) o[args.ldo_up + col] = __fmul_rn(uj, s);
           } else {
             float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(g[j], s);
-            if (DUAL) o[col1] = __fmul_rn(u[j], s);
+            o[col] = __fmul_rn(gj, s);
+            if (DUAL) o[col1] = __fmul_rn(uj, s);
           }
+        }
+      };
+      uint32_t ga[32], ua[32], gb[32], ub[32];
+      auto load = [&](uint32_t ch, uint32_t (&g)[32], uint32_t (&u)[32]) {
+        tmem_ld32_async(tbase + ch * 32, g);
+        if (DUAL) tmem_ld32_async(tbase + NT + ch * 32, u);
+      };
+      auto settle = [&](uint32_t (&g)[32], uint32_t (&u)[32]) {
+        tmem_wait_ld();
+        reg_fence(g);
+        if (DUAL) reg_fence(u);
+      };
+      load(0, ga, ua);
+      settle(ga, ua);
+      for (uint32_t ch = 0; ch < nch; ch += 2) {
+        if (ch + 1 < nch) load(ch + 1, gb, ub);
+        process(ch, ga, ua);
+        settle(gb, ub);
+        if (ch + 1 < nch) {
+          if (ch + 2 < nch) load(ch + 2, ga, ua);
+          process(ch + 1, gb, ub);
+          settle(ga, ua);
         }
       }
       tc_fence_before();

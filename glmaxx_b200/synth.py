@@ -38,15 +38,23 @@ def zipf_bias(experts: int, seed: int, beta: float, s: float = 1.1, device="cpu"
     return (beta * (-s * torch.log1p(perm))).to(device)
 
 
-def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | None = None,
-                      expert_chunk: int = 8, keep_masters: bool = False):
-    """Router (replicated), NVFP4 expert shards and bf16 shared shard of rank cfg.rank."""
-    E, H, I, Ir, r = cfg.experts, cfg.hidden, cfg.intermediate, cfg.local_intermediate, cfg.rank
+def make_router(cfg: MoEConfig, seed: int, device, zipf_beta: float | None = None):
+    """Router weight bf16 [E, H] ~ N(0, 0.02) and correction bias f32 [E] ~ N(0, 0.01),
+    plus the Zipf skew term when zipf_beta is given (identical on every rank)."""
+    E, H = cfg.experts, cfg.hidden
     router_w = (torch.randn(E, H, generator=_gen(device, seed * 1000 + 1), device=device) *
                 0.02).to(torch.bfloat16)
     bias = torch.randn(E, generator=_gen(device, seed * 1000 + 2), device=device) * 0.01
     if zipf_beta is not None:
         bias = bias + zipf_bias(E, seed, zipf_beta, device=device)
+    return router_w, bias
+
+
+def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | None = None,
+                      expert_chunk: int = 8, keep_masters: bool = False):
+    """Router (replicated), NVFP4 expert shards and bf16 shared shard of rank cfg.rank."""
+    E, H, I, Ir, r = cfg.experts, cfg.hidden, cfg.intermediate, cfg.local_intermediate, cfg.rank
+    router_w, bias = make_router(cfg, seed, device, zipf_beta)
     w13_parts, w2_parts = [], []
     masters = []
     for e0 in range(0, E, expert_chunk):
@@ -86,30 +94,49 @@ def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | N
     return (w, masters) if keep_masters else w
 
 
-def fit_zipf_beta(cfg: MoEConfig, tokens: int, seed: int, device, s: float = 1.1) -> float:
-    """Bisection on beta so that the log-log slope of sorted per-expert counts is ~ -s."""
-    from .moe import RoutedMoE
-    x = make_input(tokens, cfg.hidden, seed, device)
-    lo, hi = 0.0, 1.0
-    best = 0.0
-    for _ in range(12):
+def approx_route_counts(logits: torch.Tensor, bias: torch.Tensor, groups: int,
+                        topk_groups: int, top_k: int) -> torch.Tensor:
+    """Per-expert assignment counts of group-limited sigmoid top-k routing, computed
+    with plain torch ops.  Input synthesis only (fitting the Zipf skew): tie order
+    and summation order are not the layer's."""
+    T, E = logits.shape
+    gs = E // groups
+    choice = torch.sigmoid(logits) + bias
+    gscore = choice.view(T, groups, gs).topk(min(2, gs), dim=-1).values.sum(-1)
+    keep = gscore.topk(topk_groups, dim=-1).indices
+    mask = torch.zeros(T, groups, dtype=torch.bool, device=logits.device).scatter_(1, keep, True)
+    masked = choice.masked_fill(~mask.repeat_interleave(gs, 1), float("-inf"))
+    sel = masked.topk(top_k, dim=-1).indices
+    return torch.bincount(sel.flatten(), minlength=E)
+
+
+def zipf_slope(counts: torch.Tensor) -> float:
+    """Least-squares slope of log(count) against log(rank) over the non-zero counts."""
+    c = counts.double().sort(descending=True).values
+    c = c[c > 0]
+    lr = torch.arange(1, c.numel() + 1, dtype=torch.float64, device=c.device).log()
+    lc = c.log()
+    lr0, lc0 = lr - lr.mean(), lc - lc.mean()
+    return float((lr0 * lc0).sum() / (lr0 * lr0).sum())
+
+
+def fit_zipf_beta(cfg: MoEConfig, tokens: int, seed: int, device, s: float = 1.1,
+                  iters: int = 30) -> tuple[float, float]:
+    """Bisection on beta so that the log-log slope of the sorted per-expert token
+    counts is -s under this seed's router and input.  Returns (beta, slope)."""
+    x = make_input(tokens, cfg.hidden, seed, device).float()
+    router_w, bias0 = make_router(cfg, seed, device, None)
+    logits = x @ router_w.float().t()
+    lo, hi = 0.0, 2.0
+    best = (0.0, 0.0)
+    for _ in range(iters):
         mid = 0.5 * (lo + hi)
-        w = make_rank_weights(MoEConfig(**{**cfg.__dict__, "tp": 1, "rank": 0,
-                                           "shared_intermediate": 0}), seed, device,
-                              zipf_beta=mid, expert_chunk=cfg.experts)
-        layer = RoutedMoE(MoEConfig(**{**cfg.__dict__, "shared_intermediate": 0}), w, tokens)
-        layer(x)
-        counts = torch.bincount(layer.route_experts[:tokens].long().flatten(),
-                                minlength=cfg.experts).float().sort(descending=True).values
-        counts = counts[counts > 0]
-        ranks = torch.arange(1, counts.numel() + 1, device=counts.device, dtype=torch.float32)
-        slope = float(torch.linalg.lstsq(torch.stack([ranks.log(), torch.ones_like(ranks)], 1),
-                                         counts.log()[:, None]).solution[0])
-        best = mid
+        bias = bias0 + zipf_bias(cfg.experts, seed, mid, s=s, device=device)
+        slope = zipf_slope(approx_route_counts(logits, bias, cfg.groups, cfg.topk_groups,
+                                               cfg.top_k))
+        best = (mid, slope)
         if -slope < s:
             lo = mid
         else:
             hi = mid
-        if math.isclose(-slope, s, rel_tol=0.02):
-            break
     return best
