@@ -79,7 +79,12 @@ template <bool FP4, bool DUAL, int NT>
 struct GemmShape {
   static constexpr int kAcc = DUAL ? 2 : 1;
   static constexpr int kNJ = NT >= 128 ? NT / 128 : 1;              // SFB atoms along N
-  static constexpr int kSfCols = FP4 ? (kAcc * 16 + 16 * kNJ) : 0;  // TMEM columns for scales
+  // TMEM columns of one stage's scale factors (4 K-blocks x 4 columns per operand).
+  static constexpr int kSfSetCols = FP4 ? (kAcc * 16 + 16 * kNJ) : 0;
+  // Two scale sets alternate between consecutive stages, so the scale copy of
+  // stage s+1 never overwrites columns that the MMAs of stage s still read.
+  static constexpr int kSfSets = FP4 ? 2 : 0;
+  static constexpr int kSfCols = kSfSets * kSfSetCols;  // TMEM columns for scales
   // Accumulator buffers (up to 4) let the MMA warp run items ahead of the epilogue.
   static constexpr int kAccBufsFit = (512 - kSfCols) / (kAcc * NT);
   static constexpr int kAccBufs = kAccBufsFit >= 4 ? 4 : (kAccBufsFit >= 1 ? kAccBufsFit : 1);
@@ -254,9 +259,8 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t sf_base = tmem + S::kAccBufs * S::kAcc * NT;  // column offset
-      const uint32_t sfa_t0 = sf_base, sfa_t1 = sf_base + 16;
-      const uint32_t sfb_t = sf_base + S::kAcc * 16;
+      const uint32_t sf_base0 = tmem + S::kAccBufs * S::kAcc * NT;  // column offset
+      uint32_t sf_set = 0;
       constexpr uint32_t kIdesc = FP4 ? idesc_mxf4nvf4(NT) : idesc_bf16(NT);
       uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
       bool ok = true;
@@ -276,6 +280,10 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           tc_fence_after();
+          const uint32_t sf_base = sf_base0 + sf_set * S::kSfSetCols;
+          const uint32_t sfa_t0 = sf_base, sfa_t1 = sf_base + 16;
+          const uint32_t sfb_t = sf_base + S::kAcc * 16;
+          sf_set ^= 1u;
           if (FP4) {
 #pragma unroll
             for (int kb = 0; kb < 4; ++kb) {
@@ -370,7 +378,10 @@ __global__ void __launch_bounds__(192, 1)
       // is processed.  Chunk ch covers rows 32*ch.. of the tile: register slot ch.
       const uint32_t nch = (t.rows + 31) / 32;
       const uint32_t tbase = lane_base + c_acc;
-      auto process = [&](uint32_t ch, const uint32_t (&g)[32], const uint32_t (&u)[32]) {
+      // Values of all 32 columns are computed first, branch-free, so that their
+      // latency chains (exp, reciprocal) overlap; the stores then skip the rows
+      // past the end of the tile.
+      auto process = [&](uint32_t ch, uint32_t (&g)[32], uint32_t (&u)[32]) {
         float src_s = r_scale[0], src_w = r_weight[0];
         uint32_t src_d = r_dst[0];
 #pragma unroll
@@ -383,36 +394,41 @@ __global__ void __launch_bounds__(192, 1)
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const uint32_t n = ch * 32 + j;
-          const float rs = __shfl_sync(0xffffffffu, src_s, j);
-          const float rw = __shfl_sync(0xffffffffu, src_w, j);
-          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
-          if (n >= t.rows) continue;
-          const float s = __fmul_rn(scale_a, rs);
-          const float gj = __uint_as_float(g[j]);
-          const float uj = DUAL ? __uint_as_float(u[j]) : 0.0f;
+          const float s = __fmul_rn(scale_a, __shfl_sync(0xffffffffu, src_s, j));
+          const float gj = __fmul_rn(__uint_as_float(g[j]), s);
+          const float uj = DUAL ? __fmul_rn(__uint_as_float(u[j]), s) : 0.0f;
           if (EPI == kEpiSwiGLU) {
-            const float gv = __fmul_rn(gj, s);
-            const float uv = DUAL ? __fmul_rn(uj, s) : 1.0f;
-            const float h = __fmul_rn(silu(gv), uv);
+            g[j] = __float_as_uint(__fmul_rn(silu(gj), DUAL ? uj : 1.0f));
+          } else if (EPI == kEpiRoutedPlane || EPI == kEpiRoutedAtomic) {
+            const float rw = __shfl_sync(0xffffffffu, src_w, j);
+            g[j] = __float_as_uint(__fmul_rn(rw, gj));
+            if (DUAL) u[j] = __float_as_uint(__fmul_rn(rw, uj));
+          } else {
+            g[j] = __float_as_uint(gj);
+            if (DUAL) u[j] = __float_as_uint(uj);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
+          if (ch * 32 + j >= t.rows) continue;
+          const float v0 = __uint_as_float(g[j]);
+          const float v1 = __uint_as_float(u[j]);
+          if (EPI == kEpiSwiGLU) {
             reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(rd) * args.ldo + col] =
-                __float2bfloat16_rn(h);
-          } else if (EPI == kEpiRoutedPlane) {
-            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(rw, __fmul_rn(gj, s));
-            if (DUAL) o[col1] = __fmul_rn(rw, __fmul_rn(uj, s));
+                __float2bfloat16_rn(v0);
           } else if (EPI == kEpiRoutedAtomic) {
             float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            atomicAdd(o + col, __fmul_rn(rw, __fmul_rn(gj, s)));
-            if (DUAL) atomicAdd(o + col1, __fmul_rn(rw, __fmul_rn(uj, s)));
+            atomicAdd(o + col, v0);
+            if (DUAL) atomicAdd(o + col1, v1);
           } else if (EPI == kEpiStorePartial) {
             float* o = reinterpret_cast<float*>(args.out) + split_base + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(gj, s);
-            if (DUAL) o[args.ldo_up + col] = __fmul_rn(uj, s);
-          } else {
+            o[col] = v0;
+            if (DUAL) o[args.ldo_up + col] = v1;
+          } else {  // kEpiRoutedPlane, kEpiStoreF32
             float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            o[col] = __fmul_rn(gj, s);
-            if (DUAL) o[col1] = __fmul_rn(uj, s);
+            o[col] = v0;
+            if (DUAL) o[col1] = v1;
           }
         }
       };

@@ -107,6 +107,118 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// Router logits for large T (same canonical order as above).  CTA tile: 128
+// tokens x 128 experts x one K chunk (blockIdx.z); 256 threads, each owning 8
+// tokens x 8 experts (experts tx*4.. and 64+tx*4..).  K advances in 32-wide
+// slabs staged in shared memory as fp32 (tokens as duplicated pairs, so that
+// one fma.rn.f32x2 applies one x to two experts), double-buffered with the
+// next slab's global loads in flight.  fma.rn.f32x2 is two independent
+// correctly rounded fmas, so every output is still one ascending fma chain.
+constexpr uint32_t kRtSlab = 32;
+constexpr uint32_t kRtXPitch = 128 * 2 + 8;  // floats per k row of token pairs
+constexpr uint32_t kRtWPitch = 128 + 4;      // floats per k row of experts
+constexpr uint32_t kRtBufFloats = kRtSlab * (kRtXPitch + kRtWPitch);
+constexpr uint32_t kRouterTiledMinTokens = 256;
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+__global__ void __launch_bounds__(256, 2) router_logits_tiled_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
+    uint32_t T, uint32_t H, uint32_t E, uint32_t* __restrict__ bitmap, uint32_t bitmap_words) {
+  extern __shared__ __align__(16) float rtsm[];
+  const uint32_t tid = threadIdx.x;
+  const uint32_t e0 = blockIdx.x * 128, t0 = blockIdx.y * 128, c = blockIdx.z;
+  const uint32_t chunk = H / 8;
+  {
+    const uint64_t lin = (uint64_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    const uint64_t nthreads = uint64_t(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
+    for (uint64_t i = lin * blockDim.x + tid; i < bitmap_words; i += nthreads) bitmap[i] = 0;
+  }
+  // staging: per slab and operand 128 rows x 64 bytes = 512 pieces of 16 bytes, 2 per thread
+  uint4 rx[2], rw[2];
+  auto gload = [&](uint32_t k0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t p = tid + 256u * i, row = p >> 2, part = p & 3;
+      const uint64_t col = uint64_t(c) * chunk + k0 + part * 8;
+      rx[i] = t0 + row < T ? *reinterpret_cast<const uint4*>(x + uint64_t(t0 + row) * H + col)
+                           : make_uint4(0, 0, 0, 0);
+      rw[i] = e0 + row < E ? *reinterpret_cast<const uint4*>(w + uint64_t(e0 + row) * H + col)
+                           : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto sstore = [&](float* buf) {
+    float* xs2 = buf;
+    float* ws = buf + kRtSlab * kRtXPitch;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint32_t p = tid + 256u * i, row = p >> 2, part = p & 3;
+      const uint32_t xv[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
+      const uint32_t wv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t k = part * 8 + 2 * q;
+        const float xl = __uint_as_float(xv[q] << 16), xh = __uint_as_float(xv[q] & 0xffff0000u);
+        *reinterpret_cast<float2*>(xs2 + k * kRtXPitch + 2 * row) = make_float2(xl, xl);
+        *reinterpret_cast<float2*>(xs2 + (k + 1) * kRtXPitch + 2 * row) = make_float2(xh, xh);
+        ws[k * kRtWPitch + row] = __uint_as_float(wv[q] << 16);
+        ws[(k + 1) * kRtWPitch + row] = __uint_as_float(wv[q] & 0xffff0000u);
+      }
+    }
+  };
+  const uint32_t tx = tid & 15, ty = tid >> 4;
+  uint64_t acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0;
+  const uint32_t nslab = chunk / kRtSlab;
+  gload(0);
+  sstore(rtsm);
+  __syncthreads();
+  for (uint32_t s = 0; s < nslab; ++s) {
+    const float* cur = rtsm + (s & 1) * kRtBufFloats;
+    if (s + 1 < nslab) gload((s + 1) * kRtSlab);
+    const float* xs2 = cur;
+    const float* ws = cur + kRtSlab * kRtXPitch;
+#pragma unroll 4
+    for (uint32_t k = 0; k < kRtSlab; ++k) {
+      const ulonglong2* xp = reinterpret_cast<const ulonglong2*>(xs2 + k * kRtXPitch + ty * 16);
+      const ulonglong2 x01 = xp[0], x23 = xp[1], x45 = xp[2], x67 = xp[3];
+      const uint64_t xi[8] = {x01.x, x01.y, x23.x, x23.y, x45.x, x45.y, x67.x, x67.y};
+      const ulonglong2 wa = *reinterpret_cast<const ulonglong2*>(ws + k * kRtWPitch + tx * 4);
+      const ulonglong2 wb = *reinterpret_cast<const ulonglong2*>(ws + k * kRtWPitch + 64 + tx * 4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i][0] = ffma2(xi[i], wa.x, acc[i][0]);
+        acc[i][1] = ffma2(xi[i], wa.y, acc[i][1]);
+        acc[i][2] = ffma2(xi[i], wb.x, acc[i][2]);
+        acc[i][3] = ffma2(xi[i], wb.y, acc[i][3]);
+      }
+    }
+    if (s + 1 < nslab) sstore(rtsm + ((s + 1) & 1) * kRtBufFloats);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t t = t0 + ty * 8 + i;
+    if (t >= T) continue;
+    float* row = partial + (uint64_t(c) * T + t) * E + e0;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const uint64_t p0 = acc[i][2 * g], p1 = acc[i][2 * g + 1];
+      *reinterpret_cast<float4*>(row + 64 * g + tx * 4) =
+          make_float4(__uint_as_float(uint32_t(p0)), __uint_as_float(uint32_t(p0 >> 32)),
+                      __uint_as_float(uint32_t(p1)), __uint_as_float(uint32_t(p1 >> 32)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Router selection, one warp per token (lane owns experts lane + 32j):
 //   s = sigmoid(logit), choice = s + bias; group score = top1 + top2 of choice;
 //   keep the best `topk_groups` groups; pick `top_k` experts by choice among
@@ -796,6 +908,21 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* pa
                                           static_cast<int>(smem));
     if (st != cudaSuccess) return st;
     configured[dev] = true;
+  }
+  if (T >= kRouterTiledMinTokens && E % 128 == 0) {
+    const size_t tsmem = 2ull * kRtBufFloats * 4;
+    static bool tconfigured[64] = {};
+    if (!tconfigured[dev]) {
+      cudaError_t st = cudaFuncSetAttribute(router_logits_tiled_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            static_cast<int>(tsmem));
+      if (st != cudaSuccess) return st;
+      tconfigured[dev] = true;
+    }
+    dim3 tgrid(E / 128, (T + 127) / 128, 8);
+    router_logits_tiled_kernel<<<tgrid, 256, tsmem, stream>>>(x, w, partial, T, H, E, bitmap,
+                                                             bitmap_words);
+    return cudaPeekAtLastError();
   }
   dim3 grid((E + 31) / 32, (T + 31) / 32, 8);
   router_logits_kernel<<<grid, 256, smem, stream>>>(x, w, partial, T, H, E, bitmap, bitmap_words);
