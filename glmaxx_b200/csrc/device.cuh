@@ -198,6 +198,36 @@ __device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
                : "memory");
 }
 
+// Descriptor of a 128-row x 32-byte block for tcgen05.cp.128x256b: the first
+// 16 bytes of every row in one 2 KB half, the second 16 bytes in the next
+// (leading byte offset 2 KB), 8-row core groups 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf_pair(const void* smem) {
+  return smem_desc_sf(smem) | (uint64_t(2048 >> 4) << 16);
+}
+__device__ __forceinline__ void tc_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+// Asynchronous 16-byte global -> shared copy (L1-allocating), its commit group
+// and the wait for all but the newest N groups.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (TMA, tcgen05.cp) of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(

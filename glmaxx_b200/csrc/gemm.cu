@@ -76,7 +76,7 @@ cudaError_t run(const GemmLaunch& g, int num_sms, cudaStream_t stream) {
   if (st != cudaSuccess) return st;
   st = encode_b(&tb, g.b, g.b_rows, g.b_row_bytes, NT);
   if (st != cudaSuccess) return st;
-  kernel<<<num_sms, 192, smem, stream>>>(ta, tb, g.args);
+  kernel<<<num_sms, GemmShape<FP4, DUAL, NT>::kThreads, smem, stream>>>(ta, tb, g.args);
   return cudaPeekAtLastError();
 }
 
@@ -121,11 +121,13 @@ cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStr
     case kFc2DecodeFp4Store:
       return run<true, false, 32, 8, kEpiStoreF32>(g, num_sms, stream);
     case kFc1PrefillFp4:
-      return run<true, true, 128, 4, kEpiSwiGLU>(g, num_sms, stream);
+      return run<true, true, 128, 3, kEpiSwiGLU>(g, num_sms, stream);
     case kFc2PrefillFp4:
-      return run<true, false, 128, 6, kEpiRoutedAtomic>(g, num_sms, stream);
+      return run<true, false, 128, 4, kEpiRoutedAtomic>(g, num_sms, stream);
     case kFc2PrefillFp4Store:
-      return run<true, false, 128, 6, kEpiStoreF32>(g, num_sms, stream);
+      return run<true, false, 128, 4, kEpiStoreF32>(g, num_sms, stream);
+    case kFc2PrefillFp4Pair:
+      return run<true, true, 128, 3, kEpiRoutedAtomic>(g, num_sms, stream);
     case kShared1Bf16N64:
       return run<false, true, 64, 5, kEpiSwiGLU>(g, num_sms, stream);
     case kShared2Bf16N64:

@@ -96,9 +96,16 @@ struct GemmShape {
                                                       : 512;
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = NT * 128;
-  static constexpr int kSfaBytes = FP4 ? 2048 : 0;
-  static constexpr int kSfbBytes = FP4 ? 2048 * kNJ : 0;
+  // Lane-major scales (128-row N tiles): each operand's scales of a stage are
+  // staged as two 4 KB blocks, one per K-block pair, each [atom kb x4 | atom
+  // kb+1 x4], and reach TMEM with two 128x256b copies instead of four 32x128b
+  // broadcast copies.  A converter warp writes them; the TMA moves A and B only.
+  static constexpr bool kLaneSf = FP4 && NT == 128;
+  static constexpr int kSfaBytes = FP4 ? (kLaneSf ? 8192 : 2048) : 0;
+  static constexpr int kSfbBytes = FP4 ? (kLaneSf ? 8192 : 2048 * kNJ) : 0;
   static constexpr int kStageBytes = kAcc * kABytes + kBBytes + kAcc * kSfaBytes + kSfbBytes;
+  static constexpr int kTxBytes = kLaneSf ? kAcc * kABytes + kBBytes : kStageBytes;
+  static constexpr int kThreads = kLaneSf ? 224 : 192;
   static_assert(kUsedCols <= 512, "TMEM budget");
   static_assert(NT % 32 == 0 && NT <= 128, "tile rows");
   static_assert(kStageBytes % 1024 == 0, "stage alignment");
@@ -106,11 +113,11 @@ struct GemmShape {
 
 template <bool FP4, bool DUAL, int NT, int STAGES>
 constexpr int gemm_smem_bytes() {
-  return GemmShape<FP4, DUAL, NT>::kStageBytes * STAGES + 1024 /* align slack */ + 256;
+  return GemmShape<FP4, DUAL, NT>::kStageBytes * STAGES + 1024 /* align slack */ + 512;
 }
 
 template <bool FP4, bool DUAL, int NT, int STAGES, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
   using S = GemmShape<FP4, DUAL, NT>;
@@ -124,7 +131,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* tfull_bar = bars + 2 * STAGES;
   uint64_t* tempty_bar = bars + 2 * STAGES + 4;
   uint64_t* drain_bar = bars + 2 * STAGES + 8;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 9);
+  uint64_t* sfull_bar = bars + 2 * STAGES + 9;  // lane-major scales written (kLaneSf)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 9);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -134,6 +142,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
+      mbar_init(&sfull_bar[s], 1);
     }
     for (int b = 0; b < S::kAccBufs; ++b) {
       mbar_init(&tfull_bar[b], 1);
@@ -194,7 +203,7 @@ __global__ void __launch_bounds__(192, 1)
     if (args.status) atomicOr(args.status, bit);
   };
 
-  constexpr uint32_t kTx = S::kStageBytes;
+  constexpr uint32_t kTx = S::kTxBytes;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_3d(stage_a(stage, 1), &tmap_a, &full_bar[stage], kx,
                         int32_t(i * m_stride + args.up_row_offset), int32_t(t.expert));
           tma_load_2d(stage_b(stage), &tmap_b, &full_bar[stage], kx, int32_t(t.row_start));
-          if (FP4) {
+          if (FP4 && !S::kLaneSf) {
             bulk_load(stage_sfa(stage, 0),
                       sfa_e + 512ull * (uint64_t(i * m_stride / 128) * args.kblocks + kc * 4), 2048,
                       &full_bar[stage]);
@@ -274,7 +283,8 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t d1 = d0 + NT;
         const uint32_t kc0 = item_kc0(item), kc1 = item_kc1(item);
         for (uint32_t kc = kc0; kc < kc1; ++kc) {
-          if (!mbar_wait(&full_bar[stage], phase, s_abort)) {
+          if (!mbar_wait(&full_bar[stage], phase, s_abort) ||
+              (S::kLaneSf && !mbar_wait(&sfull_bar[stage], phase, s_abort))) {
             fail(kStatusWaitTimeout);
             ok = false;
             break;
@@ -284,7 +294,16 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t sfa_t0 = sf_base, sfa_t1 = sf_base + 16;
           const uint32_t sfb_t = sf_base + S::kAcc * 16;
           sf_set ^= 1u;
-          if (FP4) {
+          if (S::kLaneSf) {
+            // one 128x256b copy per operand and K-block pair (8 TMEM columns)
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+              tc_cp_sf_pair(sfa_t0 + pr * 8, smem_desc_sf_pair(stage_sfa(stage, 0) + pr * 4096));
+              if (DUAL)
+                tc_cp_sf_pair(sfa_t1 + pr * 8, smem_desc_sf_pair(stage_sfa(stage, 1) + pr * 4096));
+              tc_cp_sf_pair(sfb_t + pr * 8, smem_desc_sf_pair(stage_sfb(stage) + pr * 4096));
+            }
+          } else if (FP4) {
 #pragma unroll
             for (int kb = 0; kb < 4; ++kb) {
               tc_cp_sf(sfa_t0 + kb * 4, smem_desc_sf(stage_sfa(stage, 0) + kb * 512));
@@ -329,6 +348,69 @@ __global__ void __launch_bounds__(192, 1)
       // Drain all tensor-core work issued by this thread before TMEM is freed.
       tc_commit(drain_bar);
       if (!mbar_wait(drain_bar, 0, nullptr)) fail(kStatusTmemTimeout);
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------- scale converter
+    // (kLaneSf only) Copies each stage's scale atoms (4 K-blocks x 512 bytes per
+    // operand) from global memory four times over into the stage's lane-major
+    // blocks -- lane row 32q + r of a 128x256b copy must hold atom row r, whose
+    // word q is the scale word of row 32q + r -- with asynchronous 16-byte
+    // copies, kConvDepth stages in flight; a stage is published (sfull) once
+    // its copies have landed.
+    if constexpr (S::kLaneSf) {
+      constexpr int kConvDepth = 1;
+      constexpr int kOps = S::kAcc + 1;
+      uint32_t stage = 0, phase = 0, pending = 0;
+      bool ok = true;
+      auto publish_oldest = [&]() {
+        fence_proxy_async_smem();
+        __syncwarp();
+        const uint32_t s_old = (stage + STAGES - pending) % STAGES;
+        if (lane == 0) mbar_arrive(&sfull_bar[s_old]);
+        --pending;
+      };
+      for (uint32_t item = blockIdx.x; ok && item < items; item += gridDim.x) {
+        const uint32_t i = item_i(item);
+        const NTile t = tile_of(item_q(item));
+        const uint8_t* sfa_e = args.sfa + uint64_t(t.expert) * args.sfa_expert_bytes;
+        const uint64_t a0_atom = uint64_t(i * m_stride / 128) * args.kblocks;
+        const uint64_t a1_atom = uint64_t((i * m_stride + args.up_row_offset) / 128) * args.kblocks;
+        const uint64_t b_atom = uint64_t(t.sf_row_start / 128) * args.kblocks;
+        const uint32_t kc1 = item_kc1(item);
+        for (uint32_t kc = item_kc0(item); kc < kc1; ++kc) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, s_abort)) {
+            fail(kStatusWaitTimeout);
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int o = 0; o < kOps; ++o) {
+            const uint8_t* src = (o == kOps - 1)
+                                     ? args.sfb + 512ull * (b_atom + kc * 4)
+                                     : sfa_e + 512ull * ((o == 0 ? a0_atom : a1_atom) + kc * 4);
+            uint8_t* dst = (o == kOps - 1) ? stage_sfb(stage) : stage_sfa(stage, o);
+#pragma unroll
+            for (int kb = 0; kb < 4; ++kb) {
+              const uint8_t* g = src + 512 * kb + 16 * lane;
+              uint8_t* blk = dst + 4096 * (kb / 2) + 2048 * (kb % 2) + 16 * lane;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) cp_async_16(blk + 512 * q, g);
+            }
+          }
+          cp_async_commit();
+          ++pending;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (pending > static_cast<uint32_t>(kConvDepth)) {
+            cp_async_wait<kConvDepth>();
+            publish_oldest();
+          }
+        }
+      }
+      cp_async_wait<0>();
+      while (ok && pending > 0) publish_oldest();
     }
   } else {
     // ------------------------------------------------------------ epilogue

@@ -392,10 +392,11 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     GemmArgs& a = g.args;
     a.tiles = tiles;
     a.tile_count = tile_count;
-    // decode: two adjacent 128-row M tiles per item (shared B tile)
-    a.m_tiles = p.decode ? p.H / 256 : p.H / 128;
-    a.m_stride = p.decode ? 256 : 128;
-    a.up_row_offset = p.decode ? 128 : 0;
+    // two adjacent 128-row M tiles per item share one B tile (twice the weight
+    // bytes per pipeline stage, half the B-tile and scale-copy work per FLOP)
+    a.m_tiles = p.H / 256;
+    a.m_stride = 256;
+    a.up_row_offset = 128;
     a.k_chunks = p.I / 256;
     a.kblocks = p.I / 64;
     a.ldo = p.H;
@@ -410,7 +411,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     a.row_slot = q.row_slot;
     a.row_weight = q.row_weight;
     a.status = status;
-    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair : kFc2PrefillFp4, g, info.sms, stream));
+    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair : kFc2PrefillFp4Pair, g, info.sms, stream));
   }
   // 8. deterministic combine (decode): ascending-expert sum + shared
   CHECK(mark(kStageCombine, stream));
