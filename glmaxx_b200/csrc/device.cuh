@@ -222,6 +222,13 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// Four independent float atomic adds to 16 consecutive bytes (one vector
+// reduction instruction).
+__device__ __forceinline__ void red_add_v4(float* p, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (TMA, tcgen05.cp) of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -59,9 +59,9 @@ cudaError_t encode_b(CUtensorMap* m, const void* base, uint32_t rows, uint32_t r
 
 template <bool FP4, bool DUAL, int NT, int STAGES, int EPI>
 cudaError_t run(const GemmLaunch& g, int num_sms, cudaStream_t stream) {
-  static_assert(gemm_smem_bytes<FP4, DUAL, NT, STAGES>() <= 227 * 1024, "smem budget");
+  static_assert(gemm_smem_bytes<FP4, DUAL, NT, STAGES, EPI>() <= 227 * 1024, "smem budget");
   auto kernel = grouped_gemm_kernel<FP4, DUAL, NT, STAGES, EPI>;
-  constexpr int smem = gemm_smem_bytes<FP4, DUAL, NT, STAGES>();
+  constexpr int smem = gemm_smem_bytes<FP4, DUAL, NT, STAGES, EPI>();
   static bool configured[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;

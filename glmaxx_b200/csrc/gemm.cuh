@@ -111,9 +111,21 @@ struct GemmShape {
   static_assert(kStageBytes % 1024 == 0, "stage alignment");
 };
 
-template <bool FP4, bool DUAL, int NT, int STAGES>
+// Per-warp transpose tile of the N=128 epilogues: 16 tokens x 32 columns, rows
+// padded so that the 16-byte row reads of 8 lanes hit distinct banks.
+template <bool FP4, bool DUAL, int NT, int EPI>
+struct EpiTile {
+  static constexpr bool kOn = GemmShape<FP4, DUAL, NT>::kLaneSf && EPI != kEpiStorePartial;
+  static constexpr bool kBf16 = EPI == kEpiSwiGLU;
+  static constexpr int kPitch = kBf16 ? 80 : 144;
+  static constexpr int kWarpBytes = kOn ? 16 * kPitch : 0;
+  static constexpr int kBytes = 4 * kWarpBytes;
+};
+
+template <bool FP4, bool DUAL, int NT, int STAGES, int EPI>
 constexpr int gemm_smem_bytes() {
-  return GemmShape<FP4, DUAL, NT>::kStageBytes * STAGES + 1024 /* align slack */ + 512;
+  return GemmShape<FP4, DUAL, NT>::kStageBytes * STAGES + 1024 /* align slack */ + 512 +
+         EpiTile<FP4, DUAL, NT, EPI>::kBytes;
 }
 
 template <bool FP4, bool DUAL, int NT, int STAGES, int EPI>
@@ -133,6 +145,8 @@ __global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
   uint64_t* drain_bar = bars + 2 * STAGES + 8;
   uint64_t* sfull_bar = bars + 2 * STAGES + 9;  // lane-major scales written (kLaneSf)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 9);
+  using ET = EpiTile<FP4, DUAL, NT, EPI>;
+  uint8_t* epi_smem = smem + S::kStageBytes * STAGES + 512;  // after the barrier block
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -490,27 +504,74 @@ __global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
             if (DUAL) u[j] = __float_as_uint(uj);
           }
         }
+        if constexpr (ET::kOn) {
+          // Transposed stores: 16 tokens at a time go through this warp's tile, then
+          // each lane writes 16-byte pieces of one token row (h rows or output rows).
+          uint8_t* tb = epi_smem + quarter * ET::kWarpBytes;
+          constexpr int kPasses = (DUAL && !ET::kBf16) ? 2 : 1;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
-          if (ch * 32 + j >= t.rows) continue;
-          const float v0 = __uint_as_float(g[j]);
-          const float v1 = __uint_as_float(u[j]);
-          if (EPI == kEpiSwiGLU) {
-            reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(rd) * args.ldo + col] =
-                __float2bfloat16_rn(v0);
-          } else if (EPI == kEpiRoutedAtomic) {
-            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            atomicAdd(o + col, v0);
-            if (DUAL) atomicAdd(o + col1, v1);
-          } else if (EPI == kEpiStorePartial) {
-            float* o = reinterpret_cast<float*>(args.out) + split_base + uint64_t(rd) * args.ldo;
-            o[col] = v0;
-            if (DUAL) o[args.ldo_up + col] = v1;
-          } else {  // kEpiRoutedPlane, kEpiStoreF32
-            float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
-            o[col] = v0;
-            if (DUAL) o[col1] = v1;
+          for (int pass = 0; pass < kPasses; ++pass) {
+            const uint32_t colbase = (pass ? col1 : col) - lane;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              __syncwarp();
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const uint32_t v = pass ? u[16 * hf + jj] : g[16 * hf + jj];
+                if (ET::kBf16)
+                  *reinterpret_cast<uint16_t*>(tb + jj * ET::kPitch + 2 * lane) =
+                      __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v)));
+                else
+                  *reinterpret_cast<uint32_t*>(tb + jj * ET::kPitch + 4 * lane) = v;
+              }
+              __syncwarp();
+              const uint32_t jj = lane & 15, half = lane >> 4;
+              const uint32_t rd = __shfl_sync(0xffffffffu, src_d, 16 * hf + jj);
+              if (ch * 32 + 16 * hf + jj < t.rows) {
+                const uint8_t* rowp = tb + jj * ET::kPitch;
+                if (ET::kBf16) {
+                  uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) +
+                                                      uint64_t(rd) * args.ldo + colbase + half * 16);
+                  o[0] = *reinterpret_cast<const uint4*>(rowp + half * 32);
+                  o[1] = *reinterpret_cast<const uint4*>(rowp + half * 32 + 16);
+                } else {
+                  float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo + colbase +
+                             half * 16;
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float4 f = *reinterpret_cast<const float4*>(rowp + half * 64 + 16 * q);
+                    if (EPI == kEpiRoutedAtomic)
+                      red_add_v4(o + 4 * q, f);
+                    else
+                      *reinterpret_cast<float4*>(o + 4 * q) = f;
+                  }
+                }
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
+            if (ch * 32 + j >= t.rows) continue;
+            const float v0 = __uint_as_float(g[j]);
+            const float v1 = __uint_as_float(u[j]);
+            if (EPI == kEpiSwiGLU) {
+              reinterpret_cast<__nv_bfloat16*>(args.out)[uint64_t(rd) * args.ldo + col] =
+                  __float2bfloat16_rn(v0);
+            } else if (EPI == kEpiRoutedAtomic) {
+              float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
+              atomicAdd(o + col, v0);
+              if (DUAL) atomicAdd(o + col1, v1);
+            } else if (EPI == kEpiStorePartial) {
+              float* o = reinterpret_cast<float*>(args.out) + split_base + uint64_t(rd) * args.ldo;
+              o[col] = v0;
+              if (DUAL) o[args.ldo_up + col] = v1;
+            } else {  // kEpiRoutedPlane, kEpiStoreF32
+              float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo;
+              o[col] = v0;
+              if (DUAL) o[col1] = v1;
+            }
           }
         }
       };
