@@ -156,6 +156,7 @@ SIGNATURES = {
     "glmaxx_nvfp4_fc2_dense_control_launch": (ctypes.c_int32, [_P, u32, _P, _I32P]),
     "glmaxx_nvfp4_fc2_grouped_control_launch": (ctypes.c_int32, [_P, _U16P, u32, _P, _I32P]),
     "glmaxx_exl3_projection_launch": (ctypes.c_int32, [_P, _P, _I32P]),
+    "glmaxx_exl3_gemv_launch": (ctypes.c_int32, [u64, u64, u32, u32, u32, u32, u64, _P]),
     "glmaxx_graph_exec_launch": (ctypes.c_int32, [u64, u64]),
     "glmaxx_graph_exec_destroy": (ctypes.c_int32, [u64]),
     "glmaxx_event_create": (ctypes.c_int32, [_U64P]),

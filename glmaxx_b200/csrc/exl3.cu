@@ -22,30 +22,6 @@ namespace {
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
-__device__ __forceinline__ uint16_t decode_3inst(uint32_t window) {
-  const uint32_t value = window * 0xCBAC1FEDu;
-  const uint32_t packed = (value & 0x8FFF8FFFu) ^ 0x3B603B60u;
-  return f2h(__fadd_rn(h2f(uint16_t(packed)), h2f(uint16_t(packed >> 16))));
-}
-
-__device__ __forceinline__ uint16_t decode_at(const uint16_t* __restrict__ trellis, uint32_t n,
-                                              uint32_t bits, uint32_t row, uint32_t col) {
-  const uint32_t tile_halves = 16 * bits, tile_words = 8 * bits;
-  const uint64_t tile = uint64_t(row / 16) * (n / 16) + col / 16;
-  const uint16_t* base = trellis + tile * tile_halves;
-  const uint32_t lr = row & 15, lc = col & 15;
-  const uint32_t lane = ((lc >> 1) & 3) * 8 + (lc & 1) * 4 + ((lr & 7) >> 1);
-  const uint32_t weight = (lc >= 8 ? 4 : 0) + (lr >= 8 ? 2 : 0) + (lr & 1);
-  const uint32_t end_bit = (lane * 8 + weight + 257) * bits;
-  const uint32_t first = (end_bit - 16) / 32, last = (end_bit - 1) / 32;
-  const uint32_t shift = (last + 1) * 32 - end_bit;
-  auto word = [&](uint32_t i) {
-    const uint32_t h = (i % tile_words) * 2;
-    return uint32_t(base[h]) | (uint32_t(base[h + 1]) << 16);
-  };
-  const uint64_t merged = (uint64_t(word(first)) << 32) | word(last);
-  return decode_3inst(uint32_t((merged >> shift) & 0xffff));
-}
 
 // H128 of one 128-block held in shared memory, as exl3.rs:515-531: each output
 // is the ascending-column sum of +-input, times 1/sqrt(128).
@@ -70,16 +46,161 @@ __global__ void exl3_rotate_in(const uint16_t* __restrict__ x, const uint16_t* _
   rotated[idx] = f2h(hadamard_row(blk, i, norm));
 }
 
-// grid (N/128, rows), 128 threads: one output column per thread, ascending k.
-__global__ void exl3_project(const uint16_t* __restrict__ rotated,
-                             const uint16_t* __restrict__ trellis, uint16_t* __restrict__ projected,
-                             uint32_t K, uint32_t N, uint32_t bits) {
-  const uint32_t r = blockIdx.y, col = blockIdx.x * 128 + threadIdx.x;
-  const uint16_t* src = rotated + uint64_t(r) * K;
-  float acc = 0.f;
-  for (uint32_t k = 0; k < K; ++k)
-    acc = __fadd_rn(acc, __fmul_rn(h2f(src[k]), h2f(decode_at(trellis, N, bits, k, col))));
-  projected[uint64_t(r) * N + col] = f2h(acc);
+// ---------------------------------------------------------------------------
+// Decode-fused EXL3 GEMV/GEMM: P[row][n] = f16( sum_k x[row][k] * W[k][n] ) with
+// the reference's arithmetic (exl3.rs:404-453: fp32, multiply then add, k
+// ascending from 0, one chain per output), so results are bit-identical to
+// the CPU definition.  One warp owns 32 output columns (two 16x16 trellis tile
+// columns); every 16 k it decodes its two tiles cooperatively -- lane l holds
+// weights l*8 .. l*8+7 of a tile's 256-weight circular bitstream, the 4x2
+// block (k, n) = (2(l&3) + (w&1) + 8((w>>1)&1), 2((l>>3)&3) + ((l>>2)&1) +
+// 8((w>>2)&1)) -- transposes them through shared memory, and each lane then
+// extends the chains of its column for RB rows.  Work items are (group = one
+// weight matrix, block of RB rows of that group).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kExl3Bits = 3;
+constexpr uint32_t kExl3TileHalves = 16 * kExl3Bits;  // 48 halves = 24 words per 16x16 tile
+constexpr uint32_t kExl3KChunk = 256;                  // x staged per 256 k
+
+// Bit position (MSB-first stream order) of lane `lane`'s first window inside
+// the tile's 768-bit circular stream: weight i of the tile uses the 16 bits
+// ending at bit (i + 257) * 3 (exl3.rs:490-513), and lane l owns i = 8l .. 8l+7,
+// so its 8 windows lie in 37 consecutive bits starting at (8l + 257) * 3 - 16.
+struct Exl3LaneWindow {
+  uint32_t word0;  // first 32-bit word (mod 24) holding the span
+  uint32_t off;    // bit offset of the span inside that word (0 = MSB)
+};
+__device__ __forceinline__ Exl3LaneWindow exl3_lane_window(uint32_t lane) {
+  const uint32_t start = (lane * 8 + 257) * kExl3Bits - 16;
+  return {start / 32, start % 32};
+}
+
+// The three words of a tile that hold lane's span (halves base[0..47] are
+// words (h0 | h1 << 16), the stream wraps after 24 words).
+__device__ __forceinline__ void exl3_load_span(const uint16_t* __restrict__ base,
+                                               Exl3LaneWindow lw, uint32_t (&wd)[3]) {
+  constexpr uint32_t kTileWords = 8 * kExl3Bits;
+  const uint32_t* base32 = reinterpret_cast<const uint32_t*>(base);
+#pragma unroll
+  for (int j = 0; j < 3; ++j) wd[j] = __ldg(base32 + (lw.word0 + j) % kTileWords);
+}
+
+// 3INST decode of the 8 windows in the span: value = window * 0xCBAC1FED,
+// (value & 0x8FFF8FFF) ^ 0x3B603B60 read as two fp16 halves, summed.  Both halves
+// have exponent fields 12..15, so their exact sum fits fp32 and the fp16 add
+// rounds it once, exactly as fp16(f32(lo) + f32(hi)) of the reference.
+__device__ __forceinline__ void exl3_decode_span(const uint32_t (&wd)[3], uint32_t off,
+                                                 uint16_t (&w16)[8]) {
+  const uint64_t v = (uint64_t(wd[0]) << 32) | wd[1];
+  const uint64_t span = off ? ((v << off) | (wd[2] >> (32 - off))) : v;  // bit 63 = span start
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint32_t window = uint32_t(span >> (48 - 3 * w)) & 0xffffu;
+    const uint32_t packed = ((window * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    const __half2 h = *reinterpret_cast<const __half2*>(&packed);
+    w16[w] = __half_as_ushort(__hadd(__low2half(h), __high2half(h)));
+  }
+}
+
+struct Exl3GemvArgs {
+  const uint16_t* x;             // [rows][K] f16, row r of group g at x + r*K
+  const uint16_t* trellis;       // group g's trellis at trellis + g * trellis_stride (halves)
+  uint64_t trellis_stride;
+  const uint32_t* group_rows;    // [groups + 1] row offsets (exclusive prefix), or null:
+                                 // one group of implicit_rows rows
+  const uint32_t* items;         // [n_items] (group << 16 | row block), device list
+  const uint32_t* n_items;       // device count of items
+  uint32_t implicit_rows;
+  uint16_t* out;                 // [rows][N] f16
+  uint32_t K, N;
+};
+
+template <int RB>
+__global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
+  __shared__ __align__(16) uint16_t ws[16][32 + 2];      // decoded 16 k x 32 columns
+  __shared__ __align__(16) float xs[RB][kExl3KChunk];    // x of this item's rows
+  const uint32_t lane = threadIdx.x;
+  const Exl3LaneWindow lw = exl3_lane_window(lane);
+  const uint32_t c0 = blockIdx.x * 32;                   // first column of this warp
+  const uint32_t nt0 = c0 / 16;                          // first tile column
+  const bool listed = a.group_rows != nullptr;
+  const uint32_t count = listed ? *a.n_items : (a.implicit_rows + RB - 1) / RB;
+  for (uint32_t it = blockIdx.y; it < count; it += gridDim.y) {
+    const uint32_t item = listed ? a.items[it] : it;
+    const uint32_t g = listed ? item >> 16 : 0, blk = listed ? item & 0xffff : item;
+    const uint32_t r0 = (listed ? a.group_rows[g] : 0) + blk * RB;
+    const uint32_t rend = listed ? a.group_rows[g + 1] : a.implicit_rows;
+    const uint32_t nr = min(uint32_t(RB), rend - r0);
+    const uint16_t* tr = a.trellis + uint64_t(g) * a.trellis_stride;
+    float acc[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) acc[r] = 0.f;
+    for (uint32_t kc = 0; kc < a.K; kc += kExl3KChunk) {
+      const uint32_t kn = min(kExl3KChunk, a.K - kc);  // a multiple of 16
+      __syncwarp();
+      for (uint32_t i = lane; i < RB * kExl3KChunk; i += 32) {
+        const uint32_t r = i / kExl3KChunk, k = i % kExl3KChunk;
+        xs[r][k] = (r < nr && k < kn) ? h2f(a.x[uint64_t(r0 + r) * a.K + kc + k]) : 0.f;
+      }
+      __syncwarp();
+      uint32_t span[2][3];
+      auto tile_ptr = [&](uint32_t k, int j) {
+        return tr + (uint64_t(k / 16) * (a.N / 16) + nt0 + j) * kExl3TileHalves;
+      };
+      exl3_load_span(tile_ptr(kc, 0), lw, span[0]);
+      exl3_load_span(tile_ptr(kc, 1), lw, span[1]);
+      for (uint32_t k16 = 0; k16 < kn; k16 += 16) {
+        uint16_t w16[2][8];
+        exl3_decode_span(span[0], lw.off, w16[0]);
+        exl3_decode_span(span[1], lw.off, w16[1]);
+        if (k16 + 16 < kn) {  // next step's words are in flight during this step
+          exl3_load_span(tile_ptr(kc + k16 + 16, 0), lw, span[0]);
+          exl3_load_span(tile_ptr(kc + k16 + 16, 1), lw, span[1]);
+        }
+        const uint32_t lcb = 2 * ((lane >> 3) & 3) + ((lane >> 2) & 1);
+        const uint32_t lrb = 2 * (lane & 3);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t lr = lrb + (w & 1) + 8 * ((w >> 1) & 1);
+            const uint32_t lc = lcb + 8 * ((w >> 2) & 1);
+            ws[lr][16 * j + lc] = w16[j][w];
+          }
+        __syncwarp();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const float wf = h2f(ws[kk][lane]);
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(xs[r][k16 + kk], wf));
+        }
+        __syncwarp();
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+      if (r < static_cast<int>(nr)) a.out[uint64_t(r0 + r) * a.N + c0 + lane] = f2h(acc[r]);
+  }
+}
+
+// Work list: one item per (group, block of rb rows) with rows; single CTA.
+__global__ void exl3_items_kernel(const uint32_t* __restrict__ group_rows, uint32_t groups,
+                                  uint32_t rb, uint32_t* __restrict__ items,
+                                  uint32_t* __restrict__ n_items) {
+  __shared__ uint32_t base;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  for (uint32_t g0 = 0; g0 < groups; g0 += blockDim.x) {
+    const uint32_t g = g0 + threadIdx.x;
+    const uint32_t rows = g < groups ? group_rows[g + 1] - group_rows[g] : 0;
+    const uint32_t nb = (rows + rb - 1) / rb;
+    // block-wide exclusive scan of nb (small: sequential warps via atomics keeps order free)
+    const uint32_t off = nb ? atomicAdd(&base, nb) : 0;
+    for (uint32_t b = 0; b < nb; ++b) items[off + b] = (g << 16) | b;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_items = base;
 }
 
 // grid (N/128, rows), 128 threads
@@ -94,6 +215,60 @@ __global__ void exl3_rotate_out(const uint16_t* __restrict__ projected,
   const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
   out[idx] = f2h(__fmul_rn(hadamard_row(blk, i, norm), h2f(svh[b * 128 + i])));
 }
+
+// Rows per work item of the grouped launch (decode batches put 1-2 rows on most
+// experts; more rows make more items, each decoding the matrix again).
+constexpr int kExl3GroupRowBlock = 2;
+
+}  // namespace
+
+template <int RB>
+cudaError_t run_exl3_gemv(const Exl3GemvArgs& a, uint32_t max_items, cudaStream_t stream) {
+  dim3 grid(a.N / 32, max_items < 4096 ? max_items : 4096);
+  exl3_gemv_kernel<RB><<<grid, 32, 0, stream>>>(a);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_exl3_gemv_single(const uint16_t* x, const uint16_t* trellis, uint32_t rows,
+                                    uint32_t K, uint32_t N, uint16_t* out, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  if (K % 16 || N % 32) return cudaErrorInvalidValue;
+  Exl3GemvArgs a{};
+  a.x = x;
+  a.trellis = trellis;
+  a.out = out;
+  a.K = K;
+  a.N = N;
+  a.implicit_rows = rows;
+  // rows per item: the FMA work of a block is RB chains per decoded weight
+  if (rows == 1) return run_exl3_gemv<1>(a, 1, stream);
+  if (rows == 2) return run_exl3_gemv<2>(a, 1, stream);
+  if (rows <= 4) return run_exl3_gemv<4>(a, 1, stream);
+  return run_exl3_gemv<8>(a, (rows + 7) / 8, stream);
+}
+
+cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
+                                     uint64_t trellis_stride, const uint32_t* group_rows,
+                                     uint32_t groups, uint32_t max_items, uint32_t* items,
+                                     uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
+                                     cudaStream_t stream) {
+  if (K % 16 || N % 32 || groups >= 65536) return cudaErrorInvalidValue;
+  exl3_items_kernel<<<1, 256, 0, stream>>>(group_rows, groups, kExl3GroupRowBlock, items,
+                                           n_items);
+  Exl3GemvArgs a{};
+  a.x = x;
+  a.trellis = trellis;
+  a.trellis_stride = trellis_stride;
+  a.group_rows = group_rows;
+  a.items = items;
+  a.n_items = n_items;
+  a.out = out;
+  a.K = K;
+  a.N = N;
+  return run_exl3_gemv<kExl3GroupRowBlock>(a, max_items, stream);
+}
+
+namespace {
 
 bool valid_exl3(const glmaxx_exl3_descriptor& d) {
   if (d.abi_version != GLMAXX_EXL3_ABI_VERSION || d.struct_bytes != sizeof(d) || d.flags) return false;
@@ -128,12 +303,30 @@ extern "C" int32_t glmaxx_exl3_projection_launch(const glmaxx_exl3_descriptor* d
   exl3_rotate_in<<<dim3(d.logical_k / 128, d.rows), 128, 0, s>>>(
       reinterpret_cast<const uint16_t*>(d.input_f16), reinterpret_cast<const uint16_t*>(d.suh_f16),
       reinterpret_cast<uint16_t*>(d.rotated_input_f16), d.logical_k);
-  exl3_project<<<dim3(d.logical_n / 128, d.rows), 128, 0, s>>>(
-      reinterpret_cast<const uint16_t*>(d.rotated_input_f16),
-      reinterpret_cast<const uint16_t*>(d.trellis_u16),
-      reinterpret_cast<uint16_t*>(d.projected_f16), d.logical_k, d.logical_n, d.bits);
+  st = launch_exl3_gemv_single(reinterpret_cast<const uint16_t*>(d.rotated_input_f16),
+                               reinterpret_cast<const uint16_t*>(d.trellis_u16), d.rows,
+                               d.logical_k, d.logical_n, reinterpret_cast<uint16_t*>(d.projected_f16),
+                               s);
+  if (st != cudaSuccess) return int32_t(st);
   exl3_rotate_out<<<dim3(d.logical_n / 128, d.rows), 128, 0, s>>>(
       reinterpret_cast<const uint16_t*>(d.projected_f16), reinterpret_cast<const uint16_t*>(d.svh_f16),
       reinterpret_cast<uint16_t*>(d.output_f16), d.logical_n);
   return int32_t(cudaPeekAtLastError());
+}
+
+extern "C" int32_t glmaxx_exl3_gemv_launch(uint64_t input_f16, uint64_t trellis_u16, uint32_t rows,
+                                           uint32_t logical_k, uint32_t logical_n, uint32_t bits,
+                                           uint64_t output_f16, void* cuda_stream) {
+  using namespace glmaxx;
+  if (!input_f16 || !trellis_u16 || !output_f16 || cuda_stream == nullptr) return GLMAXX_ERR_NULL;
+  if (bits != 3 || rows == 0 || logical_k == 0 || logical_n == 0 || logical_k % 16 ||
+      logical_n % 32)
+    return GLMAXX_ERR_DESCRIPTOR;
+  DeviceInfo info;
+  const int32_t arch = current_device_info(&info);
+  if (arch != 0) return arch;
+  return int32_t(launch_exl3_gemv_single(
+      reinterpret_cast<const uint16_t*>(input_f16), reinterpret_cast<const uint16_t*>(trellis_u16),
+      rows, logical_k, logical_n, reinterpret_cast<uint16_t*>(output_f16),
+      reinterpret_cast<cudaStream_t>(cuda_stream)));
 }

@@ -40,4 +40,14 @@ uint64_t router_workspace_bytes(uint32_t tokens, uint32_t experts, uint32_t top_
 int32_t router_compact_launch(const glmaxx_router_descriptor* desc, void* stream,
                               int32_t* async_err);
 
+// EXL3 decode-fused projection (exl3.cu): P = f16(x . W) in the reference's
+// order; single matrix over `rows` rows, or groups of rows (one trellis each).
+cudaError_t launch_exl3_gemv_single(const uint16_t* x, const uint16_t* trellis, uint32_t rows,
+                                    uint32_t K, uint32_t N, uint16_t* out, cudaStream_t stream);
+cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
+                                     uint64_t trellis_stride, const uint32_t* group_rows,
+                                     uint32_t groups, uint32_t max_items, uint32_t* items,
+                                     uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
+                                     cudaStream_t stream);
+
 }  // namespace glmaxx

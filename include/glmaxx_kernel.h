@@ -385,6 +385,18 @@ uint64_t glmaxx_router_workspace_bytes(uint32_t tokens, uint32_t hidden, uint32_
                                        uint32_t top_k);
 uint64_t glmaxx_moe_layer_workspace_bytes(const struct glmaxx_moe_layer_descriptor* descriptor);
 
+/* EXL3 decode-fused projection alone (the core of glmaxx_exl3_projection_launch
+ * without the suh/H128 input and H128/svh output rotations): output[r][n] =
+ * f16(sum_k input[r][k] * W[k][n]) over the 3-bit trellis W (exl3.rs layout,
+ * K x N logical), fp32 multiply-then-add in ascending k exactly as
+ * Exl3Trellis::matmul_reference_f16 (crates/glm-format/src/exl3.rs:404-453)
+ * and the reference's warp-staging proof (warp_proof.rs:378-381).  k % 16 == 0,
+ * n % 32 == 0, bits == 3.  Returns 0, GLMAXX_ERR_NULL, GLMAXX_ERR_DESCRIPTOR, an
+ * arch error, or a cudaError_t. */
+int32_t glmaxx_exl3_gemv_launch(uint64_t input_f16, uint64_t trellis_u16, uint32_t rows,
+                                uint32_t logical_k, uint32_t logical_n, uint32_t bits,
+                                uint64_t output_f16, void* cuda_stream);
+
 int32_t glmaxx_router_compact_launch(const struct glmaxx_router_descriptor* descriptor,
                                      void* cuda_stream, int32_t* asynchronous_error);
 

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from exl3_util import warp_activations
 
 
 def test_actual_shape_packed_sha256(golden):
@@ -74,16 +75,6 @@ def test_exl3_native_decode_digest(golden):
     assert O.u16_hash(O.exl3_reconstruct_native(tr, g["k"], g["n"], g["bits"])) == g["sha256"]
 
 
-def _warp_activations(rows: int, k: int) -> np.ndarray:
-    """warp_proof.rs:364-376"""
-    out = np.zeros((rows, k), np.float32)
-    for r in range(rows):
-        ints = ((r * 1009 + np.arange(k) * 7919 + 17) % 1021).astype(np.int64) - 510
-        vals = (ints.astype(np.float32) / np.float32(4096.0))
-        out[r] = [O.f16_bits_to_f32(O.f32_to_f16_bits(float(v))) for v in vals]
-    return out
-
-
 @pytest.mark.parametrize("index", [0, 1])
 def test_exl3_warp_proof_hashes(golden, index):
     g = golden["exl3_warp_proof"]["shapes"][index]
@@ -97,7 +88,7 @@ def test_exl3_warp_proof_hashes(golden, index):
     assert wh.hexdigest() == g["weight_sha256"]
     wf = O.bf16_bits_to_f32(np.zeros(1, np.uint16))  # dtype helper warm-up
     wf = np.array([O.f16_bits_to_f32(int(b)) for b in range(65536)], np.float32)[native]
-    act = _warp_activations(golden["exl3_warp_proof"]["rows"], k)
+    act = warp_activations(golden["exl3_warp_proof"]["rows"], k)
     acc = np.zeros((act.shape[0], n), np.float32)
     for kk in range(k):  # multiply_then_add, ascending k (warp_proof.rs:378-381)
         acc = acc + act[:, kk:kk + 1] * wf[kk:kk + 1, :]
