@@ -17,17 +17,19 @@ LIB_PATH = _PKG / "libglmaxx_sm100.so"
 FC1_ABI_VERSION = 1
 FC2_ABI_VERSION = 1
 EXL3_ABI_VERSION = 1
+MOE_EXL3_ABI_VERSION = 1
 ROUTER_ABI_VERSION = 3
 MOE_LAYER_ABI_VERSION = 3
 DECODE_PERSISTENT = 1
 PREFILL_GROUPED = 2
 EXL3_GATE, EXL3_UP, EXL3_DOWN = 1, 2, 3
 PLANES = {"fc1_output_bf16": 0, "row_token_u32": 1, "row_slot_u32": 2, "row_weight_f32": 3,
-          "expert_offsets_u32": 4, "shared_f32": 5}
+          "expert_offsets_u32": 4, "shared_f32": 5, "routed_f32": 6}
 LAYER_STAGES = ["router", "compact", "quant", "fc1", "fc2_quant", "shared", "fc2", "combine"]
 ROUTER_STATIC_SCRATCH_BYTES = 4 << 20
 MOE_ROUTES_GIVEN = 1 << 0
 MOE_SHARED_EXPERT = 1 << 1
+MOE_EXL3_EXPERTS = 1 << 2
 
 STATUS_BITS = {
     1 << 0: "route-token-out-of-range",
@@ -124,11 +126,19 @@ class MoeLayerDescriptor(_Desc):
                             "w2_global_f32", "shared13_bf16", "shared2_bf16",
                             "route_experts_u16", "route_weights_f32", "output_f32",
                             "validation_error_u32", "workspace", "workspace_bytes",
-                            "sequence")] + [("reserved", u64 * 4)]
+                            "sequence", "exl3_experts")] + [("reserved", u64 * 3)]
+
+
+class MoeExl3Experts(_Desc):
+    """glmaxx_moe_exl3_experts (new), 128 bytes."""
+    _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "bits", "reserved0")] + \
+        [(n, u64) for n in ("codec_u8", "gate_trellis_u16", "up_trellis_u16", "down_trellis_u16",
+                            "gate_suh_f16", "gate_svh_f16", "up_suh_f16", "up_svh_f16",
+                            "down_suh_f16", "down_svh_f16")] + [("reserved", u64 * 4)]
 
 
 EXPECTED_SIZES = {Fc1Descriptor: 224, Fc2Descriptor: 224, Exl3Descriptor: 144,
-                  RouterDescriptor: 192, MoeLayerDescriptor: 240}
+                  RouterDescriptor: 192, MoeLayerDescriptor: 240, MoeExl3Experts: 128}
 
 _P = ctypes.c_void_p
 _I32P = ctypes.POINTER(ctypes.c_int32)

@@ -184,18 +184,20 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
   }
 }
 
-// Work list: one item per (group, block of rb rows) with rows; single CTA.
+// Work list: one item per (group, block of rb rows) of every group with rows
+// whose codec is EXL3 (codec == null: every group); single CTA.  Item order
+// does not affect results (every item computes its own outputs).
 __global__ void exl3_items_kernel(const uint32_t* __restrict__ group_rows, uint32_t groups,
-                                  uint32_t rb, uint32_t* __restrict__ items,
-                                  uint32_t* __restrict__ n_items) {
+                                  const uint8_t* __restrict__ codec, uint32_t rb,
+                                  uint32_t* __restrict__ items, uint32_t* __restrict__ n_items) {
   __shared__ uint32_t base;
   if (threadIdx.x == 0) base = 0;
   __syncthreads();
   for (uint32_t g0 = 0; g0 < groups; g0 += blockDim.x) {
     const uint32_t g = g0 + threadIdx.x;
-    const uint32_t rows = g < groups ? group_rows[g + 1] - group_rows[g] : 0;
+    uint32_t rows = g < groups ? group_rows[g + 1] - group_rows[g] : 0;
+    if (codec != nullptr && g < groups && codec[g] != 1) rows = 0;
     const uint32_t nb = (rows + rb - 1) / rb;
-    // block-wide exclusive scan of nb (small: sequential warps via atomics keeps order free)
     const uint32_t off = nb ? atomicAdd(&base, nb) : 0;
     for (uint32_t b = 0; b < nb; ++b) items[off + b] = (g << 16) | b;
     __syncthreads();
@@ -216,8 +218,104 @@ __global__ void exl3_rotate_out(const uint16_t* __restrict__ projected,
   out[idx] = f2h(__fmul_rn(hadamard_row(blk, i, norm), h2f(svh[b * 128 + i])));
 }
 
-// Rows per work item of the grouped launch (decode batches put 1-2 rows on most
-// experts; more rows make more items, each decoding the matrix again).
+// ---------------------------------------------------------------------------
+// Per-assignment-row stages of the EXL3 experts (rows in compacted order,
+// expert e owns rows offsets[e] .. offsets[e+1]; rows of NVFP4 experts are left
+// alone).  Each CTA handles one 128-wide block of one row.
+// ---------------------------------------------------------------------------
+struct Exl3RowMap {
+  const uint32_t* offsets;  // [E + 1]
+  const uint8_t* codec;     // [E] or null (every expert EXL3)
+  uint32_t E;
+};
+
+// Expert owning row r, or -1 when r is past the last row or the expert is not EXL3.
+__device__ __forceinline__ int exl3_row_expert(const Exl3RowMap& m, uint32_t r) {
+  if (r >= m.offsets[m.E]) return -1;
+  uint32_t lo = 0, hi = m.E;  // offsets[lo] <= r < offsets[hi]
+  while (hi - lo > 1) {
+    const uint32_t mid = (lo + hi) / 2;
+    if (m.offsets[mid] <= r) lo = mid; else hi = mid;
+  }
+  if (m.codec != nullptr && m.codec[lo] != 1) return -1;
+  return static_cast<int>(lo);
+}
+
+// Input rotation (exl3.rs:404-453 steps 1-2): out[r][k] = f16(H128(f16(x[r][k] *
+// suh[e][k]))).  x is either the bf16 token row row_token[r] of the layer
+// input (converted to fp16 first) or the fp16 row r of `src`.
+__global__ void exl3_rows_rotate_in(Exl3RowMap m, const uint16_t* __restrict__ x_bf16,
+                                    const uint32_t* __restrict__ row_token,
+                                    const uint16_t* __restrict__ src_f16,
+                                    const uint16_t* __restrict__ suh, uint32_t K,
+                                    uint16_t* __restrict__ out) {
+  __shared__ float blk[128];
+  __shared__ int s_e;
+  const uint32_t r = blockIdx.y, b = blockIdx.x, i = threadIdx.x;
+  if (i == 0) s_e = exl3_row_expert(m, r);
+  __syncthreads();
+  const int e = s_e;
+  if (e < 0) return;
+  const uint32_t k = b * 128 + i;
+  float xv;
+  if (x_bf16 != nullptr) {
+    const uint16_t bits = x_bf16[uint64_t(row_token[r]) * K + k];
+    xv = h2f(f2h(__uint_as_float(uint32_t(bits) << 16)));
+  } else {
+    xv = h2f(src_f16[uint64_t(r) * K + k]);
+  }
+  blk[i] = h2f(f2h(__fmul_rn(xv, h2f(suh[uint64_t(e) * K + k]))));
+  __syncthreads();
+  const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  out[uint64_t(r) * K + k] = f2h(hadamard_row(blk, i, norm));
+}
+
+// Output rotation (steps 4-5): y = f16(H128(p) * svh[e]).  With `plane` set the
+// routing-weighted fp32 value w * y goes to plane[token][slot][n] (the operand
+// of the expert-order combine); otherwise y replaces p in place.
+__global__ void exl3_rows_rotate_out(Exl3RowMap m, uint16_t* __restrict__ p,
+                                     const uint16_t* __restrict__ svh, uint32_t N,
+                                     float* __restrict__ plane, const uint32_t* __restrict__ row_token,
+                                     const uint32_t* __restrict__ row_slot,
+                                     const float* __restrict__ row_weight, uint32_t top_k) {
+  __shared__ float blk[128];
+  __shared__ int s_e;
+  const uint32_t r = blockIdx.y, b = blockIdx.x, i = threadIdx.x;
+  if (i == 0) s_e = exl3_row_expert(m, r);
+  __syncthreads();
+  const int e = s_e;
+  if (e < 0) return;
+  const uint32_t n = b * 128 + i;
+  blk[i] = h2f(p[uint64_t(r) * N + n]);
+  __syncthreads();
+  const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  const uint16_t y = f2h(__fmul_rn(hadamard_row(blk, i, norm), h2f(svh[uint64_t(e) * N + n])));
+  if (plane != nullptr) {
+    const uint64_t dst = uint64_t(row_token[r]) * top_k + row_slot[r];
+    plane[dst * N + n] = __fmul_rn(row_weight[r], h2f(y));
+  } else {
+    p[uint64_t(r) * N + n] = y;
+  }
+}
+
+// SwiGLU between the EXL3 projections: h = f16(silu(g) * u) with silu(v) =
+// v / (1 + exp(-v)) (CUDA's expf and an IEEE division).
+__global__ void exl3_rows_swiglu(Exl3RowMap m, const uint16_t* __restrict__ g,
+                                 const uint16_t* __restrict__ u, uint32_t I,
+                                 uint16_t* __restrict__ h) {
+  __shared__ int s_e;
+  const uint32_t r = blockIdx.y;
+  if (threadIdx.x == 0) s_e = exl3_row_expert(m, r);
+  __syncthreads();
+  if (s_e < 0) return;
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= I) return;
+  const uint64_t idx = uint64_t(r) * I + c;
+  const float gv = h2f(g[idx]);
+  const float sv = __fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv)));
+  h[idx] = f2h(__fmul_rn(sv, h2f(u[idx])));
+}
+
 constexpr int kExl3GroupRowBlock = 2;
 
 }  // namespace
@@ -247,14 +345,21 @@ cudaError_t launch_exl3_gemv_single(const uint16_t* x, const uint16_t* trellis, 
   return run_exl3_gemv<8>(a, (rows + 7) / 8, stream);
 }
 
+cudaError_t launch_exl3_items(const uint32_t* group_rows, uint32_t groups, const uint8_t* codec,
+                              uint32_t* items, uint32_t* n_items, cudaStream_t stream) {
+  if (groups >= 65536) return cudaErrorInvalidValue;
+  exl3_items_kernel<<<1, 256, 0, stream>>>(group_rows, groups, codec, kExl3GroupRowBlock, items,
+                                           n_items);
+  return cudaPeekAtLastError();
+}
+
+// Grouped projection over the item list of launch_exl3_items.
 cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
                                      uint64_t trellis_stride, const uint32_t* group_rows,
-                                     uint32_t groups, uint32_t max_items, uint32_t* items,
-                                     uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
+                                     uint32_t max_items, const uint32_t* items,
+                                     const uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
                                      cudaStream_t stream) {
-  if (K % 16 || N % 32 || groups >= 65536) return cudaErrorInvalidValue;
-  exl3_items_kernel<<<1, 256, 0, stream>>>(group_rows, groups, kExl3GroupRowBlock, items,
-                                           n_items);
+  if (K % 16 || N % 32) return cudaErrorInvalidValue;
   Exl3GemvArgs a{};
   a.x = x;
   a.trellis = trellis;
@@ -266,6 +371,69 @@ cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
   a.K = K;
   a.N = N;
   return run_exl3_gemv<kExl3GroupRowBlock>(a, max_items, stream);
+}
+
+uint64_t exl3_experts_workspace_bytes(uint32_t A, uint32_t H, uint32_t I, uint32_t E) {
+  const uint64_t wide = H > I ? H : I;
+  return 4 * uint64_t(A) * wide * 2 + uint64_t(A) * I * 2 + (uint64_t(E) + A + 2) * 4 + 6 * 256;
+}
+
+cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& L, cudaStream_t stream) {
+  const uint32_t A = L.A, H = L.H, I = L.I;
+  if (H % 128 || I % 128 || A == 0) return cudaErrorInvalidValue;
+  // workspace: xr [A][max(H,I)], p0, p1, p2 [A][max(H,I)], h [A][I], items
+  const uint64_t wide = H > I ? H : I;
+  uint8_t* w = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(L.workspace) + 255) & ~uintptr_t(255));
+  auto take = [&](uint64_t bytes) {
+    uint8_t* q = w;
+    w += (bytes + 255) / 256 * 256;
+    return q;
+  };
+  uint16_t* xr = reinterpret_cast<uint16_t*>(take(uint64_t(A) * wide * 2));
+  uint16_t* p0 = reinterpret_cast<uint16_t*>(take(uint64_t(A) * wide * 2));
+  uint16_t* p1 = reinterpret_cast<uint16_t*>(take(uint64_t(A) * wide * 2));
+  uint16_t* p2 = reinterpret_cast<uint16_t*>(take(uint64_t(A) * wide * 2));
+  uint16_t* h = reinterpret_cast<uint16_t*>(take(uint64_t(A) * I * 2));
+  uint32_t* n_items = reinterpret_cast<uint32_t*>(take(16));
+  uint32_t* items = reinterpret_cast<uint32_t*>(take((uint64_t(L.E) + A) * 4));
+  const uint32_t max_items = L.E + (A + kExl3GroupRowBlock - 1) / kExl3GroupRowBlock;
+  Exl3RowMap m{L.offsets, L.codec, L.E};
+  const uint64_t gate_stride = uint64_t(H) * I * kExl3Bits / 16;  // halves per expert
+#define X3(expr)                              \
+  do {                                        \
+    cudaError_t _st = (expr);                 \
+    if (_st != cudaSuccess) return _st;       \
+  } while (0)
+  X3(launch_exl3_items(L.offsets, L.E, L.codec, items, n_items, stream));
+  // gate / up: rotate the token rows with each projection's suh, project, rotate out
+  for (int proj = 0; proj < 2; ++proj) {
+    const uint16_t* suh = proj ? L.up_suh : L.gate_suh;
+    const uint16_t* svh = proj ? L.up_svh : L.gate_svh;
+    const uint16_t* tr = proj ? L.up_trellis : L.gate_trellis;
+    uint16_t* pout = proj ? p1 : p0;
+    exl3_rows_rotate_in<<<dim3(H / 128, A), 128, 0, stream>>>(m, L.x_bf16, L.row_token, nullptr,
+                                                               suh, H, xr);
+    X3(cudaPeekAtLastError());
+    X3(launch_exl3_gemv_grouped(xr, tr, gate_stride, L.offsets, max_items, items, n_items, H, I,
+                                pout, stream));
+    exl3_rows_rotate_out<<<dim3(I / 128, A), 128, 0, stream>>>(m, pout, svh, I, nullptr, nullptr,
+                                                                nullptr, nullptr, 0);
+    X3(cudaPeekAtLastError());
+  }
+  exl3_rows_swiglu<<<dim3((I + 255) / 256, A), 256, 0, stream>>>(m, p0, p1, I, h);
+  X3(cudaPeekAtLastError());
+  // down: rotate h, project to hidden, rotate out into the weighted plane
+  exl3_rows_rotate_in<<<dim3(I / 128, A), 128, 0, stream>>>(m, nullptr, nullptr, h, L.down_suh, I,
+                                                             xr);
+  X3(cudaPeekAtLastError());
+  X3(launch_exl3_gemv_grouped(xr, L.down_trellis, gate_stride, L.offsets, max_items, items,
+                              n_items, I, H, p2, stream));
+  exl3_rows_rotate_out<<<dim3(H / 128, A), 128, 0, stream>>>(m, p2, L.down_svh, H, L.plane,
+                                                              L.row_token, L.row_slot,
+                                                              L.row_weight, L.top_k);
+  X3(cudaPeekAtLastError());
+#undef X3
+  return cudaSuccess;
 }
 
 namespace {

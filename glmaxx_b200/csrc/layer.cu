@@ -53,6 +53,11 @@ struct LayerPlan {
   uint32_t H, I, Is, nt, sf_rows, max_tiles;
   uint32_t s1_splits, s1_kc, s2_splits, s2_kc;  // shared-expert split-K (decode)
   bool decode, shared;
+  // exl3: some experts are EXL3; nvfp4: some experts are NVFP4 (the NVFP4 stages
+  // run); plane_mode: routed results go through the per-slot plane and the
+  // deterministic expert-order combine (decode, and any layer with EXL3 experts)
+  bool exl3, nvfp4, plane_mode;
+  uint64_t exl3_ws;
   uint64_t tiles, tile_count, route_row, row_token, row_slot, row_weight, gx, gh, row_prow;
   uint64_t xq, xsf, hbuf, hq, hsf, plane, hs, sbuf, sparts1, sparts2, total;
 
@@ -64,6 +69,11 @@ struct LayerPlan {
     shared = (d.flags & GLMAXX_MOE_SHARED_EXPERT) != 0;
     Is = shared ? d.shared_intermediate : 0;
     decode = d.path == GLMAXX_FC1_DECODE_PERSISTENT || (d.path == 0 && d.tokens <= 256);
+    exl3 = (d.flags & GLMAXX_MOE_EXL3_EXPERTS) != 0;
+    const glmaxx_moe_exl3_experts* xe =
+        exl3 ? reinterpret_cast<const glmaxx_moe_exl3_experts*>(d.exl3_experts) : nullptr;
+    nvfp4 = !exl3 || (xe != nullptr && xe->codec_u8 != 0);
+    plane_mode = decode || exl3;
     nt = decode ? 32 : 128;
     const uint32_t A = r.A;
     const uint32_t active = A < r.E ? A : r.E;
@@ -83,9 +93,10 @@ struct LayerPlan {
     hbuf = c.take(uint64_t(A) * I * 2);
     hq = c.take(uint64_t(A) * I / 2);
     hsf = c.take(uint64_t(sf_rows) * I / 16);
-    plane = decode ? c.take(uint64_t(A) * H * 4) : c.take(0);
+    plane = plane_mode ? c.take(uint64_t(A) * H * 4) : c.take(0);
     hs = shared ? c.take(uint64_t(r.T) * Is * 2) : c.take(0);
-    sbuf = (shared && decode) ? c.take(uint64_t(r.T) * H * 4) : c.take(0);
+    sbuf = (shared && plane_mode) ? c.take(uint64_t(r.T) * H * 4) : c.take(0);
+    exl3_ws = exl3 ? c.take(exl3_experts_workspace_bytes(A, H, I, r.E)) : c.take(0);
     // Decode runs the shared expert as split-K GEMMs so that its few output
     // tiles still cover every SM (sized for up to 148 SMs).
     s1_splits = s1_kc = s2_splits = s2_kc = 1;
@@ -108,7 +119,28 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
     if (v) return false;
   for (uint64_t v : d.reserved)
     if (v) return false;
-  if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT)) return false;
+  if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT |
+                          GLMAXX_MOE_EXL3_EXPERTS))
+    return false;
+  bool nvfp4_weights = true;
+  if (d.flags & GLMAXX_MOE_EXL3_EXPERTS) {
+    if (d.exl3_experts == 0) return false;
+    const auto& xe = *reinterpret_cast<const glmaxx_moe_exl3_experts*>(d.exl3_experts);
+    if (xe.abi_version != GLMAXX_MOE_EXL3_ABI_VERSION || xe.struct_bytes != sizeof(xe) ||
+        xe.bits != 3 || xe.reserved0)
+      return false;
+    for (uint64_t v : xe.reserved)
+      if (v) return false;
+    if (!aligned(xe.gate_trellis_u16, 16) || !aligned(xe.up_trellis_u16, 16) ||
+        !aligned(xe.down_trellis_u16, 16) || !aligned(xe.gate_suh_f16, 2) ||
+        !aligned(xe.gate_svh_f16, 2) || !aligned(xe.up_suh_f16, 2) || !aligned(xe.up_svh_f16, 2) ||
+        !aligned(xe.down_suh_f16, 2) || !aligned(xe.down_svh_f16, 2))
+      return false;
+    if (d.hidden % 128 || d.local_intermediate % 128) return false;
+    nvfp4_weights = xe.codec_u8 != 0;
+  } else if (d.exl3_experts) {
+    return false;
+  }
   if (d.path > GLMAXX_FC1_PREFILL_GROUPED) return false;
   if (d.tokens == 0 || d.tokens > 65536) return false;
   if (d.hidden == 0 || d.hidden % 256 != 0 || d.hidden > 16384) return false;  // <= 256 k-blocks
@@ -131,9 +163,11 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
       return false;
     if (!aligned(d.shared13_bf16, 256) || !aligned(d.shared2_bf16, 256)) return false;
   }
-  return aligned(d.input_bf16, 256) && aligned(d.w13_values, 256) && aligned(d.w13_scales, 16) &&
-         aligned(d.w13_global_f32, 4) && aligned(d.w2_values, 256) && aligned(d.w2_scales, 16) &&
-         aligned(d.w2_global_f32, 4) && aligned(d.route_experts_u16, 4) &&
+  if (nvfp4_weights &&
+      !(aligned(d.w13_values, 256) && aligned(d.w13_scales, 16) && aligned(d.w13_global_f32, 4) &&
+        aligned(d.w2_values, 256) && aligned(d.w2_scales, 16) && aligned(d.w2_global_f32, 4)))
+    return false;
+  return aligned(d.input_bf16, 256) && aligned(d.route_experts_u16, 4) &&
          aligned(d.route_weights_f32, 4) && aligned(d.output_f32, 16) && aligned(d.workspace, 16);
 }
 
@@ -195,8 +229,12 @@ int32_t layer_plane(const glmaxx_moe_layer_descriptor* desc, uint32_t which, uin
       *address = ws + p.r.offsets, *bytes = uint64_t(p.r.E + 1) * 4;
       break;
     case GLMAXX_PLANE_SHARED_F32:
-      if (!p.shared || !p.decode) return GLMAXX_ERR_DESCRIPTOR;
+      if (!p.shared || !p.plane_mode) return GLMAXX_ERR_DESCRIPTOR;
       *address = ws + p.sbuf, *bytes = uint64_t(p.r.T) * p.H * 4;
+      break;
+    case GLMAXX_PLANE_ROUTED_F32:
+      if (!p.plane_mode) return GLMAXX_ERR_DESCRIPTOR;
+      *address = ws + p.plane, *bytes = A * p.H * 4;
       break;
     default:
       return GLMAXX_ERR_DESCRIPTOR;
@@ -250,10 +288,13 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   CHECK(mark(kStageCompact, stream));
   NTile* tiles = at<NTile>(ws, p.tiles);
   uint32_t* tile_count = at<uint32_t>(ws, p.tile_count);
+  const glmaxx_moe_exl3_experts* xe =
+      p.exl3 ? reinterpret_cast<const glmaxx_moe_exl3_experts*>(d.exl3_experts) : nullptr;
+  const uint8_t* codec = xe ? reinterpret_cast<const uint8_t*>(xe->codec_u8) : nullptr;
   CHECK(launch_compact(at<uint32_t>(ws, r.bitmap), r.T, r.E, p.nt, p.sf_rows, p.max_tiles,
                        at<uint32_t>(ws, r.wprefix), at<uint32_t>(ws, r.counts),
                        at<uint32_t>(ws, r.offsets), at<uint32_t>(ws, r.poffs), tiles, tile_count,
-                       status, stream));
+                       status, stream, codec));
   // 3. NVFP4 quantisation of x into the assignment rows
   CHECK(mark(kStageQuant, stream));
   QuantScatterArgs q{};
@@ -280,9 +321,36 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   q.sf_row_cap = p.sf_rows;
   q.nt = p.nt;
   CHECK(launch_quant_scatter(q, stream));
-  // 4. grouped FC1 (gate+up) with fused SwiGLU -> h [A][I] bf16
+  // 4. grouped FC1 (gate+up) with fused SwiGLU -> h [A][I] bf16 (NVFP4 experts);
+  //    EXL3 experts: gate/up/down projections straight into the routed plane
   CHECK(mark(kStageFc1, stream));
-  {
+  if (p.exl3) {
+    Exl3ExpertsLaunch L{};
+    L.A = r.A;
+    L.H = p.H;
+    L.I = p.I;
+    L.E = r.E;
+    L.top_k = r.K;
+    L.x_bf16 = x;
+    L.offsets = at<uint32_t>(ws, r.offsets);
+    L.codec = codec;
+    L.row_token = q.row_token;
+    L.row_slot = q.row_slot;
+    L.row_weight = q.row_weight;
+    L.gate_trellis = reinterpret_cast<const uint16_t*>(xe->gate_trellis_u16);
+    L.up_trellis = reinterpret_cast<const uint16_t*>(xe->up_trellis_u16);
+    L.down_trellis = reinterpret_cast<const uint16_t*>(xe->down_trellis_u16);
+    L.gate_suh = reinterpret_cast<const uint16_t*>(xe->gate_suh_f16);
+    L.gate_svh = reinterpret_cast<const uint16_t*>(xe->gate_svh_f16);
+    L.up_suh = reinterpret_cast<const uint16_t*>(xe->up_suh_f16);
+    L.up_svh = reinterpret_cast<const uint16_t*>(xe->up_svh_f16);
+    L.down_suh = reinterpret_cast<const uint16_t*>(xe->down_suh_f16);
+    L.down_svh = reinterpret_cast<const uint16_t*>(xe->down_svh_f16);
+    L.plane = at<float>(ws, p.plane);
+    L.workspace = at<void>(ws, p.exl3_ws);
+    CHECK(launch_exl3_experts(L, stream));
+  }
+  if (p.nvfp4) {
     GemmLaunch g{};
     g.a = reinterpret_cast<const void*>(d.w13_values);
     g.a_experts = r.E;
@@ -322,7 +390,10 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   f.count = r.A;
   f.I = p.I;
   f.sf_row_cap = p.sf_rows;
-  CHECK(launch_fc2_quant(f, stream));
+  f.offsets = at<uint32_t>(ws, r.offsets);
+  f.skip_codec = codec;
+  f.E = r.E;
+  if (p.nvfp4) CHECK(launch_fc2_quant(f, stream));
   // 6. shared expert (bf16), and the output initialisation it provides
   CHECK(mark(kStageShared, stream));
   if (p.shared) {
@@ -372,15 +443,16 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
       g1.args.ldo = p.Is;
       g1.args.out = at<void>(ws, p.hs);
       CHECK(launch_gemm(kShared1Bf16N128, g1, info.sms, stream));
-      g2.args.out = static_cast<void*>(out);
+      // plane mode: the combine adds the shared expert from sbuf
+      g2.args.out = p.plane_mode ? at<void>(ws, p.sbuf) : static_cast<void*>(out);
       CHECK(launch_gemm(kShared2Bf16N128, g2, info.sms, stream));
     }
-  } else if (!p.decode) {
+  } else if (!p.plane_mode) {
     CHECK(cudaMemsetAsync(out, 0, uint64_t(r.T) * p.H * 4, stream));
   }
   // 7. grouped FC2 with the routing-weighted combine
   CHECK(mark(kStageFc2, stream));
-  {
+  if (p.nvfp4) {
     GemmLaunch g{};
     g.a = reinterpret_cast<const void*>(d.w2_values);
     g.a_experts = r.E;
@@ -406,19 +478,24 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     a.sfb = f.hsf;
     a.a_global = reinterpret_cast<const float*>(d.w2_global_f32);
     a.b_global = f.gscale;
-    a.out = p.decode ? at<void>(ws, p.plane) : static_cast<void*>(out);
+    a.out = p.plane_mode ? at<void>(ws, p.plane) : static_cast<void*>(out);
     a.row_token = q.row_token;
     a.row_slot = q.row_slot;
     a.row_weight = q.row_weight;
     a.status = status;
-    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair : kFc2PrefillFp4Pair, g, info.sms, stream));
+    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair
+                             : (p.plane_mode ? kFc2PrefillFp4PairPlane : kFc2PrefillFp4Pair),
+                      g, info.sms, stream));
   }
-  // 8. deterministic combine (decode): ascending-expert sum + shared
+  // 8. deterministic combine (plane mode): ascending-expert sum + shared
   CHECK(mark(kStageCombine, stream));
-  if (p.decode)
-    CHECK(launch_combine(at<float>(ws, p.plane), experts,
-                         p.shared ? at<float>(ws, p.sparts2) : nullptr, p.s2_splits,
-                         p.shared ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H, r.K, stream));
+  if (p.plane_mode) {
+    const float* shared_in = !p.shared ? nullptr
+                             : (p.decode ? at<float>(ws, p.sparts2) : at<float>(ws, p.sbuf));
+    CHECK(launch_combine(at<float>(ws, p.plane), experts, shared_in, p.decode ? p.s2_splits : 1,
+                         (p.shared && p.decode) ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H,
+                         r.K, stream));
+  }
   CHECK(mark(kLayerStages, stream));
 #undef CHECK
   return 0;

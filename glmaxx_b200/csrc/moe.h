@@ -95,6 +95,10 @@ struct Fc2QuantArgs {
   uint32_t* status;
   const uint32_t* count_ptr; // device count of rows (offsets[E]) or null
   uint32_t count, I, sf_row_cap;
+  // optional: rows of experts with skip_codec[e] == 1 (EXL3) are not quantised
+  const uint32_t* offsets;   // [E + 1] compacted row offsets
+  const uint8_t* skip_codec; // [E]
+  uint32_t E;
 };
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
@@ -111,7 +115,8 @@ cudaError_t launch_routes_to_bitmap(const uint16_t* experts, const float* weight
 cudaError_t launch_compact(const uint32_t* bitmap, uint32_t T, uint32_t E, uint32_t nt,
                            uint32_t sf_row_cap, uint32_t max_tiles, uint32_t* wprefix,
                            uint32_t* counts, uint32_t* offsets, uint32_t* poffs, NTile* tiles,
-                           uint32_t* tile_count, uint32_t* status, cudaStream_t stream);
+                           uint32_t* tile_count, uint32_t* status, cudaStream_t stream,
+                           const uint8_t* no_tiles = nullptr);
 cudaError_t launch_quant_scatter(const QuantScatterArgs& a, cudaStream_t stream);
 cudaError_t launch_compact_write(const CompactWriteArgs& a, cudaStream_t stream);
 cudaError_t launch_compat_prepare(const CompatPrepareArgs& a, cudaStream_t stream);
@@ -154,6 +159,7 @@ enum GemmVariant : int {
   kShared2Bf16N64Split = 11,  // BF16, N tile 64, split-K partials
   kFc2DecodeFp4Pair = 12,     // NVFP4, two adjacent M tiles per item, N tile 32, routed plane
   kFc2PrefillFp4Pair = 13,    // NVFP4, two adjacent M tiles per item, N tile 128, routed atomics
+  kFc2PrefillFp4PairPlane = 14,  // as 13, writing the routed plane (deterministic combine)
 };
 
 // Number of K slices (and chunks per slice) that spread `tiles` output tiles of

@@ -371,7 +371,9 @@ __global__ void __launch_bounds__(1024) compact_kernel(
     const uint32_t* __restrict__ bitmap, uint32_t W, uint32_t E, uint32_t nt, uint32_t sf_row_cap,
     uint32_t max_tiles, uint32_t* __restrict__ wprefix, uint32_t* __restrict__ counts,
     uint32_t* __restrict__ offsets, uint32_t* __restrict__ poffs, NTile* __restrict__ tiles,
-    uint32_t* __restrict__ tile_count, uint32_t* __restrict__ status) {
+    uint32_t* __restrict__ tile_count, uint32_t* __restrict__ status,
+    const uint8_t* __restrict__ no_tiles) {
+  // no_tiles[e] != 0 (optional): expert e gets rows but no GEMM tiles (an EXL3 expert)
   __shared__ uint32_t cnt_s[256], toff_s[257], poff_s[257], off_s[257];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (uint32_t e = warp; e < E; e += 32) {
@@ -400,7 +402,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
       if (e < E) {
         sc += cnt_s[e];
         sp += (cnt_s[e] + nt - 1) / nt * 128;
-        st += (cnt_s[e] + nt - 1) / nt;
+        st += (no_tiles && no_tiles[e]) ? 0 : (cnt_s[e] + nt - 1) / nt;
       }
     }
     uint32_t ic = sc, ip = sp, it = st;
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
         counts[e] = cnt_s[e];
         oc += cnt_s[e];
         op += (cnt_s[e] + nt - 1) / nt * 128;
-        ot += (cnt_s[e] + nt - 1) / nt;
+        ot += (no_tiles && no_tiles[e]) ? 0 : (cnt_s[e] + nt - 1) / nt;
       }
     }
     if (lane == 31) {
@@ -444,7 +446,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
   __syncthreads();
   if (tiles == nullptr || poff_s[E] > sf_row_cap || toff_s[E] > max_tiles) return;
   for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) {
-    const uint32_t c = cnt_s[e];
+    const uint32_t c = (no_tiles && no_tiles[e]) ? 0 : cnt_s[e];
     for (uint32_t j = 0; j * nt < c; ++j) {
       NTile tl;
       tl.expert = e;
@@ -548,7 +550,15 @@ __global__ void __launch_bounds__(256) fc2_quant_kernel(Fc2QuantArgs a) {
   const uint32_t r_local = threadIdx.x / KB2, kb = threadIdx.x % KB2;
   const uint32_t row = blockIdx.x * rows_per_block + r_local;
   const uint32_t count = a.count_ptr ? min(*a.count_ptr, a.count) : a.count;
-  const bool active = row < count;
+  bool active = row < count;
+  if (active && a.skip_codec != nullptr) {
+    uint32_t lo = 0, hi = a.E;  // expert of the row: offsets[lo] <= row < offsets[hi]
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) / 2;
+      if (a.offsets[mid] <= row) lo = mid; else hi = mid;
+    }
+    active = a.skip_codec[lo] != 1;
+  }
   float v[64];
   float amax = 0.f;
   bool finite = true;
@@ -953,9 +963,11 @@ cudaError_t launch_routes_to_bitmap(const uint16_t* experts, const float* weight
 cudaError_t launch_compact(const uint32_t* bitmap, uint32_t T, uint32_t E, uint32_t nt,
                            uint32_t sf_row_cap, uint32_t max_tiles, uint32_t* wprefix,
                            uint32_t* counts, uint32_t* offsets, uint32_t* poffs, NTile* tiles,
-                           uint32_t* tile_count, uint32_t* status, cudaStream_t stream) {
+                           uint32_t* tile_count, uint32_t* status, cudaStream_t stream,
+                           const uint8_t* no_tiles) {
   compact_kernel<<<1, 1024, 0, stream>>>(bitmap, (T + 31) / 32, E, nt, sf_row_cap, max_tiles,
-                                         wprefix, counts, offsets, poffs, tiles, tile_count, status);
+                                         wprefix, counts, offsets, poffs, tiles, tile_count, status,
+                                         no_tiles);
   return cudaPeekAtLastError();
 }
 

@@ -44,10 +44,23 @@ int32_t router_compact_launch(const glmaxx_router_descriptor* desc, void* stream
 // order; single matrix over `rows` rows, or groups of rows (one trellis each).
 cudaError_t launch_exl3_gemv_single(const uint16_t* x, const uint16_t* trellis, uint32_t rows,
                                     uint32_t K, uint32_t N, uint16_t* out, cudaStream_t stream);
-cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
-                                     uint64_t trellis_stride, const uint32_t* group_rows,
-                                     uint32_t groups, uint32_t max_items, uint32_t* items,
-                                     uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
-                                     cudaStream_t stream);
+// EXL3 routed experts of the layer (exl3.cu): rows in compacted order, every
+// EXL3 expert's rows through gate/up projections, SwiGLU and down projection,
+// the routing-weighted result into plane[token][slot][hidden].
+struct Exl3ExpertsLaunch {
+  uint32_t A, H, I, E, top_k;
+  const uint16_t* x_bf16;      // layer input [T][H]
+  const uint32_t* offsets;     // [E + 1] compacted row offsets
+  const uint8_t* codec;        // [E] or null
+  const uint32_t* row_token;
+  const uint32_t* row_slot;
+  const float* row_weight;
+  const uint16_t *gate_trellis, *up_trellis, *down_trellis;
+  const uint16_t *gate_suh, *gate_svh, *up_suh, *up_svh, *down_suh, *down_svh;
+  float* plane;                // [T][top_k][H]
+  void* workspace;             // exl3_experts_workspace_bytes
+};
+uint64_t exl3_experts_workspace_bytes(uint32_t A, uint32_t H, uint32_t I, uint32_t E);
+cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& launch, cudaStream_t stream);
 
 }  // namespace glmaxx

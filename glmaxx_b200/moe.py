@@ -88,14 +88,33 @@ def pack_nvfp4(src: torch.Tensor) -> PackedNvfp4:
 
 
 @dataclass
+class Exl3Experts:
+    """One rank's EXL3 3-bit expert shards (glmaxx_moe_exl3_experts): trellises
+    in the reference tile layout (exl3.rs) as int16 words, expert-major; fp16
+    suh (input) / svh (output) scales; codec [E] uint8 (1 = EXL3, 0 = the
+    NVFP4 weights) or None for an all-EXL3 layer."""
+    gate_trellis: torch.Tensor   # [E, (H/16)*(I_r/16)*48] int16  (K = H, N = I_r)
+    up_trellis: torch.Tensor     # [E, (H/16)*(I_r/16)*48] int16
+    down_trellis: torch.Tensor   # [E, (I_r/16)*(H/16)*48] int16  (K = I_r, N = H)
+    gate_suh: torch.Tensor       # [E, H] f16
+    gate_svh: torch.Tensor       # [E, I_r] f16
+    up_suh: torch.Tensor         # [E, H] f16
+    up_svh: torch.Tensor         # [E, I_r] f16
+    down_suh: torch.Tensor       # [E, I_r] f16
+    down_svh: torch.Tensor       # [E, H] f16
+    codec: torch.Tensor | None = None
+
+
+@dataclass
 class RankWeights:
     """One rank's layer weights (device tensors)."""
     router_weight: torch.Tensor          # [E, H] bf16 (replicated)
     router_bias: torch.Tensor            # [E] f32 (replicated)
-    w13: PackedNvfp4                     # [E] x [2*I_r, H]: rank gate rows then up rows
-    w2: PackedNvfp4                      # [E] x [H, I_r]
+    w13: PackedNvfp4 | None              # [E] x [2*I_r, H]: rank gate rows then up rows
+    w2: PackedNvfp4 | None               # [E] x [H, I_r]
     shared13: torch.Tensor | None = None  # [2*Is_r, H] bf16
     shared2: torch.Tensor | None = None   # [H, Is_r] bf16
+    exl3: Exl3Experts | None = None       # EXL3 experts (all, or those codec selects)
 
 
 class RoutedMoE:
@@ -122,6 +141,19 @@ class RoutedMoE:
         flags = (abi.MOE_ROUTES_GIVEN if routes_given else 0)
         if c.shared_intermediate and w.shared13 is not None:
             flags |= abi.MOE_SHARED_EXPERT
+        xd = None
+        if w.exl3 is not None:
+            flags |= abi.MOE_EXL3_EXPERTS
+            x3 = w.exl3
+            xd = abi.MoeExl3Experts.new(
+                abi_version=abi.MOE_EXL3_ABI_VERSION, bits=3, codec_u8=_ptr(x3.codec),
+                gate_trellis_u16=_ptr(x3.gate_trellis), up_trellis_u16=_ptr(x3.up_trellis),
+                down_trellis_u16=_ptr(x3.down_trellis), gate_suh_f16=_ptr(x3.gate_suh),
+                gate_svh_f16=_ptr(x3.gate_svh), up_suh_f16=_ptr(x3.up_suh),
+                up_svh_f16=_ptr(x3.up_svh), down_suh_f16=_ptr(x3.down_suh),
+                down_svh_f16=_ptr(x3.down_svh))
+        w13 = w.w13
+        w2 = w.w2
         d = abi.MoeLayerDescriptor.new(
             abi_version=abi.MOE_LAYER_ABI_VERSION, flags=flags, path=path, tokens=tokens,
             hidden=c.hidden, experts=c.experts, local_intermediate=c.local_intermediate,
@@ -129,13 +161,17 @@ class RoutedMoE:
             route_scale=c.route_scale,
             shared_intermediate=c.local_shared if flags & abi.MOE_SHARED_EXPERT else 0,
             input_bf16=x.data_ptr(), router_weight_bf16=_ptr(w.router_weight),
-            router_bias_f32=_ptr(w.router_bias), w13_values=w.w13.values.data_ptr(),
-            w13_scales=w.w13.scales.data_ptr(), w13_global_f32=w.w13.global_scale.data_ptr(),
-            w2_values=w.w2.values.data_ptr(), w2_scales=w.w2.scales.data_ptr(),
-            w2_global_f32=w.w2.global_scale.data_ptr(), shared13_bf16=_ptr(w.shared13),
+            router_bias_f32=_ptr(w.router_bias),
+            w13_values=_ptr(w13.values if w13 else None),
+            w13_scales=_ptr(w13.scales if w13 else None),
+            w13_global_f32=_ptr(w13.global_scale if w13 else None),
+            w2_values=_ptr(w2.values if w2 else None), w2_scales=_ptr(w2.scales if w2 else None),
+            w2_global_f32=_ptr(w2.global_scale if w2 else None), shared13_bf16=_ptr(w.shared13),
             shared2_bf16=_ptr(w.shared2), route_experts_u16=self.route_experts.data_ptr(),
             route_weights_f32=self.route_weights.data_ptr(), output_f32=out.data_ptr(),
-            validation_error_u32=self.status.data_ptr(), sequence=1)
+            validation_error_u32=self.status.data_ptr(), sequence=1,
+            exl3_experts=ctypes.addressof(xd) if xd is not None else 0)
+        d._exl3 = xd  # the library reads it through exl3_experts at launch
         need = int(self.lib.glmaxx_moe_layer_workspace_bytes(ctypes.byref(d)))
         key = (tokens, flags, path)
         ws = self._ws.get(key)

@@ -15,7 +15,7 @@ import math
 
 import torch
 
-from .moe import MoEConfig, RankWeights, pack_nvfp4
+from .moe import Exl3Experts, MoEConfig, RankWeights, pack_nvfp4
 
 
 def _gen(device, seed: int) -> torch.Generator:
@@ -50,6 +50,23 @@ def make_router(cfg: MoEConfig, seed: int, device, zipf_beta: float | None = Non
     return router_w, bias
 
 
+def make_shared(cfg: MoEConfig, seed: int, device):
+    """bf16 shared-expert shard of rank cfg.rank: gate/up rows [2*Is_r, H] (rank
+    gate rows then up rows) and down [H, Is_r], from full N(0, 0.02) matrices;
+    (None, None) without a shared expert."""
+    if not cfg.shared_intermediate:
+        return None, None
+    H, r = cfg.hidden, cfg.rank
+    Is, Isr = cfg.shared_intermediate, cfg.local_shared
+    gen = _gen(device, seed * 1000 + 7)
+    f13 = torch.randn(2 * Is, H, generator=gen, device=device) * 0.02
+    f2 = torch.randn(H, Is, generator=gen, device=device) * 0.02
+    shared13 = torch.cat([f13[r * Isr:(r + 1) * Isr], f13[Is + r * Isr:Is + (r + 1) * Isr]]
+                         ).to(torch.bfloat16).contiguous()
+    shared2 = f2[:, r * Isr:(r + 1) * Isr].to(torch.bfloat16).contiguous()
+    return shared13, shared2
+
+
 def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | None = None,
                       expert_chunk: int = 8, keep_masters: bool = False):
     """Router (replicated), NVFP4 expert shards and bf16 shared shard of rank cfg.rank."""
@@ -80,15 +97,7 @@ def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | N
                            torch.cat([p.global_scale for p in parts]),
                            torch.cat([p.global_amax for p in parts]), parts[0].n, parts[0].k)
 
-    shared13 = shared2 = None
-    if cfg.shared_intermediate:
-        Is, Isr = cfg.shared_intermediate, cfg.local_shared
-        gen = _gen(device, seed * 1000 + 7)
-        f13 = torch.randn(2 * Is, H, generator=gen, device=device) * 0.02
-        f2 = torch.randn(H, Is, generator=gen, device=device) * 0.02
-        shared13 = torch.cat([f13[r * Isr:(r + 1) * Isr], f13[Is + r * Isr:Is + (r + 1) * Isr]]
-                             ).to(torch.bfloat16).contiguous()
-        shared2 = f2[:, r * Isr:(r + 1) * Isr].to(torch.bfloat16).contiguous()
+    shared13, shared2 = make_shared(cfg, seed, device)
     w = RankWeights(router_w.contiguous(), bias.contiguous(), cat(w13_parts), cat(w2_parts),
                     shared13, shared2)
     return (w, masters) if keep_masters else w
@@ -140,3 +149,57 @@ def fit_zipf_beta(cfg: MoEConfig, tokens: int, seed: int, device, s: float = 1.1
         else:
             hi = mid
     return best
+
+
+def exl3_decoded_std() -> float:
+    """Standard deviation of the 3INST decoded weight over uniformly random 16-bit
+    trellis windows (value = window * 0xCBAC1FED, (value & 0x8FFF8FFF) ^ 0x3B603B60
+    read as two fp16 halves, summed; exl3.rs:471-477)."""
+    import numpy as np
+    w = np.arange(65536, dtype=np.uint64)
+    v = ((w * 0xCBAC1FED) & 0xFFFFFFFF) & 0x8FFF8FFF ^ 0x3B603B60
+    lo = (v & 0xFFFF).astype(np.uint16).view(np.float16).astype(np.float32)
+    hi = (v >> 16).astype(np.uint16).view(np.float16).astype(np.float32)
+    return float(np.std((lo + hi).astype(np.float16).astype(np.float32)))
+
+
+def make_exl3_experts(cfg: MoEConfig, seed: int, device, codec: torch.Tensor | None = None,
+                      weight_std: float = 0.02) -> Exl3Experts:
+    """Seeded EXL3 3-bit expert shards of rank cfg.rank.  The reference's CPU
+    encoder is not part of the reference repository, so the trellis words are
+    seeded random, as in its own fixtures (exl3.rs:667-684); suh holds random
+    signs and svh random signs of magnitude weight_std / std(decoded weight),
+    which gives the effective weights (H128-rotated on both sides) std weight_std."""
+    E, H, Ir, r = cfg.experts, cfg.hidden, cfg.local_intermediate, cfg.rank
+    g = _gen(device, seed * 7717 + 101 * r + 13)
+    words_gu = (H // 16) * (Ir // 16) * 48
+
+    def trellis():
+        return torch.randint(-32768, 32768, (E, words_gu), generator=g, device=device,
+                             dtype=torch.int32).to(torch.int16)
+
+    def signs(n, mag):
+        s = torch.randint(0, 2, (E, n), generator=g, device=device).to(torch.float32) * 2 - 1
+        return (s * mag).to(torch.float16)
+
+    mag = weight_std / exl3_decoded_std()
+    return Exl3Experts(gate_trellis=trellis(), up_trellis=trellis(), down_trellis=trellis(),
+                       gate_suh=signs(H, 1.0), gate_svh=signs(Ir, mag),
+                       up_suh=signs(H, 1.0), up_svh=signs(Ir, mag),
+                       down_suh=signs(Ir, 1.0), down_svh=signs(H, mag), codec=codec)
+
+
+def make_exl3_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | None = None,
+                           nvfp4_experts: torch.Tensor | None = None) -> RankWeights:
+    """Router, EXL3 experts and bf16 shared shard of rank cfg.rank.  With
+    nvfp4_experts (a bool [E] mask) the layer is hybrid: those experts use NVFP4
+    weights (generated as make_rank_weights does) and the rest EXL3."""
+    if nvfp4_experts is None:
+        router_w, bias = make_router(cfg, seed, device, zipf_beta)
+        shared13, shared2 = make_shared(cfg, seed, device)
+        return RankWeights(router_w.contiguous(), bias.contiguous(), None, None, shared13,
+                           shared2, make_exl3_experts(cfg, seed, device))
+    w = make_rank_weights(cfg, seed, device, zipf_beta=zipf_beta)
+    codec = (~nvfp4_experts.to(device)).to(torch.uint8)
+    w.exl3 = make_exl3_experts(cfg, seed, device, codec=codec)
+    return w

@@ -45,6 +45,7 @@ enum {
   GLMAXX_EXL3_ABI_VERSION = 1,
   GLMAXX_ROUTER_ABI_VERSION = 3,
   GLMAXX_MOE_LAYER_ABI_VERSION = 3,
+  GLMAXX_MOE_EXL3_ABI_VERSION = 1,
   GLMAXX_FC1_DECODE_PERSISTENT = 1,
   GLMAXX_FC1_PREFILL_GROUPED = 2,
   GLMAXX_EXL3_GATE = 1,
@@ -77,6 +78,7 @@ enum {
 enum {
   GLMAXX_MOE_ROUTES_GIVEN = 1u << 0,   /* route_experts/route_weights are inputs */
   GLMAXX_MOE_SHARED_EXPERT = 1u << 1,  /* add the bf16 shared expert            */
+  GLMAXX_MOE_EXL3_EXPERTS = 1u << 2,   /* exl3_experts describes EXL3 experts   */
 };
 
 /* glmaxx_kernel.h:22-57 (unchanged layout). */
@@ -225,6 +227,42 @@ struct glmaxx_router_descriptor {
 };
 
 /*
+ * EXL3 routed experts of a layer (new; the reference's per-expert hybrid codec,
+ * crates/glm-engine/src/weight.rs:37-50,116-215).  Each expert's gate, up and
+ * down projections are 3-bit trellises in the reference layout (exl3.rs, 16x16
+ * tiles of 48 halves, K x N logical: gate/up hidden x local_intermediate, down
+ * local_intermediate x hidden), with fp16 input signs/scales suh [K] and output
+ * scales svh [N]; arrays are expert-major ([experts][...]).  codec_u8 (device,
+ * [experts]) selects per expert: 0 = the descriptor's NVFP4 weights, 1 = EXL3;
+ * codec_u8 = 0 (null) makes every expert EXL3.  Per assignment row the layer
+ * computes y = proj(x) exactly as Exl3Trellis::matmul_reference_f16 (exl3.rs:
+ * 404-453) for gate and up (x = fp16 of the bf16 token row), h = fp16(silu(g)
+ * * u), down = proj(h), and adds the routing-weighted fp32 value in the
+ * deterministic expert order of the decode combine.
+ */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_moe_exl3_experts {
+#else
+struct glmaxx_moe_exl3_experts {
+#endif
+  uint32_t abi_version; /* GLMAXX_MOE_EXL3_ABI_VERSION */
+  uint32_t struct_bytes;
+  uint32_t bits; /* 3 */
+  uint32_t reserved0;
+  uint64_t codec_u8;
+  uint64_t gate_trellis_u16;
+  uint64_t up_trellis_u16;
+  uint64_t down_trellis_u16;
+  uint64_t gate_suh_f16;
+  uint64_t gate_svh_f16;
+  uint64_t up_suh_f16;
+  uint64_t up_svh_f16;
+  uint64_t down_suh_f16;
+  uint64_t down_svh_f16;
+  uint64_t reserved[4];
+};
+
+/*
  * Full rank-local routed-MoE step (new).  Weights are in the reference's
  * packed rank layout: per expert, gate/up NVFP4 [2*local_intermediate][hidden]
  * (rank-local gate rows, then up rows: nvfp4-physical-abi.md:18-28) and down
@@ -274,7 +312,9 @@ struct glmaxx_moe_layer_descriptor {
   uint64_t workspace;
   uint64_t workspace_bytes;
   uint64_t sequence;
-  uint64_t reserved[4];
+  /* host address of a glmaxx_moe_exl3_experts (flag GLMAXX_MOE_EXL3_EXPERTS), else 0 */
+  uint64_t exl3_experts;
+  uint64_t reserved[3];
 };
 
 /* ---- reference entry points (glmaxx_kernel.h:123-250) ---- */
@@ -447,6 +487,8 @@ enum {
   GLMAXX_PLANE_ROW_WEIGHT_F32 = 3,     /* [assignments] routing weight                    */
   GLMAXX_PLANE_EXPERT_OFFSETS_U32 = 4, /* [experts + 1] exclusive compacted offsets       */
   GLMAXX_PLANE_SHARED_F32 = 5,         /* [tokens][hidden] shared expert (decode path)     */
+  GLMAXX_PLANE_ROUTED_F32 = 6,         /* [tokens][top_k][hidden] routing-weighted expert
+                                          outputs per slot (decode path, EXL3 experts)   */
 };
 int32_t glmaxx_moe_layer_plane(const struct glmaxx_moe_layer_descriptor* descriptor,
                                uint32_t which, uint64_t* address, uint64_t* bytes);
@@ -472,6 +514,7 @@ static_assert(sizeof(glmaxx_exl3_descriptor) == 144, "Rust/C EXL3 descriptor siz
 static_assert(alignof(glmaxx_exl3_descriptor) == 16, "Rust/C EXL3 descriptor alignment mismatch");
 static_assert(sizeof(glmaxx_router_descriptor) == 192, "router descriptor size");
 static_assert(sizeof(glmaxx_moe_layer_descriptor) == 240, "layer descriptor size");
+static_assert(sizeof(glmaxx_moe_exl3_experts) == 128, "EXL3 experts descriptor size");
 #endif
 
 #endif /* GLMAXX_KERNEL_H_ */
