@@ -43,7 +43,15 @@ WORKLOADS = {
                 "metric": "routed-MoE layer tokens/s (prefill T=8192, Zipf(1.1) routing, 256 "
                           "experts, top-8, NVFP4 W4A4)",
                 "name": "prefill T=8192, Zipf(s=1.1) expert counts (BASELINE configs[2])"},
+    "exl3": {"tokens": 32, "zipf": False, "bound": "hbm", "codec": "exl3",
+             "metric": "routed-MoE layer tokens/s (EXL3 3-bit decode T=32, 256 experts, top-8)",
+             "name": "EXL3 trellis decode T=32 (BASELINE configs[3])"},
+    "hybrid": {"tokens": 2048, "zipf": True, "bound": "hbm", "codec": "hybrid", "layers": 4,
+               "metric": "4-layer routed-MoE stack tokens/s (2048 tokens, 64 NVFP4 + 192 EXL3 "
+                         "experts, Zipf routing, bf16 residual)",
+               "name": "hybrid continuous-batch step, 4 stacked layers (BASELINE configs[4])"},
 }
+HYBRID_NVFP4_EXPERTS = 64
 # NVFP4 dense tensor rate / bf16 dense tensor rate on B200 (9 / 2.25 PFLOP/s nominal):
 # the NVFP4 roofline is the measured cuBLAS bf16 rate scaled by this ratio.
 NVFP4_PER_BF16 = 4.0
@@ -208,6 +216,64 @@ def fc1_traffic_estimate(touched: int, world: int):
     return FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 * touched / world
 
 
+def exl3_layer_cpu(x16, route_experts, route_weights, tr, sc, H, I):
+    """CPU EXL3 experts for a token sample with the oracle's restated
+    Exl3Trellis::matmul_reference_f16 (crates/glm-format/src/exl3.rs:404-453):
+    gate and up on the fp16 token rows, h = fp16(silu(g) * u), down on h, routing-
+    weighted and summed in ascending expert order.  tr/sc: per-expert uint16 arrays."""
+    import numpy as np
+
+    import oracle as O
+    S, K = route_experts.shape
+    contrib = np.zeros((S, K, H), np.float32)
+    for e in np.unique(route_experts):
+        rows = [(t, k) for t in range(S) for k in range(K) if route_experts[t, k] == e]
+        xin = np.stack([x16[t] for t, _ in rows])
+        g = O.exl3_matmul_reference(tr["gate"][e], H, I, sc["gate_suh"][e], sc["gate_svh"][e], xin)
+        u = O.exl3_matmul_reference(tr["up"][e], H, I, sc["up_suh"][e], sc["up_svh"][e], xin)
+        gf = g.view(np.float16).astype(np.float32)
+        uf = u.view(np.float16).astype(np.float32)
+        h = (gf / (np.float32(1.0) + np.exp(-gf)) * uf).astype(np.float16).view(np.uint16)
+        d = O.exl3_matmul_reference(tr["down"][e], I, H, sc["down_suh"][e], sc["down_svh"][e], h)
+        df = d.view(np.float16).astype(np.float32)
+        for j, (t, k) in enumerate(rows):
+            contrib[t, k] = np.float32(route_weights[t, k]) * df[j]
+    out = np.zeros((S, H), np.float32)
+    for t in range(S):
+        order = np.argsort(route_experts[t], kind="stable")
+        acc = contrib[t, order[0]].copy()
+        for k in order[1:]:
+            acc = acc + contrib[t, k]
+        out[t] = acc
+    return out
+
+
+def cpu_baseline_exl3(layer, x, cfg, n_tokens: int):
+    """The EXL3 oracle composition timed on the host cores for a token sample
+    (per-call trellis decode, as the reference's CPU matmul does)."""
+    import numpy as np
+    T = x.shape[0]
+    S = min(n_tokens, T)
+    re, rw = layer.routes(T)
+    re = re.cpu().numpy().astype(np.int64)[:S]
+    rw = rw.cpu().numpy()[:S]
+    w = layer.w.exl3
+    used = np.unique(re)
+    tr = {n: {int(e): getattr(w, n + "_trellis")[int(e)].cpu().numpy().view(np.uint16)
+              for e in used} for n in ("gate", "up", "down")}
+    sc = {n: {int(e): getattr(w, n)[int(e)].cpu().numpy().view(np.uint16) for e in used}
+          for n in ("gate_suh", "gate_svh", "up_suh", "up_svh", "down_suh", "down_svh")}
+    xb = x[:S].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
+    x16 = (xb.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
+    import oracle as O
+    t0 = time.perf_counter()
+    exl3_layer_cpu(x16, re, rw, tr, sc, cfg.hidden, cfg.local_intermediate)
+    dt = time.perf_counter() - t0
+    return {"value": S / dt, "unit": UNIT, "cores": O.threads(), "kind": "port",
+            "sample": f"{S} of {T} tokens ({len(used)} experts), EXL3 gate/up/down per routed "
+                      f"expert with per-call trellis decode, {dt:.2f} s"}
+
+
 def torch_index(used):
     import torch
     return torch.as_tensor(used.astype("int64"))
@@ -223,7 +289,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from glmaxx_b200 import abi, synth
-    from glmaxx_b200.moe import MoEConfig, RoutedMoE
+    from glmaxx_b200.moe import MoEConfig, RoutedMoE, finish
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -243,33 +309,86 @@ def run_ours(args):
     if wl["zipf"]:
         # same beta on every rank: the fit is deterministic in (seed, router, input)
         zipf = synth.fit_zipf_beta(cfg, T, args.seed, dev)
-    weights = synth.make_rank_weights(cfg, seed=args.seed, device=dev,
-                                      zipf_beta=None if zipf is None else zipf[0])
+    beta = None if zipf is None else zipf[0]
+    codec = wl.get("codec")
+    n_layers = wl.get("layers", 1)
+    nvfp4_mask = None
+    if codec == "hybrid":
+        g = torch.Generator().manual_seed(args.seed * 13 + 1)
+        nvfp4_mask = torch.zeros(EXPERTS, dtype=torch.bool)
+        nvfp4_mask[torch.randperm(EXPERTS, generator=g)[:HYBRID_NVFP4_EXPERTS]] = True
+    layers = []
+    for li in range(n_layers):
+        seed = args.seed + 7919 * li
+        if codec == "exl3":
+            w = synth.make_exl3_rank_weights(cfg, seed=seed, device=dev, zipf_beta=beta)
+        elif codec == "hybrid":
+            w = synth.make_exl3_rank_weights(cfg, seed=seed, device=dev, zipf_beta=beta,
+                                             nvfp4_experts=nvfp4_mask)
+        else:
+            w = synth.make_rank_weights(cfg, seed=seed, device=dev, zipf_beta=beta)
+        layers.append(RoutedMoE(cfg, w, T))
+    layer = layers[0]
+    weights = layer.w
     x = synth.make_input(T, HIDDEN, seed=args.seed, device=dev)
-    layer = RoutedMoE(cfg, weights, T)
-    out = torch.empty((T, HIDDEN), dtype=torch.float32, device=dev)
+    # stack: rs[l] is the bf16 residual stream before layer l, xs[l] layer l's MoE
+    # input RMSNorm(rs[l]) (unit weight; layer 0 takes the unit-variance input as is)
+    xs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
+    rs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
+    outs = [torch.empty((T, HIDDEN), dtype=torch.float32, device=dev) for _ in range(n_layers)]
+    out = outs[-1]
     stream = torch.cuda.Stream(device=dev)
 
-    def reduce():
+    def reduce(o):
         if world > 1:
-            dist.all_reduce(out)
+            dist.all_reduce(o)
+
+    def layer_and_finish(li):
+        """layer li, and (stack) the finish that forms layer li+1's bf16 input."""
+        layers[li](xs[li], outs[li])
+
+    def finish_into_next(li):
+        if li + 1 < n_layers:
+            finish([outs[li]], rs[li], out_bf16=rs[li + 1], norm_bf16=xs[li + 1], hidden=HIDDEN)
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            layer(x, out)
-            reduce()
+            for li in range(n_layers):
+                layer_and_finish(li)
+                reduce(outs[li])
+                finish_into_next(li)
         stream.synchronize()
-        status = layer.device_status()
-        if status:
-            raise RuntimeError(f"device status after warm-up: {status}")
-        graph = torch.cuda.CUDAGraph(keep_graph=True)
-        with torch.cuda.graph(graph, stream=stream):
-            layer(x, out)
-        kernels_per_step = graph_kernel_nodes(graph)
-        graph.instantiate()
+        for lay in layers:
+            status = lay.device_status()
+            if status:
+                raise RuntimeError(f"device status after warm-up: {status}")
+        # one graph per layer (its routed step; the finish joins it when no collective
+        # sits between a layer and the next)
+        graphs = []
+        for li in range(n_layers):
+            gr = torch.cuda.CUDAGraph(keep_graph=True)
+            with torch.cuda.graph(gr, stream=stream):
+                layer_and_finish(li)
+                if world == 1:
+                    finish_into_next(li)
+            graphs.append(gr)
+        kernels_per_step = 0
+        for gr in graphs:
+            kn = graph_kernel_nodes(gr)
+            kernels_per_step = None if (kn is None or kernels_per_step is None) else \
+                kernels_per_step + kn
+            gr.instantiate()
+        graph = graphs[0]
+
+        def step():
+            for li in range(n_layers):
+                graphs[li].replay()
+                if world > 1:
+                    reduce(outs[li])
+                    finish_into_next(li)
+
         for _ in range(3):
-            graph.replay()
-            reduce()
+            step()
         stream.synchronize()
 
     uuid = None
@@ -288,8 +407,7 @@ def run_ours(args):
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(args.steps):
-            graph.replay()
-            reduce()
+            step()
         e1.record(stream)
     torch.cuda.synchronize()
     clock_info = clocks.stop()
@@ -333,8 +451,7 @@ def run_ours(args):
         e0.record(stream)
         for _ in range(args.steps):
             x_dev.copy_(x_host, non_blocking=True)
-            graph.replay()
-            reduce()
+            step()
             out_host.copy_(out, non_blocking=True)
         e1.record(stream)
     torch.cuda.synchronize()
@@ -356,7 +473,34 @@ def run_ours(args):
     layer_bytes = touched * (per["fc1"] + per["fc2"]) + shared_bytes + EXPERTS * HIDDEN * 2 + \
         T * HIDDEN * (2 + 4)
     fc1_ms = stage_avg["fc1"]
-    if wl["bound"] == "hbm":
+    exl3_expert_bytes = 3 * (HIDDEN * Ir * 3 // 8 + (HIDDEN + Ir) * 2)
+    if codec == "exl3":
+        # the EXL3 chain (rotations, decode-fused gate/up/down projections) runs in
+        # the fc1 stage: trellis + suh/svh bytes of every touched expert
+        ex_bytes = touched * exl3_expert_bytes
+        achieved = ex_bytes / (fc1_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "EXL3 decode-fused projections (gate, up, down)",
+                "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} HBM copy",
+                "traffic": None, "algorithmic_bytes_per_launch": ex_bytes,
+                "alu": {"decoded_weights_per_s": touched * 3 * HIDDEN * Ir / (fc1_ms * 1e-3),
+                        "note": "3INST trellis decode is ALU-bound: ~10 integer/fp16 ops per "
+                                "weight, fp32 multiply-then-add chains in the reference order"}}
+    elif codec == "hybrid":
+        layer_ms = ms / n_layers
+        nv_touched = int(torch.unique(re.long()[nvfp4_mask.to(re.device)[re.long()]]).numel())
+        ex_touched = touched - nv_touched
+        hy_bytes = nv_touched * (per["fc1"] + per["fc2"]) + ex_touched * exl3_expert_bytes + \
+            shared_bytes
+        achieved = hy_bytes / (layer_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "whole layer (NVFP4 + EXL3 experts, shared expert)",
+                "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} HBM copy",
+                "traffic": None, "algorithmic_bytes_per_layer": hy_bytes,
+                "layer_ms": layer_ms, "nvfp4_touched": nv_touched, "exl3_touched": ex_touched,
+                "nvfp4_rows": int(nvfp4_mask.to(re.device)[re.long()].sum()),
+                "exl3_rows": int((~nvfp4_mask.to(re.device)[re.long()]).sum())}
+    elif wl["bound"] == "hbm":
         # FC1 weights of every touched expert, the NVFP4 activation rows (values,
         # scales, global) and the bf16 SwiGLU output rows
         fc1_bytes = touched * per["fc1"] + A * (HIDDEN // 2 + HIDDEN // 16 + 4) + A * Ir * 2
@@ -392,7 +536,13 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline_from_device(layer, x, cfg, args.cpu_sample_tokens)
+            if codec == "exl3":
+                cpu = cpu_baseline_exl3(layer, x, cfg, args.cpu_sample_tokens)
+            elif codec == "hybrid":
+                cpu = {"value": None, "unit": UNIT,
+                       "note": "see the decode and exl3 workloads' baselines (per codec)"}
+            else:
+                cpu = cpu_baseline_from_device(layer, x, cfg, args.cpu_sample_tokens)
         except Exception as exc:  # noqa: BLE001
             cpu = {"value": None, "unit": UNIT, "error": repr(exc)[:200]}
 
@@ -439,6 +589,11 @@ def run_reference(args):
     import oracle as O
 
     wl = WORKLOADS[args.workload]
+    if wl.get("codec") == "hybrid":
+        print(json.dumps({"impl": "reference", "metric": wl["metric"], "unavailable":
+                          "the CPU arm times the per-codec workloads (decode, prefill, exl3); the "
+                          "hybrid stack has no separate CPU arm"}), flush=True)
+        return
     rng = np.random.default_rng(args.seed)
     T = args.tokens
     S = min(T, max(1, args.cpu_sample_tokens))
@@ -454,6 +609,50 @@ def run_reference(args):
     experts, weights = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
     used = np.unique(experts)
     remap = {int(e): i for i, e in enumerate(used)}
+    if wl.get("codec") == "exl3":
+        H, Ir = HIDDEN, INTER // world
+        words = O.exl3_trellis_words(H, Ir, 3)
+        tr = {n: {int(e): O.exl3_xorshift_trellis(args.seed * 1000 + 3 * int(e) + j, words)
+                  for e in used} for j, n in enumerate(("gate", "up", "down"))}
+
+        def signs(n, mag, salt):
+            r = np.random.default_rng(args.seed + salt)
+            return {int(e): np.where(r.random(n) < 0.5, -mag, mag).astype(np.float16)
+                    .view(np.uint16) for e in used}
+        mag = 0.02 / 1.2441
+        sc = {"gate_suh": signs(H, 1.0, 1), "gate_svh": signs(Ir, mag, 2),
+              "up_suh": signs(H, 1.0, 3), "up_svh": signs(Ir, mag, 4),
+              "down_suh": signs(Ir, 1.0, 5), "down_svh": signs(H, mag, 6)}
+        x16 = (x.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
+
+        def step():
+            t0 = time.perf_counter()
+            ex, wt = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
+            exl3_layer_cpu(x16, ex.astype(np.int64), wt, tr, sc, H, Ir)
+            return time.perf_counter() - t0
+        for _ in range(min(args.warmup, 1)):
+            step()
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < args.steps and (not times or
+                                           time.perf_counter() - t_start < REF_TIME_BUDGET_S):
+            times.append(step())
+        per_step = statistics.mean(times)
+        value = S / per_step
+        print(json.dumps({
+            "impl": "reference", "metric": wl["metric"], "value": value, "unit": UNIT,
+            "n_gpus": world, "steps": len(times), "steps_requested": args.steps,
+            "warmup": min(args.warmup, 1), "ms_per_step": per_step * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded trellis words, signs, N(0,1) activations)",
+            "config": {"workload": wl["name"], "tokens": T,
+                       "parallelism": f"tp{world} shard on one host process"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
+                             "sample": f"{S} tokens of {T} per step ({len(used)} experts), router"
+                                       " + EXL3 gate/up/down with per-call trellis decode"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
     v13, s13, g13, v2, s2, g2 = [], [], [], [], [], []
     for e in used:
         er = np.random.default_rng(args.seed * 1000 + int(e))

@@ -18,6 +18,7 @@ FC1_ABI_VERSION = 1
 FC2_ABI_VERSION = 1
 EXL3_ABI_VERSION = 1
 MOE_EXL3_ABI_VERSION = 1
+MOE_FINISH_ABI_VERSION = 1
 ROUTER_ABI_VERSION = 3
 MOE_LAYER_ABI_VERSION = 3
 DECODE_PERSISTENT = 1
@@ -129,6 +130,14 @@ class MoeLayerDescriptor(_Desc):
                             "sequence", "exl3_experts")] + [("reserved", u64 * 3)]
 
 
+class MoeFinishDescriptor(_Desc):
+    """glmaxx_moe_finish_descriptor (new), 112 bytes."""
+    _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "flags", "ranks")] + \
+        [(n, u64) for n in ("elements", "residual_f32", "residual_bf16", "attention_f32",
+                            "partials_f32", "output_f32", "output_bf16", "norm_bf16")] + \
+        [("hidden", u32), ("eps", f32), ("reserved", u64 * 3)]
+
+
 class MoeExl3Experts(_Desc):
     """glmaxx_moe_exl3_experts (new), 128 bytes."""
     _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "bits", "reserved0")] + \
@@ -138,7 +147,8 @@ class MoeExl3Experts(_Desc):
 
 
 EXPECTED_SIZES = {Fc1Descriptor: 224, Fc2Descriptor: 224, Exl3Descriptor: 144,
-                  RouterDescriptor: 192, MoeLayerDescriptor: 240, MoeExl3Experts: 128}
+                  RouterDescriptor: 192, MoeLayerDescriptor: 240, MoeExl3Experts: 128,
+                  MoeFinishDescriptor: 112}
 
 _P = ctypes.c_void_p
 _I32P = ctypes.POINTER(ctypes.c_int32)
@@ -166,6 +176,7 @@ SIGNATURES = {
     "glmaxx_nvfp4_fc2_dense_control_launch": (ctypes.c_int32, [_P, u32, _P, _I32P]),
     "glmaxx_nvfp4_fc2_grouped_control_launch": (ctypes.c_int32, [_P, _U16P, u32, _P, _I32P]),
     "glmaxx_exl3_projection_launch": (ctypes.c_int32, [_P, _P, _I32P]),
+    "glmaxx_moe_finish_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_exl3_gemv_launch": (ctypes.c_int32, [u64, u64, u32, u32, u32, u32, u64, _P]),
     "glmaxx_graph_exec_launch": (ctypes.c_int32, [u64, u64]),
     "glmaxx_graph_exec_destroy": (ctypes.c_int32, [u64]),

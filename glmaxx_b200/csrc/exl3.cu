@@ -117,12 +117,18 @@ struct Exl3GemvArgs {
 
 template <int RB>
 __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
-  __shared__ __align__(16) uint16_t ws[16][32 + 2];      // decoded 16 k x 32 columns
+  // decoded 16 k x 32 columns, column-major (column c's 16 k values contiguous);
+  // 40-half pitch keeps the 16-byte column reads and the 4-byte row-pair writes
+  // of a warp on distinct banks
+  constexpr int kPitch = 40;
+  __shared__ __align__(16) uint16_t ws[32 * kPitch];
   __shared__ __align__(16) float xs[RB][kExl3KChunk];    // x of this item's rows
   const uint32_t lane = threadIdx.x;
   const Exl3LaneWindow lw = exl3_lane_window(lane);
   const uint32_t c0 = blockIdx.x * 32;                   // first column of this warp
   const uint32_t nt0 = c0 / 16;                          // first tile column
+  const uint32_t lcb = 2 * ((lane >> 3) & 3) + ((lane >> 2) & 1);
+  const uint32_t lrb = 2 * (lane & 3);
   const bool listed = a.group_rows != nullptr;
   const uint32_t count = listed ? *a.n_items : (a.implicit_rows + RB - 1) / RB;
   for (uint32_t it = blockIdx.y; it < count; it += gridDim.y) {
@@ -157,23 +163,46 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
           exl3_load_span(tile_ptr(kc + k16 + 16, 0), lw, span[0]);
           exl3_load_span(tile_ptr(kc + k16 + 16, 1), lw, span[1]);
         }
-        const uint32_t lcb = 2 * ((lane >> 3) & 3) + ((lane >> 2) & 1);
-        const uint32_t lrb = 2 * (lane & 3);
+        // weights w and w+1 are rows lr, lr+1 of one column: one 4-byte store
 #pragma unroll
         for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            const uint32_t lr = lrb + (w & 1) + 8 * ((w >> 1) & 1);
+          for (int w = 0; w < 8; w += 2) {
+            const uint32_t lr = lrb + 8 * ((w >> 1) & 1);
             const uint32_t lc = lcb + 8 * ((w >> 2) & 1);
-            ws[lr][16 * j + lc] = w16[j][w];
+            *reinterpret_cast<uint32_t*>(&ws[(16 * j + lc) * kPitch + lr]) =
+                uint32_t(w16[j][w]) | (uint32_t(w16[j][w + 1]) << 16);
           }
         __syncwarp();
+        const uint4 c01 = *reinterpret_cast<const uint4*>(&ws[lane * kPitch]);
+        const uint4 c23 = *reinterpret_cast<const uint4*>(&ws[lane * kPitch + 8]);
+        const uint32_t cw[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
+        float wf[16];
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
-          const float wf = h2f(ws[kk][lane]);
+        for (int q = 0; q < 8; ++q) {
+          wf[2 * q] = h2f(uint16_t(cw[q] & 0xffffu));
+          wf[2 * q + 1] = h2f(uint16_t(cw[q] >> 16));
+        }
+        if (RB == 1 || nr == 1) {
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[0][k16 + 4 * k4]);
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.x, wf[4 * k4]));
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.y, wf[4 * k4 + 1]));
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.z, wf[4 * k4 + 2]));
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.w, wf[4 * k4 + 3]));
+          }
+        } else {
 #pragma unroll
           for (int r = 0; r < RB; ++r)
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(xs[r][k16 + kk], wf));
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              const float4 xv = *reinterpret_cast<const float4*>(&xs[r][k16 + 4 * k4]);
+              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.x, wf[4 * k4]));
+              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.y, wf[4 * k4 + 1]));
+              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.z, wf[4 * k4 + 2]));
+              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.w, wf[4 * k4 + 3]));
+            }
         }
         __syncwarp();
       }

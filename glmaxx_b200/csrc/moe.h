@@ -101,6 +101,21 @@ struct Fc2QuantArgs {
   uint32_t E;
 };
 
+struct FinishArgs {
+  const float* residual_f32;
+  const uint16_t* residual_bf16;
+  const float* attention_f32;  // [ranks][elements] or null
+  const float* partials[8];    // rank order
+  float* output_f32;
+  uint16_t* output_bf16;
+  uint16_t* norm_bf16;         // optional row-wise RMSNorm output
+  uint64_t elements;           // multiple of 4
+  uint32_t ranks;
+  uint32_t hidden;             // row length (norm_bf16)
+  float eps;
+};
+cudaError_t launch_finish(const FinishArgs& a, cudaStream_t stream);
+
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
                                  uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,
                                  cudaStream_t stream);

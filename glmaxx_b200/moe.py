@@ -222,3 +222,25 @@ class RoutedMoE:
 
     def routes(self, tokens: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.route_experts[:tokens], self.route_weights[:tokens]
+
+
+def finish(partials: list[torch.Tensor], residual: torch.Tensor,
+           attention: torch.Tensor | None = None, out_f32: torch.Tensor | None = None,
+           out_bf16: torch.Tensor | None = None, norm_bf16: torch.Tensor | None = None,
+           hidden: int = 0, eps: float = 1e-6) -> None:
+    """Sparse-layer finish (glmaxx_moe_finish_launch, finish_sparse_layer_oracle
+    order): residual (fp32 or bf16) + attention[r] for each rank + partials[r] for
+    each rank, in rank order, into out_f32 and/or out_bf16, and optionally the
+    row-wise RMSNorm (rows of `hidden`) of the result into norm_bf16, on the
+    current stream."""
+    n = residual.numel()
+    ptrs = (ctypes.c_uint64 * len(partials))(*[p.data_ptr() for p in partials])
+    d = abi.MoeFinishDescriptor.new(
+        abi_version=abi.MOE_FINISH_ABI_VERSION, ranks=len(partials), elements=n,
+        residual_f32=residual.data_ptr() if residual.dtype == torch.float32 else 0,
+        residual_bf16=residual.data_ptr() if residual.dtype == torch.bfloat16 else 0,
+        attention_f32=_ptr(attention), partials_f32=ctypes.addressof(ptrs),
+        output_f32=_ptr(out_f32), output_bf16=_ptr(out_bf16), norm_bf16=_ptr(norm_bf16),
+        hidden=hidden, eps=eps)
+    abi.check(abi.load().glmaxx_moe_finish_launch(ctypes.byref(d), ctypes.c_void_p(_stream())),
+              "moe_finish_launch")

@@ -68,8 +68,11 @@ def make_shared(cfg: MoEConfig, seed: int, device):
 
 
 def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | None = None,
-                      expert_chunk: int = 8, keep_masters: bool = False):
-    """Router (replicated), NVFP4 expert shards and bf16 shared shard of rank cfg.rank."""
+                      expert_chunk: int = 8, keep_masters: bool = False,
+                      only_experts: torch.Tensor | None = None):
+    """Router (replicated), NVFP4 expert shards and bf16 shared shard of rank cfg.rank.
+    only_experts (bool [E]): generate and pack only those experts; the others are
+    all-zero NVFP4 tensors (global scale 1), for layers that never route to them."""
     E, H, I, Ir, r = cfg.experts, cfg.hidden, cfg.intermediate, cfg.local_intermediate, cfg.rank
     router_w, bias = make_router(cfg, seed, device, zipf_beta)
     w13_parts, w2_parts = [], []
@@ -79,6 +82,10 @@ def make_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: float | N
         g13 = torch.empty((ne, 2 * Ir, H), dtype=torch.float32, device=device)
         g2 = torch.empty((ne, H, Ir), dtype=torch.float32, device=device)
         for j in range(ne):
+            if only_experts is not None and not bool(only_experts[e0 + j]):
+                g13[j].zero_()
+                g2[j].zero_()
+                continue
             gen = _gen(device, seed * 1000003 + 17 * (e0 + j) + 3)
             full13 = torch.randn(2 * I, H, generator=gen, device=device) * 0.02
             full2 = torch.randn(H, I, generator=gen, device=device) * 0.02
@@ -199,7 +206,7 @@ def make_exl3_rank_weights(cfg: MoEConfig, seed: int, device, *, zipf_beta: floa
         shared13, shared2 = make_shared(cfg, seed, device)
         return RankWeights(router_w.contiguous(), bias.contiguous(), None, None, shared13,
                            shared2, make_exl3_experts(cfg, seed, device))
-    w = make_rank_weights(cfg, seed, device, zipf_beta=zipf_beta)
+    w = make_rank_weights(cfg, seed, device, zipf_beta=zipf_beta, only_experts=nvfp4_experts)
     codec = (~nvfp4_experts.to(device)).to(torch.uint8)
     w.exl3 = make_exl3_experts(cfg, seed, device, codec=codec)
     return w

@@ -46,6 +46,7 @@ enum {
   GLMAXX_ROUTER_ABI_VERSION = 3,
   GLMAXX_MOE_LAYER_ABI_VERSION = 3,
   GLMAXX_MOE_EXL3_ABI_VERSION = 1,
+  GLMAXX_MOE_FINISH_ABI_VERSION = 1,
   GLMAXX_FC1_DECODE_PERSISTENT = 1,
   GLMAXX_FC1_PREFILL_GROUPED = 2,
   GLMAXX_EXL3_GATE = 1,
@@ -317,6 +318,42 @@ struct glmaxx_moe_layer_descriptor {
   uint64_t reserved[3];
 };
 
+/*
+ * Sparse-layer finish (new; finish_sparse_layer_oracle, crates/glm-reference/src/
+ * routed_fc2.rs:214-258): output[i] = residual[i], then += attention[r][i] for
+ * r = 0..ranks-1, then += partial_r[i] (each rank's routed + shared partial, the
+ * output of glmaxx_moe_layer_launch) for r = 0..ranks-1, in fp32 and in that
+ * order, so the result is the same bit for bit whatever launch does it.
+ * partials_f32 is the host address of an array of `ranks` device pointers
+ * (rank order; other GPUs' buffers when peer access is enabled).  The residual
+ * is fp32 or bf16 (exactly one given); outputs fp32 and/or bf16 (round to
+ * nearest even).  ranks 1..8.  The row-wise RMSNorm output (not in the reference,
+ * which stops at the residual) feeds the next layer of a stacked benchmark.
+ */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_moe_finish_descriptor {
+#else
+struct glmaxx_moe_finish_descriptor {
+#endif
+  uint32_t abi_version; /* GLMAXX_MOE_FINISH_ABI_VERSION */
+  uint32_t struct_bytes;
+  uint32_t flags;
+  uint32_t ranks;
+  uint64_t elements;
+  uint64_t residual_f32;
+  uint64_t residual_bf16;
+  uint64_t attention_f32;
+  uint64_t partials_f32;
+  uint64_t output_f32;
+  uint64_t output_bf16;
+  /* optional: the next layer's MoE input, bf16(o / sqrt(mean(o^2) + eps)) over each
+   * row of `hidden` elements of the fp32 result o (RMSNorm with unit weight) */
+  uint64_t norm_bf16;
+  uint32_t hidden;
+  float eps;
+  uint64_t reserved[3];
+};
+
 /* ---- reference entry points (glmaxx_kernel.h:123-250) ---- */
 int32_t glmaxx_nvfp4_routed_fc1_launch(const struct glmaxx_fc1_descriptor* descriptor,
                                        void* cuda_stream, int32_t* asynchronous_error);
@@ -457,6 +494,8 @@ int32_t glmaxx_router_compact_launch_static(const struct glmaxx_router_descripto
                                             void* cuda_stream, int32_t* asynchronous_error);
 int32_t glmaxx_moe_layer_launch(const struct glmaxx_moe_layer_descriptor* descriptor,
                                 void* cuda_stream, int32_t* asynchronous_error);
+int32_t glmaxx_moe_finish_launch(const struct glmaxx_moe_finish_descriptor* descriptor,
+                                 void* cuda_stream);
 
 /* Profiling (the CUDA-event timing of the reference, crates/glm-cuda/src/
  * ffi.rs:3057-3079, per stage): while set, layer launches on the calling
@@ -515,6 +554,7 @@ static_assert(alignof(glmaxx_exl3_descriptor) == 16, "Rust/C EXL3 descriptor ali
 static_assert(sizeof(glmaxx_router_descriptor) == 192, "router descriptor size");
 static_assert(sizeof(glmaxx_moe_layer_descriptor) == 240, "layer descriptor size");
 static_assert(sizeof(glmaxx_moe_exl3_experts) == 128, "EXL3 experts descriptor size");
+static_assert(sizeof(glmaxx_moe_finish_descriptor) == 112, "finish descriptor size");
 #endif
 
 #endif /* GLMAXX_KERNEL_H_ */
