@@ -207,7 +207,7 @@ def cpu_baseline_from_device(layer, x, cfg, n_tokens: int):
 # of the decode FC1 at 64 experts, T=64, TP1, divided by the touched experts of that
 # capture; FC1 traffic grows with the touched experts (weights dominate), so a
 # full launch is estimated as this figure x touched experts.
-FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 = None
+FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 = (911.565824e6 + 6.625024e6) / 64
 
 
 def fc1_traffic_estimate(touched: int, world: int):
