@@ -14,6 +14,8 @@
 
 #include "../../include/glmaxx_kernel.h"
 #include "device.cuh"
+#include "exl3.cuh"
+#include "moe.h"
 #include "runtime.h"
 
 namespace glmaxx {
@@ -58,49 +60,7 @@ __global__ void exl3_rotate_in(const uint16_t* __restrict__ x, const uint16_t* _
 // extends the chains of its column for RB rows.  Work items are (group = one
 // weight matrix, block of RB rows of that group).
 // ---------------------------------------------------------------------------
-constexpr uint32_t kExl3Bits = 3;
-constexpr uint32_t kExl3TileHalves = 16 * kExl3Bits;  // 48 halves = 24 words per 16x16 tile
 constexpr uint32_t kExl3KChunk = 256;                  // x staged per 256 k
-
-// Bit position (MSB-first stream order) of lane `lane`'s first window inside
-// the tile's 768-bit circular stream: weight i of the tile uses the 16 bits
-// ending at bit (i + 257) * 3 (exl3.rs:490-513), and lane l owns i = 8l .. 8l+7,
-// so its 8 windows lie in 37 consecutive bits starting at (8l + 257) * 3 - 16.
-struct Exl3LaneWindow {
-  uint32_t word0;  // first 32-bit word (mod 24) holding the span
-  uint32_t off;    // bit offset of the span inside that word (0 = MSB)
-};
-__device__ __forceinline__ Exl3LaneWindow exl3_lane_window(uint32_t lane) {
-  const uint32_t start = (lane * 8 + 257) * kExl3Bits - 16;
-  return {start / 32, start % 32};
-}
-
-// The three words of a tile that hold lane's span (halves base[0..47] are
-// words (h0 | h1 << 16), the stream wraps after 24 words).
-__device__ __forceinline__ void exl3_load_span(const uint16_t* __restrict__ base,
-                                               Exl3LaneWindow lw, uint32_t (&wd)[3]) {
-  constexpr uint32_t kTileWords = 8 * kExl3Bits;
-  const uint32_t* base32 = reinterpret_cast<const uint32_t*>(base);
-#pragma unroll
-  for (int j = 0; j < 3; ++j) wd[j] = __ldg(base32 + (lw.word0 + j) % kTileWords);
-}
-
-// 3INST decode of the 8 windows in the span: value = window * 0xCBAC1FED,
-// (value & 0x8FFF8FFF) ^ 0x3B603B60 read as two fp16 halves, summed.  Both halves
-// have exponent fields 12..15, so their exact sum fits fp32 and the fp16 add
-// rounds it once, exactly as fp16(f32(lo) + f32(hi)) of the reference.
-__device__ __forceinline__ void exl3_decode_span(const uint32_t (&wd)[3], uint32_t off,
-                                                 uint16_t (&w16)[8]) {
-  const uint64_t v = (uint64_t(wd[0]) << 32) | wd[1];
-  const uint64_t span = off ? ((v << off) | (wd[2] >> (32 - off))) : v;  // bit 63 = span start
-#pragma unroll
-  for (int w = 0; w < 8; ++w) {
-    const uint32_t window = uint32_t(span >> (48 - 3 * w)) & 0xffffu;
-    const uint32_t packed = ((window * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
-    const __half2 h = *reinterpret_cast<const __half2*>(&packed);
-    w16[w] = __half_as_ushort(__hadd(__low2half(h), __high2half(h)));
-  }
-}
 
 struct Exl3GemvArgs {
   const uint16_t* x;             // [rows][K] f16, row r of group g at x + r*K
@@ -217,7 +177,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
 // whose codec is EXL3 (codec == null: every group); single CTA.  Item order
 // does not affect results (every item computes its own outputs).
 __global__ void exl3_items_kernel(const uint32_t* __restrict__ group_rows, uint32_t groups,
-                                  const uint8_t* __restrict__ codec, uint32_t rb,
+                                  const uint8_t* __restrict__ codec, uint32_t rb, uint32_t max_rows,
                                   uint32_t* __restrict__ items, uint32_t* __restrict__ n_items) {
   __shared__ uint32_t base;
   if (threadIdx.x == 0) base = 0;
@@ -226,6 +186,7 @@ __global__ void exl3_items_kernel(const uint32_t* __restrict__ group_rows, uint3
     const uint32_t g = g0 + threadIdx.x;
     uint32_t rows = g < groups ? group_rows[g + 1] - group_rows[g] : 0;
     if (codec != nullptr && g < groups && codec[g] != 1) rows = 0;
+    if (max_rows != 0 && rows >= max_rows) rows = 0;  // left to the tensor-core path
     const uint32_t nb = (rows + rb - 1) / rb;
     const uint32_t off = nb ? atomicAdd(&base, nb) : 0;
     for (uint32_t b = 0; b < nb; ++b) items[off + b] = (g << 16) | b;
@@ -270,60 +231,119 @@ __device__ __forceinline__ int exl3_row_expert(const Exl3RowMap& m, uint32_t r) 
   return static_cast<int>(lo);
 }
 
+// H128 of one 128-element block held by a warp (lane owns elements lane + 32j,
+// j = 0..3), times 1/sqrt(128).  exact: each output is the reference's
+// ascending-column sum of +-input (exl3.rs:515-531), from the block staged in
+// `blk`; otherwise a fast Walsh-Hadamard transform (same Sylvester matrix,
+// butterflies through shuffles), for rows whose projection is not bit-exact
+// anyway (the tensor-core path).
+__device__ __forceinline__ void exl3_h128_warp(float (&v)[4], bool exact, float* blk,
+                                               uint32_t lane) {
+  const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
+  if (exact) {
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) blk[lane + 32 * j] = v[j];
+    __syncwarp();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t c = 0; c < 128; ++c) {
+      const float x = blk[c];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t i = lane + 32 * j;
+        acc[j] = __fadd_rn(acc[j], (__popc(i & c) & 1) ? -x : x);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(acc[j], norm);
+    return;
+  }
+#pragma unroll
+  for (uint32_t h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float o = __shfl_xor_sync(0xffffffffu, v[j], h);
+      v[j] = (lane & h) ? __fsub_rn(o, v[j]) : __fadd_rn(v[j], o);
+    }
+  }
+  // h = 32 and 64: partners in the lane's own registers (j bit 0 and bit 1)
+  float w0 = __fadd_rn(v[0], v[1]), w1 = __fsub_rn(v[0], v[1]);
+  float w2 = __fadd_rn(v[2], v[3]), w3 = __fsub_rn(v[2], v[3]);
+  v[0] = __fmul_rn(__fadd_rn(w0, w2), norm);
+  v[1] = __fmul_rn(__fadd_rn(w1, w3), norm);
+  v[2] = __fmul_rn(__fsub_rn(w0, w2), norm);
+  v[3] = __fmul_rn(__fsub_rn(w1, w3), norm);
+}
+
+// True when expert e's rows use the exact (reference-order) projection chain.
+__device__ __forceinline__ bool exl3_exact_rows(const Exl3RowMap& m, int e, uint32_t tc_min_rows) {
+  return tc_min_rows == 0 || m.offsets[e + 1] - m.offsets[e] < tc_min_rows;
+}
+
 // Input rotation (exl3.rs:404-453 steps 1-2): out[r][k] = f16(H128(f16(x[r][k] *
 // suh[e][k]))).  x is either the bf16 token row row_token[r] of the layer
-// input (converted to fp16 first) or the fp16 row r of `src`.
-__global__ void exl3_rows_rotate_in(Exl3RowMap m, const uint16_t* __restrict__ x_bf16,
-                                    const uint32_t* __restrict__ row_token,
-                                    const uint16_t* __restrict__ src_f16,
-                                    const uint16_t* __restrict__ suh, uint32_t K,
-                                    uint16_t* __restrict__ out) {
-  __shared__ float blk[128];
+// input (converted to fp16 first) or the fp16 row r of `src`.  One CTA per
+// row, 8 warps over its 128-blocks.
+__global__ void __launch_bounds__(256) exl3_rows_rotate_in(
+    Exl3RowMap m, const uint16_t* __restrict__ x_bf16, const uint32_t* __restrict__ row_token,
+    const uint16_t* __restrict__ src_f16, const uint16_t* __restrict__ suh, uint32_t K,
+    uint16_t* __restrict__ out, uint32_t tc_min_rows) {
+  __shared__ float blk[8][128];
   __shared__ int s_e;
-  const uint32_t r = blockIdx.y, b = blockIdx.x, i = threadIdx.x;
-  if (i == 0) s_e = exl3_row_expert(m, r);
+  const uint32_t r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) s_e = exl3_row_expert(m, r);
   __syncthreads();
   const int e = s_e;
   if (e < 0) return;
-  const uint32_t k = b * 128 + i;
-  float xv;
-  if (x_bf16 != nullptr) {
-    const uint16_t bits = x_bf16[uint64_t(row_token[r]) * K + k];
-    xv = h2f(f2h(__uint_as_float(uint32_t(bits) << 16)));
-  } else {
-    xv = h2f(src_f16[uint64_t(r) * K + k]);
+  const bool exact = exl3_exact_rows(m, e, tc_min_rows);
+  const uint64_t xrow = x_bf16 != nullptr ? uint64_t(row_token[r]) * K : uint64_t(r) * K;
+  for (uint32_t b = warp; b < K / 128; b += 8) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t k = b * 128 + lane + 32 * j;
+      const float xv = x_bf16 != nullptr ? h2f(f2h(__uint_as_float(uint32_t(x_bf16[xrow + k]) << 16)))
+                                         : h2f(src_f16[xrow + k]);
+      v[j] = h2f(f2h(__fmul_rn(xv, h2f(suh[uint64_t(e) * K + k]))));
+    }
+    exl3_h128_warp(v, exact, blk[warp], lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[uint64_t(r) * K + b * 128 + lane + 32 * j] = f2h(v[j]);
   }
-  blk[i] = h2f(f2h(__fmul_rn(xv, h2f(suh[uint64_t(e) * K + k]))));
-  __syncthreads();
-  const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-  out[uint64_t(r) * K + k] = f2h(hadamard_row(blk, i, norm));
 }
 
 // Output rotation (steps 4-5): y = f16(H128(p) * svh[e]).  With `plane` set the
 // routing-weighted fp32 value w * y goes to plane[token][slot][n] (the operand
 // of the expert-order combine); otherwise y replaces p in place.
-__global__ void exl3_rows_rotate_out(Exl3RowMap m, uint16_t* __restrict__ p,
-                                     const uint16_t* __restrict__ svh, uint32_t N,
-                                     float* __restrict__ plane, const uint32_t* __restrict__ row_token,
-                                     const uint32_t* __restrict__ row_slot,
-                                     const float* __restrict__ row_weight, uint32_t top_k) {
-  __shared__ float blk[128];
+__global__ void __launch_bounds__(256) exl3_rows_rotate_out(
+    Exl3RowMap m, uint16_t* __restrict__ p, const uint16_t* __restrict__ svh, uint32_t N,
+    float* __restrict__ plane, const uint32_t* __restrict__ row_token,
+    const uint32_t* __restrict__ row_slot, const float* __restrict__ row_weight, uint32_t top_k,
+    uint32_t tc_min_rows) {
+  __shared__ float blk[8][128];
   __shared__ int s_e;
-  const uint32_t r = blockIdx.y, b = blockIdx.x, i = threadIdx.x;
-  if (i == 0) s_e = exl3_row_expert(m, r);
+  const uint32_t r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) s_e = exl3_row_expert(m, r);
   __syncthreads();
   const int e = s_e;
   if (e < 0) return;
-  const uint32_t n = b * 128 + i;
-  blk[i] = h2f(p[uint64_t(r) * N + n]);
-  __syncthreads();
-  const float norm = __fdiv_rn(1.0f, __fsqrt_rn(128.0f));
-  const uint16_t y = f2h(__fmul_rn(hadamard_row(blk, i, norm), h2f(svh[uint64_t(e) * N + n])));
-  if (plane != nullptr) {
-    const uint64_t dst = uint64_t(row_token[r]) * top_k + row_slot[r];
-    plane[dst * N + n] = __fmul_rn(row_weight[r], h2f(y));
-  } else {
-    p[uint64_t(r) * N + n] = y;
+  const bool exact = exl3_exact_rows(m, e, tc_min_rows);
+  const uint64_t dst = plane != nullptr ? uint64_t(row_token[r]) * top_k + row_slot[r] : 0;
+  const float wgt = plane != nullptr ? row_weight[r] : 0.f;
+  for (uint32_t b = warp; b < N / 128; b += 8) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = h2f(p[uint64_t(r) * N + b * 128 + lane + 32 * j]);
+    exl3_h128_warp(v, exact, blk[warp], lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t n = b * 128 + lane + 32 * j;
+      const uint16_t y = f2h(__fmul_rn(v[j], h2f(svh[uint64_t(e) * N + n])));
+      if (plane != nullptr)
+        plane[dst * N + n] = __fmul_rn(wgt, h2f(y));
+      else
+        p[uint64_t(r) * N + n] = y;
+    }
   }
 }
 
@@ -375,10 +395,11 @@ cudaError_t launch_exl3_gemv_single(const uint16_t* x, const uint16_t* trellis, 
 }
 
 cudaError_t launch_exl3_items(const uint32_t* group_rows, uint32_t groups, const uint8_t* codec,
-                              uint32_t* items, uint32_t* n_items, cudaStream_t stream) {
+                              uint32_t max_rows, uint32_t* items, uint32_t* n_items,
+                              cudaStream_t stream) {
   if (groups >= 65536) return cudaErrorInvalidValue;
-  exl3_items_kernel<<<1, 256, 0, stream>>>(group_rows, groups, codec, kExl3GroupRowBlock, items,
-                                           n_items);
+  exl3_items_kernel<<<1, 256, 0, stream>>>(group_rows, groups, codec, kExl3GroupRowBlock,
+                                           max_rows, items, n_items);
   return cudaPeekAtLastError();
 }
 
@@ -402,9 +423,15 @@ cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
   return run_exl3_gemv<kExl3GroupRowBlock>(a, max_items, stream);
 }
 
+// Experts with at least this many rows take the tensor-core projection
+// (exl3_gemm.cu); the others the bit-exact decode-fused GEMV.
+constexpr uint32_t kExl3TcMinRows = 8;
+
 uint64_t exl3_experts_workspace_bytes(uint32_t A, uint32_t H, uint32_t I, uint32_t E) {
   const uint64_t wide = H > I ? H : I;
-  return 4 * uint64_t(A) * wide * 2 + uint64_t(A) * I * 2 + (uint64_t(E) + A + 2) * 4 + 6 * 256;
+  const uint64_t max_tiles = (uint64_t(A) + 127) / 128 + E;
+  return 4 * uint64_t(A) * wide * 2 + uint64_t(A) * I * 2 + (uint64_t(E) + A + 2) * 4 +
+         max_tiles * sizeof(NTile) + 16 + 9 * 256;
 }
 
 cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& L, cudaStream_t stream) {
@@ -425,6 +452,9 @@ cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& L, cudaStream_t stream)
   uint16_t* h = reinterpret_cast<uint16_t*>(take(uint64_t(A) * I * 2));
   uint32_t* n_items = reinterpret_cast<uint32_t*>(take(16));
   uint32_t* items = reinterpret_cast<uint32_t*>(take((uint64_t(L.E) + A) * 4));
+  const uint64_t max_tiles = (uint64_t(A) + 127) / 128 + L.E;
+  NTile* tc_tiles = reinterpret_cast<NTile*>(take(max_tiles * sizeof(NTile)));
+  uint32_t* tc_count = reinterpret_cast<uint32_t*>(take(16));
   const uint32_t max_items = L.E + (A + kExl3GroupRowBlock - 1) / kExl3GroupRowBlock;
   Exl3RowMap m{L.offsets, L.codec, L.E};
   const uint64_t gate_stride = uint64_t(H) * I * kExl3Bits / 16;  // halves per expert
@@ -433,33 +463,37 @@ cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& L, cudaStream_t stream)
     cudaError_t _st = (expr);                 \
     if (_st != cudaSuccess) return _st;       \
   } while (0)
-  X3(launch_exl3_items(L.offsets, L.E, L.codec, items, n_items, stream));
+  X3(launch_exl3_items(L.offsets, L.E, L.codec, kExl3TcMinRows, items, n_items, stream));
+  X3(launch_exl3_tc_tiles(L.offsets, L.E, L.codec, kExl3TcMinRows, tc_tiles, tc_count, stream));
   // gate / up: rotate the token rows with each projection's suh, project, rotate out
   for (int proj = 0; proj < 2; ++proj) {
     const uint16_t* suh = proj ? L.up_suh : L.gate_suh;
     const uint16_t* svh = proj ? L.up_svh : L.gate_svh;
     const uint16_t* tr = proj ? L.up_trellis : L.gate_trellis;
     uint16_t* pout = proj ? p1 : p0;
-    exl3_rows_rotate_in<<<dim3(H / 128, A), 128, 0, stream>>>(m, L.x_bf16, L.row_token, nullptr,
-                                                               suh, H, xr);
+    exl3_rows_rotate_in<<<A, 256, 0, stream>>>(m, L.x_bf16, L.row_token, nullptr, suh, H, xr,
+                                                kExl3TcMinRows);
     X3(cudaPeekAtLastError());
     X3(launch_exl3_gemv_grouped(xr, tr, gate_stride, L.offsets, max_items, items, n_items, H, I,
                                 pout, stream));
-    exl3_rows_rotate_out<<<dim3(I / 128, A), 128, 0, stream>>>(m, pout, svh, I, nullptr, nullptr,
-                                                                nullptr, nullptr, 0);
+    X3(launch_exl3_tc(xr, A, H, tr, gate_stride, tc_tiles, tc_count, I, pout, L.status, L.num_sms,
+                      stream));
+    exl3_rows_rotate_out<<<A, 256, 0, stream>>>(m, pout, svh, I, nullptr, nullptr, nullptr,
+                                                 nullptr, 0, kExl3TcMinRows);
     X3(cudaPeekAtLastError());
   }
   exl3_rows_swiglu<<<dim3((I + 255) / 256, A), 256, 0, stream>>>(m, p0, p1, I, h);
   X3(cudaPeekAtLastError());
   // down: rotate h, project to hidden, rotate out into the weighted plane
-  exl3_rows_rotate_in<<<dim3(I / 128, A), 128, 0, stream>>>(m, nullptr, nullptr, h, L.down_suh, I,
-                                                             xr);
+  exl3_rows_rotate_in<<<A, 256, 0, stream>>>(m, nullptr, nullptr, h, L.down_suh, I, xr,
+                                              kExl3TcMinRows);
   X3(cudaPeekAtLastError());
   X3(launch_exl3_gemv_grouped(xr, L.down_trellis, gate_stride, L.offsets, max_items, items,
                               n_items, I, H, p2, stream));
-  exl3_rows_rotate_out<<<dim3(H / 128, A), 128, 0, stream>>>(m, p2, L.down_svh, H, L.plane,
-                                                              L.row_token, L.row_slot,
-                                                              L.row_weight, L.top_k);
+  X3(launch_exl3_tc(xr, A, I, L.down_trellis, gate_stride, tc_tiles, tc_count, H, p2, L.status,
+                    L.num_sms, stream));
+  exl3_rows_rotate_out<<<A, 256, 0, stream>>>(m, p2, L.down_svh, H, L.plane, L.row_token,
+                                               L.row_slot, L.row_weight, L.top_k, kExl3TcMinRows);
   X3(cudaPeekAtLastError());
 #undef X3
   return cudaSuccess;

@@ -348,6 +348,8 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     L.down_svh = reinterpret_cast<const uint16_t*>(xe->down_svh_f16);
     L.plane = at<float>(ws, p.plane);
     L.workspace = at<void>(ws, p.exl3_ws);
+    L.status = status;
+    L.num_sms = info.sms;
     CHECK(launch_exl3_experts(L, stream));
   }
   if (p.nvfp4) {

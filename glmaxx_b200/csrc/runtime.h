@@ -59,8 +59,19 @@ struct Exl3ExpertsLaunch {
   const uint16_t *gate_suh, *gate_svh, *up_suh, *up_svh, *down_suh, *down_svh;
   float* plane;                // [T][top_k][H]
   void* workspace;             // exl3_experts_workspace_bytes
+  uint32_t* status;            // device status word
+  int num_sms;
 };
 uint64_t exl3_experts_workspace_bytes(uint32_t A, uint32_t H, uint32_t I, uint32_t E);
+struct NTile;  // grouped-GEMM tile descriptor (gemm.cuh)
+// Tensor-core EXL3 projection (exl3_gemm.cu) of the experts with many rows.
+cudaError_t launch_exl3_tc_tiles(const uint32_t* offsets, uint32_t E, const uint8_t* codec,
+                                 uint32_t min_rows, NTile* tiles, uint32_t* tile_count,
+                                 cudaStream_t stream);
+cudaError_t launch_exl3_tc(const uint16_t* x, uint32_t x_rows, uint32_t K, const uint16_t* trellis,
+                           uint64_t trellis_stride, const NTile* tiles, const uint32_t* tile_count,
+                           uint32_t Nproj, uint16_t* out, uint32_t* status, int num_sms,
+                           cudaStream_t stream);
 cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& launch, cudaStream_t stream);
 
 }  // namespace glmaxx

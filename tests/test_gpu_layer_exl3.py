@@ -22,6 +22,9 @@ from gpu_util import assert_layer_close, cuda, rel_l2, to_np_bf16_bits
 
 pytestmark = pytest.mark.gpu
 
+# experts with at least this many rows use the tensor-core projection (exl3_gemm.cu)
+EXL3_TC_MIN_ROWS = 8
+
 
 def _u16(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().cpu().numpy().view(np.uint16)
@@ -85,9 +88,37 @@ def test_gpu_layer_exl3_reduced():
     subset = np.arange(T)
     contrib, ref = _exl3_reference(layer, x, cfg, subset)
     plane = _plane(layer, T, cfg)
-    exact = float(np.mean(plane == contrib))
-    assert exact > 0.99, f"only {exact:.4f} of slot outputs bit-exact"
+    # experts with fewer than 8 rows run the bit-exact decode-fused GEMV chain
+    re = layer.routes(T)[0].cpu().numpy().astype(np.int64)
+    rows = np.bincount(re.ravel(), minlength=cfg.experts)
+    gemv = rows[re] < EXL3_TC_MIN_ROWS
+    assert gemv.any()
+    exact = float(np.mean(plane[gemv] == contrib[gemv]))
+    assert exact > 0.99, f"only {exact:.4f} of GEMV-path slot outputs bit-exact"
     assert_layer_close(out, ref, "exl3 layer")
+
+
+def test_gpu_layer_exl3_tensor_core_rows():
+    """Experts with >= 8 rows take the tensor-core projection (trellis decoded into
+    shared memory, fp32 tensor-core accumulation): within the layer tolerance of
+    the sequential reference composition."""
+    cfg = MoEConfig(experts=16, groups=1, topk_groups=1, intermediate=512, shared_intermediate=0)
+    dev = cuda()
+    T = 64
+    w = synth.make_exl3_rank_weights(cfg, seed=41, device=dev)
+    x = synth.make_input(T, cfg.hidden, seed=41, device=dev)
+    layer = RoutedMoE(cfg, w, T)
+    out = layer(x).cpu().numpy()
+    torch.cuda.synchronize()
+    assert layer.device_status() == []
+    counts = np.bincount(layer.routes(T)[0].cpu().numpy().astype(np.int64).ravel(),
+                         minlength=cfg.experts)
+    assert counts.max() >= 8  # the tensor-core path ran
+    subset = np.arange(0, T, 3)
+    contrib, ref = _exl3_reference(layer, x, cfg, subset)
+    assert_layer_close(out[subset], ref, "exl3 tensor-core rows")
+    plane = _plane(layer, T, cfg)[subset]
+    assert rel_l2(plane, contrib) < 1e-3
 
 
 def test_gpu_layer_exl3_decode_tp4_subset():
