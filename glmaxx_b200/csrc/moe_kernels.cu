@@ -58,17 +58,28 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
   }
   const uint32_t warp = tid >> 5, lane = tid & 31;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (uint32_t k0 = 0; k0 < chunk; k0 += kRouterSub) {
-    const uint32_t kn = min(kRouterSub, chunk - k0);  // multiple of 8 (H % 256 == 0)
-    __syncthreads();
-    // fill: 32 rows x kn bf16 of x and of w, 8 elements (16 bytes) per load
-    for (uint32_t v = tid; v < 32 * (kn / 8); v += 256) {
-      const uint32_t r = v / (kn / 8), kk = (v % (kn / 8)) * 8;
+  // Sub-tile fills are software-pipelined: the global loads of sub-tile s+1 are
+  // in flight while sub-tile s is computed.  Thread tid owns pieces tid + 256i
+  // (i < 4) of 16 bytes: row p / 32, columns (p % 32) * 8 .. +8.
+  uint4 rx[4], rw[4];
+  auto gload = [&](uint32_t k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
       const uint64_t col = uint64_t(c) * chunk + k0 + kk;
-      uint4 xv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
-      if (t0 + r < T) xv = *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + col);
-      if (e0 + r < E) wv = *reinterpret_cast<const uint4*>(w + uint64_t(e0 + r) * H + col);
-      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, wwv[4] = {wv.x, wv.y, wv.z, wv.w};
+      const bool in_k = k0 + kk < chunk;
+      rx[i] = (in_k && t0 + r < T) ? *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + col)
+                                   : make_uint4(0, 0, 0, 0);
+      rw[i] = (in_k && e0 + r < E) ? *reinterpret_cast<const uint4*>(w + uint64_t(e0 + r) * H + col)
+                                   : make_uint4(0, 0, 0, 0);
+    }
+  };
+  auto sstore = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
+      const uint32_t xw[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
+      const uint32_t wwv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
       float4* xd = reinterpret_cast<float4*>(xs + r * kRouterPitch + kk);
       float4* wd = reinterpret_cast<float4*>(ws + r * kRouterPitch + kk);
       xd[0] = make_float4(__uint_as_float(xw[0] << 16), __uint_as_float(xw[0] & 0xffff0000u),
@@ -80,7 +91,14 @@ __global__ void __launch_bounds__(256) router_logits_kernel(
       wd[1] = make_float4(__uint_as_float(wwv[2] << 16), __uint_as_float(wwv[2] & 0xffff0000u),
                           __uint_as_float(wwv[3] << 16), __uint_as_float(wwv[3] & 0xffff0000u));
     }
+  };
+  gload(0);
+  for (uint32_t k0 = 0; k0 < chunk; k0 += kRouterSub) {
+    const uint32_t kn = min(kRouterSub, chunk - k0);  // multiple of 8 (H % 256 == 0)
     __syncthreads();
+    sstore();
+    __syncthreads();
+    if (k0 + kRouterSub < chunk) gload(k0 + kRouterSub);
     const float* xr = xs + lane * kRouterPitch;
     const float* wr = ws + (warp * 4) * kRouterPitch;
 #pragma unroll 2
@@ -242,7 +260,7 @@ __global__ void __launch_bounds__(256) router_select_kernel(
   constexpr uint32_t kFull = 0xffffffffu;
   constexpr uint32_t kNone = 0u;  // key below every finite choice (fkey(-inf) > 0)
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t t = blockIdx.x * 8 + warp;
+  const uint32_t t = blockIdx.x * (blockDim.x >> 5) + warp;
   if (t >= T) return;
   const uint32_t nj = (E + 31) / 32;
   const uint32_t gs = E / groups;
@@ -1019,7 +1037,9 @@ cudaError_t launch_router_select(const float* partial, const float* bias, uint32
                                  float route_scale, uint16_t* experts, float* weights,
                                  uint32_t* bitmap, uint32_t bitmap_stride, uint32_t* status,
                                  cudaStream_t stream) {
-  router_select_kernel<<<(T + 7) / 8, 256, 0, stream>>>(partial, bias, T, E, groups, topk_groups,
+  // two tokens (warps) per CTA: the per-token selection is a latency chain, so
+  // tokens are spread over as many SMs as possible
+  router_select_kernel<<<(T + 1) / 2, 64, 0, stream>>>(partial, bias, T, E, groups, topk_groups,
                                                         top_k, route_scale, experts, weights,
                                                         bitmap, bitmap_stride, status);
   return cudaPeekAtLastError();
