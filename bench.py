@@ -61,6 +61,8 @@ NVFP4_NOMINAL_TFLOPS = 9000.0
 # whose per-token cost does not depend on the skew.
 REF_ZIPF_BETA = 0.04
 REF_TIME_BUDGET_S = 90.0
+# measured peer copy over NVLink 5 on this pool, per direction per GPU
+NVLINK_PEER_GBS = 770.0
 
 
 def parse():
@@ -74,6 +76,10 @@ def parse():
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-sample-tokens", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    # N > 1: how the ranks' partials are reduced -- the fused peer-memory finish
+    # (one kernel per layer over NVLink) or an NCCL all-reduce plus the finish
+    p.add_argument("--reduce", choices=["peer", "nccl"], default="peer")
+    p.add_argument("--peer-mode", choices=["auto", "one", "two"], default="auto")
     a = p.parse_args()
     if a.tokens is None:
         a.tokens = WORKLOADS[a.workload]["tokens"]
@@ -331,24 +337,54 @@ def run_ours(args):
     layer = layers[0]
     weights = layer.w
     x = synth.make_input(T, HIDDEN, seed=args.seed, device=dev)
+    use_peer = world > 1 and args.reduce == "peer"
+    group = None
+    if use_peer:
+        # every rank maps every rank's partial, output and stacked-layer buffers
+        from glmaxx_b200.peer import PeerGroup
+        bufs = {"partial": ((T, HIDDEN), torch.float32), "out": ((T, HIDDEN), torch.float32)}
+        for li in range(1, n_layers):
+            bufs[f"rs{li}"] = ((T, HIDDEN), torch.bfloat16)
+            bufs[f"xs{li}"] = ((T, HIDDEN), torch.bfloat16)
+        group = PeerGroup(bufs, device=dev)
+        peer_status = torch.zeros(1, dtype=torch.int32, device=dev)
     # stack: rs[l] is the bf16 residual stream before layer l, xs[l] layer l's MoE
     # input RMSNorm(rs[l]) (unit weight; layer 0 takes the unit-variance input as is)
-    xs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
-    rs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
-    outs = [torch.empty((T, HIDDEN), dtype=torch.float32, device=dev) for _ in range(n_layers)]
-    out = outs[-1]
+    if use_peer:
+        xs = [x] + [group.tensor(f"xs{li}") for li in range(1, n_layers)]
+        rs = [x] + [group.tensor(f"rs{li}") for li in range(1, n_layers)]
+        outs = [group.tensor("partial")] * n_layers  # one partial buffer, reused per layer
+        out = group.tensor("out")
+    else:
+        xs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
+        rs = [x] + [torch.empty_like(x) for _ in range(n_layers - 1)]
+        outs = [torch.empty((T, HIDDEN), dtype=torch.float32, device=dev)
+                for _ in range(n_layers)]
+        out = outs[-1]
     stream = torch.cuda.Stream(device=dev)
 
     def reduce(o):
-        if world > 1:
+        if world > 1 and not use_peer:
             dist.all_reduce(o)
+
+    def peer_finish(li):
+        """The fused reduce + finish of layer li over peer memory: into layer li+1's
+        bf16 residual and normalised input, or (last layer) the fp32 output."""
+        if li + 1 < n_layers:
+            group.finish("partial", residual=rs[li], out_bf16=f"rs{li + 1}",
+                         norm_bf16=f"xs{li + 1}", hidden=HIDDEN, mode=args.peer_mode,
+                         status=peer_status)
+        else:
+            group.finish("partial", out_f32="out", mode=args.peer_mode, status=peer_status)
 
     def layer_and_finish(li):
         """layer li, and (stack) the finish that forms layer li+1's bf16 input."""
         layers[li](xs[li], outs[li])
+        if use_peer:
+            peer_finish(li)
 
     def finish_into_next(li):
-        if li + 1 < n_layers:
+        if li + 1 < n_layers and not use_peer:
             finish([outs[li]], rs[li], out_bf16=rs[li + 1], norm_bf16=xs[li + 1], hidden=HIDDEN)
 
     with torch.cuda.stream(stream):
@@ -362,6 +398,8 @@ def run_ours(args):
             status = lay.device_status()
             if status:
                 raise RuntimeError(f"device status after warm-up: {status}")
+        if use_peer and int(peer_status.item()):
+            raise RuntimeError(f"peer finish status after warm-up: {int(peer_status.item())}")
         # one graph per layer (its routed step; the finish joins it when no collective
         # sits between a layer and the next)
         graphs = []
@@ -383,7 +421,7 @@ def run_ours(args):
         def step():
             for li in range(n_layers):
                 graphs[li].replay()
-                if world > 1:
+                if world > 1 and not use_peer:
                     reduce(outs[li])
                     finish_into_next(li)
 
@@ -418,6 +456,52 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    if use_peer and int(peer_status.item()):
+        raise RuntimeError(f"peer finish status: {int(peer_status.item())}")
+
+    # ------------------------------------------- the reduce alone (N > 1)
+    reduce_info = None
+    if world > 1:
+        from glmaxx_b200.peer import two_shot_pays
+
+        def one_reduce():
+            if use_peer:
+                group.finish("partial", out_f32="out", mode=args.peer_mode, status=peer_status)
+            else:
+                dist.all_reduce(outs[-1])
+
+        n_red = max(10, min(args.steps, 200))
+        with torch.cuda.stream(stream):
+            for _ in range(5):
+                one_reduce()
+            stream.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(n_red):
+                one_reduce()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        red_ms = e0.elapsed_time(e1) / n_red
+        t = torch.tensor([red_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        red_ms = float(t.item())
+        S = T * HIDDEN * 4
+        mode = args.peer_mode
+        if mode == "auto":
+            mode = "two" if two_shot_pays(T * HIDDEN, world) else "one"
+        busbw = 2 * (world - 1) / world * S / (red_ms * 1e-3) / 1e9
+        reduce_info = {
+            "kind": f"peer {mode}-shot (fused finish kernel)" if use_peer else "NCCL all-reduce",
+            "us_per_launch": red_ms * 1e3, "bytes": S,
+            "nvlink_bytes_per_rank": ((world - 1) * S if use_peer and mode == "one"
+                                      else 2 * (world - 1) * S // world),
+            "busbw_gbs": busbw, "peak_gbs": NVLINK_PEER_GBS,
+            "frac": busbw / 2 / NVLINK_PEER_GBS,
+            "note": "busbw = 2(N-1)/N x bytes / time (the all-reduce convention); frac = the "
+                    "per-direction (N-1)/N x bytes / time against the measured 770 GB/s peer copy"}
+        if use_peer and int(peer_status.item()):
+            raise RuntimeError(f"peer finish status: {int(peer_status.item())}")
 
     # ------------------------------------------- per-stage kernel timing (roofline)
     L = abi.load()
@@ -556,12 +640,17 @@ def run_ours(args):
             "config": {"workload": wl["name"], "tokens": T,
                        "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOPK, "groups": 8,
                        "topk_groups": 4, "intermediate": INTER, "shared_intermediate": INTER,
-                       "parallelism": f"tp{world} (expert intermediate sharded, NCCL all-reduce)",
+                       "parallelism": f"tp{world} (expert intermediate sharded, "
+                                      + ("fused peer-memory finish over NVLink)" if use_peer
+                                         else "NCCL all-reduce)"),
                        "l2": "weights per step >> 126 MB L2 (no flush needed)",
-                       "timing": "CUDA-graph replay of the layer + eager NCCL all-reduce, "
-                                 "CUDA events on the launch stream, max over ranks"},
+                       "timing": ("CUDA-graph replay of the layer and its peer finish"
+                                  if use_peer else "CUDA-graph replay of the layer"
+                                  + (" + eager NCCL all-reduce" if world > 1 else ""))
+                                 + ", CUDA events on the launch stream, max over ranks"},
             "roofline": roof,
             "stage_ms": stage_avg,
+            "reduce": reduce_info,
             "cpu_baseline": cpu,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 4,
@@ -572,6 +661,11 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         del graph
+        graphs.clear()
+        torch.cuda.synchronize()
+        if group is not None:
+            outs, out, xs, rs = None, None, None, None
+            group.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -19,6 +19,8 @@ FC2_ABI_VERSION = 1
 EXL3_ABI_VERSION = 1
 MOE_EXL3_ABI_VERSION = 1
 MOE_FINISH_ABI_VERSION = 1
+MOE_PEER_ABI_VERSION = 1
+PEER_ONE_SHOT, PEER_TWO_SHOT = 1, 2
 ROUTER_ABI_VERSION = 3
 MOE_LAYER_ABI_VERSION = 3
 DECODE_PERSISTENT = 1
@@ -42,6 +44,7 @@ STATUS_BITS = {
     1 << 6: "capacity-exceeded",
     1 << 8: "wait-timeout",
     1 << 9: "tmem-timeout",
+    1 << 10: "peer-timeout",
 }
 
 u32, u64, f32 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
@@ -138,6 +141,13 @@ class MoeFinishDescriptor(_Desc):
         [("hidden", u32), ("eps", f32), ("reserved", u64 * 3)]
 
 
+class MoePeerDescriptor(_Desc):
+    """glmaxx_moe_peer_descriptor (new), 80 bytes."""
+    _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "flags", "rank")] + \
+        [(n, u64) for n in ("signals_u32", "outputs_f32", "outputs_bf16", "norms_bf16",
+                            "status_u32")] + [("reserved", u64 * 3)]
+
+
 class MoeExl3Experts(_Desc):
     """glmaxx_moe_exl3_experts (new), 128 bytes."""
     _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "bits", "reserved0")] + \
@@ -148,7 +158,7 @@ class MoeExl3Experts(_Desc):
 
 EXPECTED_SIZES = {Fc1Descriptor: 224, Fc2Descriptor: 224, Exl3Descriptor: 144,
                   RouterDescriptor: 192, MoeLayerDescriptor: 240, MoeExl3Experts: 128,
-                  MoeFinishDescriptor: 112}
+                  MoeFinishDescriptor: 112, MoePeerDescriptor: 80}
 
 _P = ctypes.c_void_p
 _I32P = ctypes.POINTER(ctypes.c_int32)
@@ -177,6 +187,11 @@ SIGNATURES = {
     "glmaxx_nvfp4_fc2_grouped_control_launch": (ctypes.c_int32, [_P, _U16P, u32, _P, _I32P]),
     "glmaxx_exl3_projection_launch": (ctypes.c_int32, [_P, _P, _I32P]),
     "glmaxx_moe_finish_launch": (ctypes.c_int32, [_P, _P]),
+    "glmaxx_moe_finish_peer_launch": (ctypes.c_int32, [_P, _P, _P]),
+    "glmaxx_moe_peer_signal_bytes": (u64, [u32]),
+    "glmaxx_ipc_handle": (ctypes.c_int32, [u64, ctypes.POINTER(ctypes.c_uint8)]),
+    "glmaxx_ipc_open": (ctypes.c_int32, [ctypes.POINTER(ctypes.c_uint8), _U64P]),
+    "glmaxx_ipc_close": (ctypes.c_int32, [u64]),
     "glmaxx_exl3_gemv_launch": (ctypes.c_int32, [u64, u64, u32, u32, u32, u32, u64, _P]),
     "glmaxx_graph_exec_launch": (ctypes.c_int32, [u64, u64]),
     "glmaxx_graph_exec_destroy": (ctypes.c_int32, [u64]),

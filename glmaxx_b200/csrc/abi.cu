@@ -355,45 +355,6 @@ int32_t glmaxx_moe_layer_launch(const glmaxx_moe_layer_descriptor* descriptor, v
   return moe_layer_launch(descriptor, cuda_stream, asynchronous_error);
 }
 
-int32_t glmaxx_moe_finish_launch(const glmaxx_moe_finish_descriptor* descriptor,
-                                 void* cuda_stream) {
-  if (descriptor == nullptr) return GLMAXX_ERR_NULL;
-  const glmaxx_moe_finish_descriptor& d = *descriptor;
-  if (d.abi_version != GLMAXX_MOE_FINISH_ABI_VERSION || d.struct_bytes != sizeof(d) || d.flags)
-    return GLMAXX_ERR_DESCRIPTOR;
-  for (uint64_t v : d.reserved)
-    if (v) return GLMAXX_ERR_DESCRIPTOR;
-  if (d.ranks == 0 || d.ranks > 8 || d.elements == 0 || d.elements % 4) return GLMAXX_ERR_DESCRIPTOR;
-  if ((d.residual_f32 != 0) == (d.residual_bf16 != 0)) return GLMAXX_ERR_DESCRIPTOR;
-  if (d.output_f32 == 0 && d.output_bf16 == 0 && d.norm_bf16 == 0) return GLMAXX_ERR_DESCRIPTOR;
-  if (d.norm_bf16 && (d.hidden == 0 || d.elements % d.hidden || !(d.eps >= 0.0f)))
-    return GLMAXX_ERR_DESCRIPTOR;
-  if (d.partials_f32 == 0) return GLMAXX_ERR_NULL;
-  if (d.residual_f32 % 16 || d.residual_bf16 % 8 || d.attention_f32 % 16 || d.output_f32 % 16 ||
-      d.output_bf16 % 8 || d.norm_bf16 % 2)
-    return GLMAXX_ERR_DESCRIPTOR;
-  FinishArgs a{};
-  const uint64_t* parts = reinterpret_cast<const uint64_t*>(d.partials_f32);
-  for (uint32_t r = 0; r < d.ranks; ++r) {
-    if (parts[r] == 0 || parts[r] % 16) return GLMAXX_ERR_DESCRIPTOR;
-    a.partials[r] = reinterpret_cast<const float*>(parts[r]);
-  }
-  DeviceInfo info;
-  const int32_t arch = current_device_info(&info);
-  if (arch != 0) return arch;
-  a.residual_f32 = reinterpret_cast<const float*>(d.residual_f32);
-  a.residual_bf16 = reinterpret_cast<const uint16_t*>(d.residual_bf16);
-  a.attention_f32 = reinterpret_cast<const float*>(d.attention_f32);
-  a.output_f32 = reinterpret_cast<float*>(d.output_f32);
-  a.output_bf16 = reinterpret_cast<uint16_t*>(d.output_bf16);
-  a.norm_bf16 = reinterpret_cast<uint16_t*>(d.norm_bf16);
-  a.hidden = d.hidden;
-  a.eps = d.eps;
-  a.elements = d.elements;
-  a.ranks = d.ranks;
-  return int32_t(launch_finish(a, reinterpret_cast<cudaStream_t>(cuda_stream)));
-}
-
 int32_t glmaxx_moe_layer_set_stage_events(uint64_t* events, uint32_t count) {
   return set_stage_events(events, count);
 }
@@ -808,6 +769,27 @@ int32_t glmaxx_device_alloc(uint64_t bytes, uint64_t* pointer) {
 int32_t glmaxx_device_free(uint64_t pointer) {
   if (pointer == 0) return GLMAXX_ERR_NULL;
   return int32_t(cudaFree(reinterpret_cast<void*>(pointer)));
+}
+int32_t glmaxx_ipc_handle(uint64_t pointer, uint8_t handle[64]) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handle size");
+  if (pointer == 0 || handle == nullptr) return GLMAXX_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  const cudaError_t st = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(pointer));
+  if (st == cudaSuccess) std::memcpy(handle, &h, sizeof(h));
+  return int32_t(st);
+}
+int32_t glmaxx_ipc_open(const uint8_t handle[64], uint64_t* pointer) {
+  if (handle == nullptr || pointer == nullptr) return GLMAXX_ERR_NULL;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t st = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (st == cudaSuccess) *pointer = reinterpret_cast<uint64_t>(p);
+  return int32_t(st);
+}
+int32_t glmaxx_ipc_close(uint64_t pointer) {
+  if (pointer == 0) return GLMAXX_ERR_NULL;
+  return int32_t(cudaIpcCloseMemHandle(reinterpret_cast<void*>(pointer)));
 }
 int32_t glmaxx_pinned_alloc(uint64_t bytes, uint64_t* pointer) {
   if (bytes == 0 || pointer == nullptr) return GLMAXX_ERR_NULL;

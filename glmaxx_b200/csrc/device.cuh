@@ -24,6 +24,7 @@ enum : uint32_t {
   kStatusCapacityExceeded = 1u << 6,
   kStatusWaitTimeout = 1u << 8,   // a bounded pipeline wait gave up
   kStatusTmemTimeout = 1u << 9,   // drain of in-flight tensor-core work gave up
+  kStatusPeerTimeout = 1u << 10,  // a wait on another rank's flag gave up
 };
 
 // A bounded wait gives up after this many nanoseconds (%globaltimer).  Every

@@ -115,6 +115,18 @@ struct FinishArgs {
   float eps;
 };
 cudaError_t launch_finish(const FinishArgs& a, cudaStream_t stream);
+// Peer form of the finish: every rank's signal buffer and, for two-shot, every
+// rank's outputs (rank order).
+struct FinishPeer {
+  uint32_t* signals[8];
+  float* outputs_f32[8];
+  uint16_t* outputs_bf16[8];
+  uint16_t* norms_bf16[8];
+  uint32_t* status;
+  uint32_t rank;
+  bool two_shot;
+};
+cudaError_t launch_finish_peer(const FinishArgs& a, const FinishPeer& p, cudaStream_t stream);
 
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
                                  uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,

@@ -848,81 +848,6 @@ __global__ void combine_kernel(const float* __restrict__ plane, const uint16_t* 
   *reinterpret_cast<float4*>(out + uint64_t(t) * H + c) = acc;
 }
 
-// Sparse-layer finish (finish_sparse_layer_oracle order): residual, then the
-// ranks' attention terms, then the ranks' partials, one fp32 add each.
-__global__ void finish_kernel(FinishArgs a) {
-  const uint64_t n4 = a.elements / 4;
-  for (uint64_t v = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; v < n4;
-       v += uint64_t(gridDim.x) * blockDim.x) {
-    float o[4];
-    if (a.residual_f32) {
-      const float4 r = reinterpret_cast<const float4*>(a.residual_f32)[v];
-      o[0] = r.x, o[1] = r.y, o[2] = r.z, o[3] = r.w;
-    } else {
-      const uint2 r = reinterpret_cast<const uint2*>(a.residual_bf16)[v];
-      o[0] = __uint_as_float(r.x << 16), o[1] = __uint_as_float(r.x & 0xffff0000u);
-      o[2] = __uint_as_float(r.y << 16), o[3] = __uint_as_float(r.y & 0xffff0000u);
-    }
-    if (a.attention_f32)
-      for (uint32_t r = 0; r < a.ranks; ++r) {
-        const float4 t = reinterpret_cast<const float4*>(a.attention_f32 + r * a.elements)[v];
-        o[0] = __fadd_rn(o[0], t.x), o[1] = __fadd_rn(o[1], t.y);
-        o[2] = __fadd_rn(o[2], t.z), o[3] = __fadd_rn(o[3], t.w);
-      }
-    for (uint32_t r = 0; r < a.ranks; ++r) {
-      const float4 t = reinterpret_cast<const float4*>(a.partials[r])[v];
-      o[0] = __fadd_rn(o[0], t.x), o[1] = __fadd_rn(o[1], t.y);
-      o[2] = __fadd_rn(o[2], t.z), o[3] = __fadd_rn(o[3], t.w);
-    }
-    if (a.output_f32) reinterpret_cast<float4*>(a.output_f32)[v] = make_float4(o[0], o[1], o[2], o[3]);
-    if (a.output_bf16) {
-      uint32_t b[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = __bfloat16_as_ushort(__float2bfloat16_rn(o[j]));
-      reinterpret_cast<uint2*>(a.output_bf16)[v] = make_uint2(b[0] | (b[1] << 16), b[2] | (b[3] << 16));
-    }
-  }
-}
-
-// Finish with the row-wise RMSNorm output: one CTA per row of `hidden`
-// elements; the sum of squares is reduced in a fixed order (per-thread
-// sequential over its columns, then a fixed tree), so results are deterministic.
-__global__ void __launch_bounds__(256) finish_norm_kernel(FinishArgs a) {
-  __shared__ float red[256];
-  const uint64_t row = blockIdx.x;
-  const uint32_t H = a.hidden;
-  float ss = 0.f;
-  for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
-    const uint64_t i = row * H + c;
-    float o = a.residual_f32 ? a.residual_f32[i] : bf16_to_f32(a.residual_bf16[i]);
-    if (a.attention_f32)
-      for (uint32_t r = 0; r < a.ranks; ++r) o = __fadd_rn(o, a.attention_f32[r * a.elements + i]);
-    for (uint32_t r = 0; r < a.ranks; ++r) o = __fadd_rn(o, a.partials[r][i]);
-    if (a.output_f32) a.output_f32[i] = o;
-    if (a.output_bf16) a.output_bf16[i] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
-    ss = __fmaf_rn(o, o, ss);
-  }
-  red[threadIdx.x] = ss;
-  __syncthreads();
-  for (uint32_t s = 128; s > 0; s >>= 1) {
-    if (threadIdx.x < s) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + s]);
-    __syncthreads();
-  }
-  const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(red[0], float(H)), a.eps));
-  for (uint32_t c = threadIdx.x; c < H; c += blockDim.x) {
-    const uint64_t i = row * H + c;
-    // the row values again, from the outputs just written or recomputed
-    float o = a.output_f32 ? a.output_f32[i]
-                           : (a.residual_f32 ? a.residual_f32[i] : bf16_to_f32(a.residual_bf16[i]));
-    if (!a.output_f32) {
-      if (a.attention_f32)
-        for (uint32_t r = 0; r < a.ranks; ++r) o = __fadd_rn(o, a.attention_f32[r * a.elements + i]);
-      for (uint32_t r = 0; r < a.ranks; ++r) o = __fadd_rn(o, a.partials[r][i]);
-    }
-    a.norm_bf16[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(o, inv)));
-  }
-}
-
 // Shared-expert FC1 finish after split-K: gate/up = sums of the slice partials
 // (parts[s][t][0..I) gate, [I..2I) up, slice order), h = bf16(silu(gate) * up).
 __global__ void swiglu_finish_kernel(const float* __restrict__ parts, uint32_t splits, uint32_t T,
@@ -1145,17 +1070,4 @@ cudaError_t launch_pack(const void* src, int src_bf16, uint32_t batch, uint32_t 
 
 }  // namespace glmaxx
 
-namespace glmaxx {
-cudaError_t launch_finish(const FinishArgs& a, cudaStream_t stream) {
-  if (a.norm_bf16 != nullptr) {
-    if (a.hidden == 0 || a.elements % a.hidden) return cudaErrorInvalidValue;
-    finish_norm_kernel<<<static_cast<uint32_t>(a.elements / a.hidden), 256, 0, stream>>>(a);
-    return cudaPeekAtLastError();
-  }
-  const uint64_t n4 = a.elements / 4;
-  if (n4 == 0) return cudaSuccess;
-  const uint64_t want = (n4 + 255) / 256;
-  finish_kernel<<<static_cast<uint32_t>(want < 148 * 16 ? want : 148 * 16), 256, 0, stream>>>(a);
-  return cudaPeekAtLastError();
-}
-}  // namespace glmaxx
+

@@ -47,6 +47,7 @@ enum {
   GLMAXX_MOE_LAYER_ABI_VERSION = 3,
   GLMAXX_MOE_EXL3_ABI_VERSION = 1,
   GLMAXX_MOE_FINISH_ABI_VERSION = 1,
+  GLMAXX_MOE_PEER_ABI_VERSION = 1,
   GLMAXX_FC1_DECODE_PERSISTENT = 1,
   GLMAXX_FC1_PREFILL_GROUPED = 2,
   GLMAXX_EXL3_GATE = 1,
@@ -73,6 +74,7 @@ enum {
   GLMAXX_STATUS_CAPACITY_EXCEEDED = 1u << 6,
   GLMAXX_STATUS_WAIT_TIMEOUT = 1u << 8,
   GLMAXX_STATUS_TMEM_TIMEOUT = 1u << 9,
+  GLMAXX_STATUS_PEER_TIMEOUT = 1u << 10,
 };
 
 /* Flags of glmaxx_moe_layer_descriptor.flags. */
@@ -354,6 +356,52 @@ struct glmaxx_moe_finish_descriptor {
   uint64_t reserved[3];
 };
 
+/*
+ * Peer form of the finish (new; replaces the NCCL all-reduce of the partials,
+ * crates/glm-engine/src/manifest.rs:228, and the finish after it): every rank of a
+ * tensor-parallel group calls glmaxx_moe_finish_peer_launch at the same point of
+ * its stream with the same finish descriptor except for its own outputs;
+ * partials_f32 then holds every rank's partial buffer as mapped on this GPU (CUDA
+ * IPC).  The residual may be absent (a plain all-reduce).  A flag barrier over
+ * the ranks' signal buffers orders the launch after every rank's partial and keeps
+ * each partial unchanged until every rank has read it.  The result is the same
+ * bit for bit as glmaxx_moe_finish_launch on the same partials, on every rank.
+ *  GLMAXX_MOE_PEER_ONE_SHOT: every rank reads all partials and writes its own
+ *    outputs (the outputs_* arrays are 0).
+ *  GLMAXX_MOE_PEER_TWO_SHOT: rank r reduces the r-th slice (of rows with the
+ *    RMSNorm output) and writes it into every rank's outputs; outputs_f32,
+ *    outputs_bf16, norms_bf16 are host arrays of `ranks` device addresses (rank
+ *    order, entry `rank` equal to the descriptor's own output), 0 exactly when the
+ *    descriptor's output is 0.
+ * signals_u32: host array of `ranks` device addresses, every rank's signal buffer
+ * (glmaxx_moe_peer_signal_bytes(ranks) bytes each, zeroed once before the first
+ * launch, 16-byte aligned).  A wait on another rank gives up after 1 s and sets
+ * GLMAXX_STATUS_PEER_TIMEOUT in status_u32 (optional device word); the signal
+ * buffers must then be zeroed on every rank, after a host barrier, before the next
+ * launch.  norm_bf16 and output_bf16 are 8-byte aligned, hidden % 4 == 0 with the
+ * RMSNorm.
+ */
+enum {
+  GLMAXX_MOE_PEER_ONE_SHOT = 1,
+  GLMAXX_MOE_PEER_TWO_SHOT = 2,
+};
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_moe_peer_descriptor {
+#else
+struct glmaxx_moe_peer_descriptor {
+#endif
+  uint32_t abi_version; /* GLMAXX_MOE_PEER_ABI_VERSION */
+  uint32_t struct_bytes;
+  uint32_t flags;       /* GLMAXX_MOE_PEER_ONE_SHOT or GLMAXX_MOE_PEER_TWO_SHOT */
+  uint32_t rank;
+  uint64_t signals_u32;
+  uint64_t outputs_f32;
+  uint64_t outputs_bf16;
+  uint64_t norms_bf16;
+  uint64_t status_u32;
+  uint64_t reserved[3];
+};
+
 /* ---- reference entry points (glmaxx_kernel.h:123-250) ---- */
 int32_t glmaxx_nvfp4_routed_fc1_launch(const struct glmaxx_fc1_descriptor* descriptor,
                                        void* cuda_stream, int32_t* asynchronous_error);
@@ -496,6 +544,19 @@ int32_t glmaxx_moe_layer_launch(const struct glmaxx_moe_layer_descriptor* descri
                                 void* cuda_stream, int32_t* asynchronous_error);
 int32_t glmaxx_moe_finish_launch(const struct glmaxx_moe_finish_descriptor* descriptor,
                                  void* cuda_stream);
+uint64_t glmaxx_moe_peer_signal_bytes(uint32_t ranks);
+int32_t glmaxx_moe_finish_peer_launch(const struct glmaxx_moe_finish_descriptor* descriptor,
+                                      const struct glmaxx_moe_peer_descriptor* peer,
+                                      void* cuda_stream);
+
+/* CUDA IPC of a glmaxx_device_alloc allocation between the processes of one host
+ * (new; the peer form of the finish maps every rank's buffers with these).
+ * glmaxx_ipc_handle writes the 64-byte handle of the allocation starting at
+ * `pointer`; glmaxx_ipc_open maps another process's handle on the current device
+ * (peer access enabled lazily); glmaxx_ipc_close unmaps it. */
+int32_t glmaxx_ipc_handle(uint64_t pointer, uint8_t handle[64]);
+int32_t glmaxx_ipc_open(const uint8_t handle[64], uint64_t* pointer);
+int32_t glmaxx_ipc_close(uint64_t pointer);
 
 /* Profiling (the CUDA-event timing of the reference, crates/glm-cuda/src/
  * ffi.rs:3057-3079, per stage): while set, layer launches on the calling
@@ -555,6 +616,7 @@ static_assert(sizeof(glmaxx_router_descriptor) == 192, "router descriptor size")
 static_assert(sizeof(glmaxx_moe_layer_descriptor) == 240, "layer descriptor size");
 static_assert(sizeof(glmaxx_moe_exl3_experts) == 128, "EXL3 experts descriptor size");
 static_assert(sizeof(glmaxx_moe_finish_descriptor) == 112, "finish descriptor size");
+static_assert(sizeof(glmaxx_moe_peer_descriptor) == 80, "peer descriptor size");
 #endif
 
 #endif /* GLMAXX_KERNEL_H_ */
