@@ -65,13 +65,24 @@ struct FinishKernelArgs {
 };
 
 // ------------------------------------------------------------ peer barrier
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Ordering without system-scope fences (each costs microseconds on B200):
+//  * a partial was written by kernels that completed before this launch, so it
+//    sits in its GPU's L2, which serves peer reads too: the ready flag needs no
+//    fence before it;
+//  * every load of a peer's partial has returned (its value was stored) before
+//    the CTA counts itself out, so the done flag needs no fence either;
+//  * only two-shot stores into peers' memory must be complete before the done
+//    flag: there each CTA fences at system scope once, before counting out.
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
@@ -83,7 +94,7 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
 __device__ bool wait_flags(const uint32_t* sig, uint32_t base, uint32_t ranks, uint32_t e) {
   const uint64_t start = globaltimer();
   for (uint32_t p = 0; p < ranks; ++p) {
-    while (static_cast<int32_t>(ld_acquire_sys(sig + base + p) - e) < 0) {
+    while (static_cast<int32_t>(ld_relaxed_sys(sig + base + p) - e) < 0) {
       if (globaltimer() - start > kWaitTimeoutNs) return false;
     }
   }
@@ -99,12 +110,8 @@ __device__ uint32_t peer_enter(const FinishKernelArgs& a, uint32_t* s_epoch, uin
   if (threadIdx.x == 0) {
     // the epoch word changes only after every CTA of this launch has arrived
     const uint32_t e = ld_relaxed_gpu(own + 2 * N) + 1;
-    if (atomicAdd(own + 2 * N + 1, 1u) == 0) {
-      // everything this rank's stream wrote before the launch (the partial) is
-      // complete; make it visible system-wide before the flag
-      __threadfence_system();
-      for (uint32_t p = 0; p < N; ++p) st_release_sys(a.signals[p] + a.rank, e);
-    }
+    if (atomicAdd(own + 2 * N + 1, 1u) == 0)
+      for (uint32_t p = 0; p < N; ++p) st_relaxed_sys(a.signals[p] + a.rank, e);
     const bool ok = wait_flags(own, 0, N, e);
     if (!ok && a.status) atomicOr(a.status, kStatusPeerTimeout);
     *s_epoch = e;
@@ -122,45 +129,66 @@ __device__ void peer_exit(const FinishKernelArgs& a, uint32_t e) {
   if (threadIdx.x != 0) return;
   const uint32_t N = a.ranks;
   uint32_t* own = a.signals[a.rank];
-  __threadfence_system();  // this CTA's peer stores before the departure count
+  if (a.dests > 1) fence_acq_rel_sys();  // two-shot: stores into peers' outputs landed
   if (atomicAdd(own + 2 * N + 2, 1u) != gridDim.x - 1) return;
   own[2 * N + 1] = 0;  // every CTA has arrived and left
   own[2 * N + 2] = 0;
-  __threadfence_system();
-  for (uint32_t p = 0; p < N; ++p) st_release_sys(a.signals[p] + N + a.rank, e);
+  for (uint32_t p = 0; p < N; ++p) st_relaxed_sys(a.signals[p] + N + a.rank, e);
   if (!wait_flags(own, N, N, e) && a.status) atomicOr(a.status, kStatusPeerTimeout);
   *reinterpret_cast<volatile uint32_t*>(own + 2 * N) = e;
 }
 
 // ------------------------------------------------------------ arithmetic
-__device__ __forceinline__ void finish4(const FinishKernelArgs& a, uint64_t v, float (&o)[4]) {
-  if (a.residual_f32) {
-    const float4 r = __ldcg(reinterpret_cast<const float4*>(a.residual_f32) + v);
-    o[0] = r.x, o[1] = r.y, o[2] = r.z, o[3] = r.w;
-  } else if (a.residual_bf16) {
-    const uint2 r = __ldcg(reinterpret_cast<const uint2*>(a.residual_bf16) + v);
-    o[0] = __uint_as_float(r.x << 16), o[1] = __uint_as_float(r.x & 0xffff0000u);
-    o[2] = __uint_as_float(r.y << 16), o[3] = __uint_as_float(r.y & 0xffff0000u);
-  } else {
-    o[0] = o[1] = o[2] = o[3] = 0.0f;
+// U float4 groups at once, every load in flight before the first add.
+template <uint32_t U>
+__device__ __forceinline__ void finish_u(const FinishKernelArgs& a, const uint64_t (&v)[U],
+                                         const bool (&in)[U], float (&o)[U][4]) {
+#pragma unroll
+  for (uint32_t u = 0; u < U; ++u) {
+    o[u][0] = o[u][1] = o[u][2] = o[u][3] = 0.0f;
+    if (!in[u]) continue;
+    if (a.residual_f32) {
+      const float4 r = __ldcg(reinterpret_cast<const float4*>(a.residual_f32) + v[u]);
+      o[u][0] = r.x, o[u][1] = r.y, o[u][2] = r.z, o[u][3] = r.w;
+    } else if (a.residual_bf16) {
+      const uint2 r = __ldcg(reinterpret_cast<const uint2*>(a.residual_bf16) + v[u]);
+      o[u][0] = __uint_as_float(r.x << 16), o[u][1] = __uint_as_float(r.x & 0xffff0000u);
+      o[u][2] = __uint_as_float(r.y << 16), o[u][3] = __uint_as_float(r.y & 0xffff0000u);
+    }
   }
   if (a.attention_f32)
-    for (uint32_t r = 0; r < a.ranks; ++r) {
-      const float4 t = __ldcg(reinterpret_cast<const float4*>(a.attention_f32 + r * a.elements) + v);
-      o[0] = __fadd_rn(o[0], t.x), o[1] = __fadd_rn(o[1], t.y);
-      o[2] = __fadd_rn(o[2], t.z), o[3] = __fadd_rn(o[3], t.w);
-    }
-  // every rank's load in flight before the first add
-  float4 t[kMaxRanks];
 #pragma unroll
-  for (uint32_t r = 0; r < kMaxRanks; ++r)
-    if (r < a.ranks) t[r] = __ldcg(reinterpret_cast<const float4*>(a.partials[r]) + v);
+    for (uint32_t u = 0; u < U; ++u)
+      if (in[u])
+        for (uint32_t r = 0; r < a.ranks; ++r) {
+          const float4 t =
+              __ldcg(reinterpret_cast<const float4*>(a.attention_f32 + r * a.elements) + v[u]);
+          o[u][0] = __fadd_rn(o[u][0], t.x), o[u][1] = __fadd_rn(o[u][1], t.y);
+          o[u][2] = __fadd_rn(o[u][2], t.z), o[u][3] = __fadd_rn(o[u][3], t.w);
+        }
+  float4 t[U][kMaxRanks];
 #pragma unroll
-  for (uint32_t r = 0; r < kMaxRanks; ++r)
-    if (r < a.ranks) {
-      o[0] = __fadd_rn(o[0], t[r].x), o[1] = __fadd_rn(o[1], t[r].y);
-      o[2] = __fadd_rn(o[2], t[r].z), o[3] = __fadd_rn(o[3], t[r].w);
-    }
+  for (uint32_t u = 0; u < U; ++u)
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxRanks; ++r)
+      if (in[u] && r < a.ranks) t[u][r] = __ldcg(reinterpret_cast<const float4*>(a.partials[r]) + v[u]);
+#pragma unroll
+  for (uint32_t u = 0; u < U; ++u)
+#pragma unroll
+    for (uint32_t r = 0; r < kMaxRanks; ++r)
+      if (in[u] && r < a.ranks) {
+        o[u][0] = __fadd_rn(o[u][0], t[u][r].x), o[u][1] = __fadd_rn(o[u][1], t[u][r].y);
+        o[u][2] = __fadd_rn(o[u][2], t[u][r].z), o[u][3] = __fadd_rn(o[u][3], t[u][r].w);
+      }
+}
+
+__device__ __forceinline__ void finish4(const FinishKernelArgs& a, uint64_t v, float (&o)[4]) {
+  const uint64_t vv[1] = {v};
+  const bool in[1] = {true};
+  float oo[1][4];
+  finish_u<1>(a, vv, in, oo);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = oo[0][i];
 }
 
 __device__ __forceinline__ uint2 pack_bf16x4(const float (&o)[4]) {
@@ -179,6 +207,8 @@ __device__ __forceinline__ void store4(const FinishKernelArgs& a, uint64_t v, co
   }
 }
 
+constexpr uint32_t kElemsUnroll = 2;
+
 template <bool kPeer>
 __global__ void __launch_bounds__(kFinishThreads) finish_elems_kernel(FinishKernelArgs a) {
   __shared__ uint32_t s_epoch, s_ok;
@@ -188,12 +218,22 @@ __global__ void __launch_bounds__(kFinishThreads) finish_elems_kernel(FinishKern
     e = peer_enter(a, &s_epoch, &s_ok);
     ok = s_ok != 0;
   }
+  constexpr uint32_t U = kElemsUnroll;
   if (ok)
-    for (uint64_t v = a.lo + blockIdx.x * uint64_t(kFinishThreads) + threadIdx.x; v < a.hi;
-         v += uint64_t(gridDim.x) * kFinishThreads) {
-      float o[4];
-      finish4(a, v, o);
-      store4(a, v, o);
+    for (uint64_t v0 = a.lo + blockIdx.x * uint64_t(kFinishThreads * U) + threadIdx.x; v0 < a.hi;
+         v0 += uint64_t(gridDim.x) * kFinishThreads * U) {
+      uint64_t v[U];
+      bool in[U];
+#pragma unroll
+      for (uint32_t u = 0; u < U; ++u) {
+        v[u] = v0 + u * kFinishThreads;
+        in[u] = v[u] < a.hi;
+      }
+      float o[U][4];
+      finish_u<U>(a, v, in, o);
+#pragma unroll
+      for (uint32_t u = 0; u < U; ++u)
+        if (in[u]) store4(a, v[u], o[u]);
     }
   if constexpr (kPeer) peer_exit(a, e);
 }
@@ -291,6 +331,22 @@ uint32_t norm_cluster(uint64_t rows, uint32_t hidden) {
   return 1;
 }
 
+// CTAs of `kernel` (kFinishThreads threads) resident on the current device at
+// once, cached per device.
+template <typename Kernel>
+uint32_t resident_ctas(Kernel kernel) {
+  static int cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int sms = 0, per = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, kFinishThreads, 0);
+    cache[dev] = (per > 0 ? per : 1) * (sms > 0 ? sms : 148);
+  }
+  return uint32_t(cache[dev]);
+}
+
 template <bool kPeer, uint32_t kPer>
 cudaError_t launch_norm_t(const FinishKernelArgs& a, uint32_t C, uint32_t clusters,
                           cudaStream_t stream) {
@@ -313,8 +369,9 @@ cudaError_t launch_finish_any(FinishKernelArgs a, uint64_t rows, cudaStream_t st
   const bool norm = a.dest[0].norm != nullptr;
   if (!norm) {
     const uint64_t n = a.hi - a.lo;
-    uint64_t want = (n + kFinishThreads - 1) / kFinishThreads;
-    if (want > 148 * 8) want = 148 * 8;
+    uint64_t want = (n + kFinishThreads * kElemsUnroll - 1) / (kFinishThreads * kElemsUnroll);
+    const uint32_t resident = resident_ctas(finish_elems_kernel<kPeer>);
+    if (want > resident) want = resident;  // one wave: every CTA waits on the peers once
     if (want == 0) want = 1;  // a peer rank with an empty slice still joins the barrier
     finish_elems_kernel<kPeer><<<static_cast<uint32_t>(want), kFinishThreads, 0, stream>>>(a);
     return cudaPeekAtLastError();
@@ -323,9 +380,14 @@ cudaError_t launch_finish_any(FinishKernelArgs a, uint64_t rows, cudaStream_t st
   const uint32_t q = a.hidden / 4 / C;
   if (q > kFinishThreads * kNormMaxPer) return cudaErrorInvalidValue;
   const uint64_t range = a.hi - a.lo;
-  uint64_t clusters = range < 148 * 8 / C ? range : 148 * 8 / C;
-  if (clusters == 0) clusters = 1;
   const uint32_t per = (q + kFinishThreads - 1) / kFinishThreads;
+  uint64_t clusters = range;
+  uint32_t resident = 0;
+  if (per <= 1) resident = resident_ctas(finish_norm_kernel<kPeer, 1>);
+  else if (per <= 2) resident = resident_ctas(finish_norm_kernel<kPeer, 2>);
+  else resident = resident_ctas(finish_norm_kernel<kPeer, 4>);
+  if (clusters > resident / C) clusters = resident / C;
+  if (clusters == 0) clusters = 1;
   if (per <= 1) return launch_norm_t<kPeer, 1>(a, C, uint32_t(clusters), stream);
   if (per <= 2) return launch_norm_t<kPeer, 2>(a, C, uint32_t(clusters), stream);
   return launch_norm_t<kPeer, 4>(a, C, uint32_t(clusters), stream);

@@ -89,8 +89,7 @@ class CudaIpc:
         abi.check(self.L.glmaxx_ipc_close(ptr), "ipc_close")
 
     def zero(self, ptr: int, nbytes: int) -> None:
-        abi.check(self.L.glmaxx_memset_zero(ptr, nbytes, torch.cuda.current_stream().cuda_stream),
-                  "memset_zero")
+        device_view(ptr, (nbytes // 4,), torch.int32, torch.cuda.current_device()).zero_()
         torch.cuda.current_stream().synchronize()
 
 
