@@ -470,19 +470,27 @@ def run_ours(args):
             else:
                 dist.all_reduce(outs[-1])
 
-        n_red = max(10, min(args.steps, 200))
+        # a CUDA graph of 10 launches, so that host launch cost stays out of the time
+        per_graph, n_rep = 10, max(2, min(args.steps, 200) // 10)
         with torch.cuda.stream(stream):
             for _ in range(5):
                 one_reduce()
             stream.synchronize()
+            rgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(rgraph, stream=stream):
+                for _ in range(per_graph):
+                    one_reduce()
+            rgraph.replay()
+            stream.synchronize()
             dist.barrier()
             torch.cuda.synchronize()
             e0.record(stream)
-            for _ in range(n_red):
-                one_reduce()
+            for _ in range(n_rep):
+                rgraph.replay()
             e1.record(stream)
         torch.cuda.synchronize()
-        red_ms = e0.elapsed_time(e1) / n_red
+        del rgraph
+        red_ms = e0.elapsed_time(e1) / (n_rep * per_graph)
         t = torch.tensor([red_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         red_ms = float(t.item())

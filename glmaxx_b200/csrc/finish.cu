@@ -139,8 +139,8 @@ __device__ void peer_exit(const FinishKernelArgs& a, uint32_t e) {
 }
 
 // ------------------------------------------------------------ arithmetic
-// U float4 groups at once, every load in flight before the first add.
-template <uint32_t U>
+// U float4 groups at once, every load in flight before the first add; R >= ranks.
+template <uint32_t U, uint32_t R>
 __device__ __forceinline__ void finish_u(const FinishKernelArgs& a, const uint64_t (&v)[U],
                                          const bool (&in)[U], float (&o)[U][4]) {
 #pragma unroll
@@ -166,29 +166,20 @@ __device__ __forceinline__ void finish_u(const FinishKernelArgs& a, const uint64
           o[u][0] = __fadd_rn(o[u][0], t.x), o[u][1] = __fadd_rn(o[u][1], t.y);
           o[u][2] = __fadd_rn(o[u][2], t.z), o[u][3] = __fadd_rn(o[u][3], t.w);
         }
-  float4 t[U][kMaxRanks];
+  float4 t[U][R];
 #pragma unroll
   for (uint32_t u = 0; u < U; ++u)
 #pragma unroll
-    for (uint32_t r = 0; r < kMaxRanks; ++r)
+    for (uint32_t r = 0; r < R; ++r)
       if (in[u] && r < a.ranks) t[u][r] = __ldcg(reinterpret_cast<const float4*>(a.partials[r]) + v[u]);
 #pragma unroll
   for (uint32_t u = 0; u < U; ++u)
 #pragma unroll
-    for (uint32_t r = 0; r < kMaxRanks; ++r)
+    for (uint32_t r = 0; r < R; ++r)
       if (in[u] && r < a.ranks) {
         o[u][0] = __fadd_rn(o[u][0], t[u][r].x), o[u][1] = __fadd_rn(o[u][1], t[u][r].y);
         o[u][2] = __fadd_rn(o[u][2], t[u][r].z), o[u][3] = __fadd_rn(o[u][3], t[u][r].w);
       }
-}
-
-__device__ __forceinline__ void finish4(const FinishKernelArgs& a, uint64_t v, float (&o)[4]) {
-  const uint64_t vv[1] = {v};
-  const bool in[1] = {true};
-  float oo[1][4];
-  finish_u<1>(a, vv, in, oo);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) o[i] = oo[0][i];
 }
 
 __device__ __forceinline__ uint2 pack_bf16x4(const float (&o)[4]) {
@@ -207,9 +198,9 @@ __device__ __forceinline__ void store4(const FinishKernelArgs& a, uint64_t v, co
   }
 }
 
-constexpr uint32_t kElemsUnroll = 2;
-
-template <bool kPeer>
+// R: ranks rounded up to 2, 4 or 8; U: float4 groups per thread and iteration
+// (U * R loads in flight)
+template <bool kPeer, uint32_t R, uint32_t U>
 __global__ void __launch_bounds__(kFinishThreads) finish_elems_kernel(FinishKernelArgs a) {
   __shared__ uint32_t s_epoch, s_ok;
   uint32_t e = 0;
@@ -218,7 +209,6 @@ __global__ void __launch_bounds__(kFinishThreads) finish_elems_kernel(FinishKern
     e = peer_enter(a, &s_epoch, &s_ok);
     ok = s_ok != 0;
   }
-  constexpr uint32_t U = kElemsUnroll;
   if (ok)
     for (uint64_t v0 = a.lo + blockIdx.x * uint64_t(kFinishThreads * U) + threadIdx.x; v0 < a.hi;
          v0 += uint64_t(gridDim.x) * kFinishThreads * U) {
@@ -230,7 +220,7 @@ __global__ void __launch_bounds__(kFinishThreads) finish_elems_kernel(FinishKern
         in[u] = v[u] < a.hi;
       }
       float o[U][4];
-      finish_u<U>(a, v, in, o);
+      finish_u<U, R>(a, v, in, o);
 #pragma unroll
       for (uint32_t u = 0; u < U; ++u)
         if (in[u]) store4(a, v[u], o[u]);
@@ -262,7 +252,7 @@ __device__ __forceinline__ float ld_cluster_f32(const float* smem, uint32_t cta)
 
 // One cluster of C CTAs per row (grid-stride over the row range); CTA c of the
 // cluster owns float4 columns [c*q, (c+1)*q) of the row, q = hidden/4/C <= 256*kPer.
-template <bool kPeer, uint32_t kPer>
+template <bool kPeer, uint32_t R, uint32_t kPer>
 __global__ void __launch_bounds__(kFinishThreads) finish_norm_kernel(FinishKernelArgs a) {
   __shared__ uint32_t s_epoch, s_ok;
   __shared__ float warp_ss[kFinishThreads / 32];
@@ -282,16 +272,36 @@ __global__ void __launch_bounds__(kFinishThreads) finish_norm_kernel(FinishKerne
     float o[kPer][4];
     float ss = 0.0f;
     const uint64_t base = row * h4 + uint64_t(c) * q;
+    uint64_t v[kPer];
+    bool in[kPer];
 #pragma unroll
     for (uint32_t k = 0; k < kPer; ++k) {
       const uint32_t j = threadIdx.x + k * kFinishThreads;
-      if (ok && j < q) {
-        finish4(a, base + j, o[k]);
-        store4(a, base + j, o[k]);
+      v[k] = base + j;
+      in[k] = ok && j < q;
+    }
+    // at most 8 partial loads in flight per thread (registers)
+    constexpr uint32_t kChunk = (8 / R) < kPer ? (8 / R) : kPer;
+#pragma unroll
+    for (uint32_t k0 = 0; k0 < kPer; k0 += kChunk) {
+      uint64_t vv[kChunk];
+      bool ii[kChunk];
+      float oo[kChunk][4];
+#pragma unroll
+      for (uint32_t c = 0; c < kChunk; ++c) vv[c] = v[k0 + c], ii[c] = in[k0 + c];
+      finish_u<kChunk, R>(a, vv, ii, oo);
+#pragma unroll
+      for (uint32_t c = 0; c < kChunk; ++c)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[k0 + c][i] = oo[c][i];
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kPer; ++k)
+      if (in[k]) {
+        store4(a, v[k], o[k]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) ss = __fmaf_rn(o[k][i], o[k][i], ss);
       }
-    }
 #pragma unroll
     for (uint32_t off = 16; off > 0; off >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, off));
     if ((threadIdx.x & 31) == 0) warp_ss[threadIdx.x >> 5] = ss;
@@ -308,17 +318,14 @@ __global__ void __launch_bounds__(kFinishThreads) finish_norm_kernel(FinishKerne
     cluster_sync_all();  // every CTA has read cta_ss before the next row rewrites it
     const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(total, float(a.hidden)), a.eps));
 #pragma unroll
-    for (uint32_t k = 0; k < kPer; ++k) {
-      const uint32_t j = threadIdx.x + k * kFinishThreads;
-      if (ok && j < q) {
+    for (uint32_t k = 0; k < kPer; ++k)
+      if (in[k]) {
         float n[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) n[i] = __fmul_rn(o[k][i], inv);
         const uint2 b = pack_bf16x4(n);
-        for (uint32_t d = 0; d < a.dests; ++d)
-          reinterpret_cast<uint2*>(a.dest[d].norm)[base + j] = b;
+        for (uint32_t d = 0; d < a.dests; ++d) reinterpret_cast<uint2*>(a.dest[d].norm)[v[k]] = b;
       }
-    }
   }
   if constexpr (kPeer) peer_exit(a, e);
 }
@@ -347,7 +354,7 @@ uint32_t resident_ctas(Kernel kernel) {
   return uint32_t(cache[dev]);
 }
 
-template <bool kPeer, uint32_t kPer>
+template <bool kPeer, uint32_t R, uint32_t kPer>
 cudaError_t launch_norm_t(const FinishKernelArgs& a, uint32_t C, uint32_t clusters,
                           cudaStream_t stream) {
   cudaLaunchConfig_t cfg{};
@@ -361,36 +368,56 @@ cudaError_t launch_norm_t(const FinishKernelArgs& a, uint32_t C, uint32_t cluste
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, finish_norm_kernel<kPeer, kPer>, a);
+  return cudaLaunchKernelEx(&cfg, finish_norm_kernel<kPeer, R, kPer>, a);
+}
+
+// clusters: one per row up to one resident wave
+template <bool kPeer, uint32_t R, uint32_t kPer>
+cudaError_t launch_norm_r(const FinishKernelArgs& a, uint32_t C, uint64_t rows,
+                          cudaStream_t stream) {
+  const uint32_t resident = resident_ctas(finish_norm_kernel<kPeer, R, kPer>);
+  uint64_t clusters = rows < resident / C ? rows : resident / C;
+  if (clusters == 0) clusters = 1;  // a peer rank with no rows still joins the barrier
+  return launch_norm_t<kPeer, R, kPer>(a, C, uint32_t(clusters), stream);
+}
+
+template <bool kPeer, uint32_t R, uint32_t U>
+cudaError_t launch_elems(const FinishKernelArgs& a, cudaStream_t stream) {
+  const uint64_t n = a.hi - a.lo;
+  uint64_t want = (n + kFinishThreads * U - 1) / (kFinishThreads * U);
+  const uint32_t resident = resident_ctas(finish_elems_kernel<kPeer, R, U>);
+  if (want > resident) want = resident;  // one wave: every CTA waits on the peers once
+  if (want == 0) want = 1;  // a peer rank with an empty slice still joins the barrier
+  finish_elems_kernel<kPeer, R, U><<<static_cast<uint32_t>(want), kFinishThreads, 0, stream>>>(a);
+  return cudaPeekAtLastError();
 }
 
 template <bool kPeer>
 cudaError_t launch_finish_any(FinishKernelArgs a, uint64_t rows, cudaStream_t stream) {
   const bool norm = a.dest[0].norm != nullptr;
   if (!norm) {
-    const uint64_t n = a.hi - a.lo;
-    uint64_t want = (n + kFinishThreads * kElemsUnroll - 1) / (kFinishThreads * kElemsUnroll);
-    const uint32_t resident = resident_ctas(finish_elems_kernel<kPeer>);
-    if (want > resident) want = resident;  // one wave: every CTA waits on the peers once
-    if (want == 0) want = 1;  // a peer rank with an empty slice still joins the barrier
-    finish_elems_kernel<kPeer><<<static_cast<uint32_t>(want), kFinishThreads, 0, stream>>>(a);
-    return cudaPeekAtLastError();
+    if (a.ranks <= 2) return launch_elems<kPeer, 2, 4>(a, stream);
+    if (a.ranks <= 4) return launch_elems<kPeer, 4, 2>(a, stream);
+    return launch_elems<kPeer, 8, 2>(a, stream);
   }
   const uint32_t C = norm_cluster(rows, a.hidden);
   const uint32_t q = a.hidden / 4 / C;
   if (q > kFinishThreads * kNormMaxPer) return cudaErrorInvalidValue;
   const uint64_t range = a.hi - a.lo;
   const uint32_t per = (q + kFinishThreads - 1) / kFinishThreads;
-  uint64_t clusters = range;
-  uint32_t resident = 0;
-  if (per <= 1) resident = resident_ctas(finish_norm_kernel<kPeer, 1>);
-  else if (per <= 2) resident = resident_ctas(finish_norm_kernel<kPeer, 2>);
-  else resident = resident_ctas(finish_norm_kernel<kPeer, 4>);
-  if (clusters > resident / C) clusters = resident / C;
-  if (clusters == 0) clusters = 1;
-  if (per <= 1) return launch_norm_t<kPeer, 1>(a, C, uint32_t(clusters), stream);
-  if (per <= 2) return launch_norm_t<kPeer, 2>(a, C, uint32_t(clusters), stream);
-  return launch_norm_t<kPeer, 4>(a, C, uint32_t(clusters), stream);
+  if (a.ranks <= 2) {
+    if (per <= 1) return launch_norm_r<kPeer, 2, 1>(a, C, range, stream);
+    if (per <= 2) return launch_norm_r<kPeer, 2, 2>(a, C, range, stream);
+    return launch_norm_r<kPeer, 2, 4>(a, C, range, stream);
+  }
+  if (a.ranks <= 4) {
+    if (per <= 1) return launch_norm_r<kPeer, 4, 1>(a, C, range, stream);
+    if (per <= 2) return launch_norm_r<kPeer, 4, 2>(a, C, range, stream);
+    return launch_norm_r<kPeer, 4, 4>(a, C, range, stream);
+  }
+  if (per <= 1) return launch_norm_r<kPeer, 8, 1>(a, C, range, stream);
+  if (per <= 2) return launch_norm_r<kPeer, 8, 2>(a, C, range, stream);
+  return launch_norm_r<kPeer, 8, 4>(a, C, range, stream);
 }
 
 FinishKernelArgs kernel_args(const FinishArgs& f) {

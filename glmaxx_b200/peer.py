@@ -225,7 +225,10 @@ class PeerGroup:
 
 
 def two_shot_pays(elements: int, ranks: int) -> bool:
-    """Two-shot moves 2(N-1)/N of the partial across NVLink per rank against
-    (N-1) for one-shot, for one extra pass of stores; below about a megabyte the
-    launch and barrier latency dominate both."""
-    return ranks > 2 and elements * 4 >= (1 << 20)
+    """Two-shot moves (N-1)/N of the partial across NVLink each way per rank
+    against N-1 partials inbound for one-shot, for one more pass of stores and a
+    system-scope fence per CTA.  Measured on two B200s: one-shot wins at 1.5 MB
+    (10.7 vs 14.3 us), two-shot from 12.6 MB on (31 vs 35 us); with more ranks the
+    one-shot inbound volume grows N-1 times, so two-shot wins from about 1 MB."""
+    nbytes = elements * 4
+    return nbytes >= (8 << 20) if ranks == 2 else (ranks > 2 and nbytes >= (1 << 20))

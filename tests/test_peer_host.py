@@ -33,8 +33,9 @@ def test_layout_is_aligned_and_deterministic():
 
 def test_two_shot_threshold():
     assert not two_shot_pays(T * H, 2)
-    assert two_shot_pays(T * H, 8)
-    assert not two_shot_pays(1024, 8)
+    assert two_shot_pays(2048 * H, 2)
+    assert two_shot_pays(T * H, 8) and two_shot_pays(T * H, 4)
+    assert not two_shot_pays(1024, 8) and not two_shot_pays(T * H, 1)
 
 
 class FakeIpc:
