@@ -274,3 +274,37 @@ def test_gpu_layer_deterministic_decode():
     torch.cuda.synchronize()
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("path,T", [(abi.DECODE_PERSISTENT, 64), (abi.PREFILL_GROUPED, 512)])
+def test_gpu_layer_in_cuda_graph_matches_eager(path, T):
+    """The shared expert runs on a side stream forked from the launch stream and
+    joined before its consumer; captured in a CUDA graph the fork and join become
+    graph edges.  Replays on new inputs equal eager launches (bit for bit on the
+    deterministic decode path, to the layer tolerance on the atomic prefill path)."""
+    cfg = MoEConfig(tp=4, rank=1)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=11, device=dev)
+    layer = RoutedMoE(cfg, w, T)
+    x = synth.make_input(T, cfg.hidden, seed=11, device=dev)
+    out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=dev)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer(x, out, path=path)  # eager warm-up on the capture stream
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            layer(x, out, path=path)
+    for seed in (12, 13):
+        x.copy_(synth.make_input(T, cfg.hidden, seed=seed, device=dev))
+        g.replay()
+        torch.cuda.synchronize()
+        got = out.clone()
+        ref = layer(x, path=path).clone()
+        torch.cuda.synchronize()
+        assert layer.device_status() == []
+        if path == abi.DECODE_PERSISTENT:
+            assert torch.equal(got, ref)
+        else:
+            assert_layer_close(got.cpu().numpy(), ref.cpu().numpy(), "graph vs eager")
