@@ -252,6 +252,129 @@ __device__ __forceinline__ float fkey_inv(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// Same selection with lane l owning the 8 consecutive experts 8l .. 8l+7, for
+// shapes whose groups are whole runs of lanes (E % 8 == 0, gs = E / groups a
+// multiple of 8 with gs / 8 a power of two): a group's top-2 merges over its
+// lanes in log2(gs/8) shuffles, every lane ranks its group against the others by
+// one shuffle per group, and each top-k round is a lane-local argmax plus two
+// warp reductions.  Tie rules are the reference's: the lower group index and the
+// lower expert index win, so the result is the same bits as the general kernel.
+__global__ void __launch_bounds__(256) router_select_runs_kernel(
+    const float* __restrict__ partial, const float* __restrict__ bias, uint32_t T, uint32_t E,
+    uint32_t groups, uint32_t topk_groups, uint32_t top_k, float route_scale,
+    uint16_t* __restrict__ experts_out, float* __restrict__ weights_out,
+    uint32_t* __restrict__ bitmap, uint32_t bitmap_stride, uint32_t* __restrict__ status) {
+  constexpr uint32_t kFull = 0xffffffffu;
+  constexpr uint32_t kNone = 0u;  // below every finite choice
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  const uint32_t e0 = lane * 8;
+  const bool mine = e0 < E;  // E % 8 == 0: a lane's experts are all valid or all absent
+  // logits: the 8 chunk partials in chunk order, every load in flight first
+  float4 p[8][2];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const float4* src = reinterpret_cast<const float4*>(partial + (uint64_t(c) * T + t) * E + e0);
+    p[c][0] = mine ? src[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+    p[c][1] = mine ? src[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+  if (mine) {
+    b0 = reinterpret_cast<const float4*>(bias + e0)[0];
+    b1 = reinterpret_cast<const float4*>(bias + e0)[1];
+  }
+  float L[8] = {p[0][0].x, p[0][0].y, p[0][0].z, p[0][0].w,
+                p[0][1].x, p[0][1].y, p[0][1].z, p[0][1].w};
+#pragma unroll
+  for (int c = 1; c < 8; ++c) {
+    const float q[8] = {p[c][0].x, p[c][0].y, p[c][0].z, p[c][0].w,
+                        p[c][1].x, p[c][1].y, p[c][1].z, p[c][1].w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) L[j] = __fadd_rn(L[j], q[j]);
+  }
+  const float bj[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  float sc[8];
+  uint32_t key[8];
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sc[j] = 0.f;
+    key[j] = kNone;
+    if (mine) {
+      if (!isfinite(L[j])) bad = true;
+      sc[j] = router_sigmoid(L[j]);
+      key[j] = fkey(__fadd_rn(sc[j], bj[j]));
+    }
+  }
+  // group score = top1 + top2 of the group's choices (multiset top-2)
+  const uint32_t gs = E / groups, lpg = gs / 8;  // lanes per group
+  uint32_t k1 = kNone, k2 = kNone;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (key[j] > k1) {
+      k2 = k1;
+      k1 = key[j];
+    } else if (key[j] > k2) {
+      k2 = key[j];
+    }
+  }
+  for (uint32_t off = 1; off < lpg; off <<= 1) {
+    const uint32_t o1 = __shfl_xor_sync(kFull, k1, off), o2 = __shfl_xor_sync(kFull, k2, off);
+    const uint32_t n1 = max(k1, o1), n2 = max(min(k1, o1), max(k2, o2));
+    k1 = n1;
+    k2 = n2;
+  }
+  const float gscore = __fadd_rn(fkey_inv(k1), fkey_inv(k2));  // gs >= 8
+  // keep the best topk_groups groups (ties -> lower group index)
+  const uint32_t g = lane / lpg;
+  uint32_t beaten = 0;
+  for (uint32_t h = 0; h < groups; ++h) {
+    const float other = __shfl_sync(kFull, gscore, h * lpg);
+    if (other > gscore || (other == gscore && h < g)) ++beaten;
+  }
+  const bool kept = mine && beaten < topk_groups;
+  // top_k experts by choice among the kept groups (ties -> lower expert index)
+  uint32_t taken = 0;
+  uint32_t my_e = 0;
+  float my_s = 0.f, denom = 0.f;
+  for (uint32_t k = 0; k < top_k; ++k) {
+    uint32_t bk = kNone, bj_ = 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (kept && !((taken >> j) & 1u) && (bj_ == 8 || key[j] > bk)) {
+        bk = key[j];
+        bj_ = j;
+      }
+    const uint32_t mk = __reduce_max_sync(kFull, bk);
+    const uint32_t wl = __reduce_min_sync(kFull, (bj_ != 8 && bk == mk) ? lane : 32u);
+    if (wl == 32u) {
+      bad = true;
+      continue;
+    }
+    float s_win = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (uint32_t(j) == bj_) s_win = sc[j];
+    const float ws_ = __shfl_sync(kFull, s_win, wl);
+    const uint32_t we = wl * 8 + __shfl_sync(kFull, bj_, wl);
+    if (lane == wl) taken |= 1u << bj_;
+    denom = k == 0 ? ws_ : __fadd_rn(denom, ws_);
+    if (lane == k) {
+      my_e = we;
+      my_s = ws_;
+    }
+  }
+  if (lane < top_k) {
+    const float wgt = __fmul_rn(__fdiv_rn(my_s, denom), route_scale);
+    experts_out[uint64_t(t) * top_k + lane] = static_cast<uint16_t>(my_e);
+    weights_out[uint64_t(t) * top_k + lane] = wgt;
+    atomicOr(&bitmap[uint64_t(my_e) * bitmap_stride + t / 32], 1u << (t % 32));
+  }
+  bad = __any_sync(kFull, bad);
+  if (bad && lane == 0 && status) atomicOr(status, kStatusNonFiniteInput);
+}
+
 __global__ void __launch_bounds__(256) router_select_kernel(
     const float* __restrict__ partial, const float* __restrict__ bias, uint32_t T, uint32_t E,
     uint32_t groups, uint32_t topk_groups, uint32_t top_k, float route_scale,
@@ -394,7 +517,33 @@ __global__ void __launch_bounds__(1024) compact_kernel(
   // no_tiles[e] != 0 (optional): expert e gets rows but no GEMM tiles (an EXL3 expert)
   __shared__ uint32_t cnt_s[256], toff_s[257], poff_s[257], off_s[257];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (uint32_t e = warp; e < E; e += 32) {
+  if (W <= 32 && E <= 256) {
+    // T <= 1024: one bitmap word per lane; the warp's 8 experts (warp + 32q) load
+    // together and their scans interleave
+    uint32_t pc[8], incl[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t e = warp + 32u * q;
+      pc[q] = (e < E && lane < W) ? __popc(bitmap[uint64_t(e) * W + lane]) : 0u;
+      incl[q] = pc[q];
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, incl[q], off);
+        if (lane >= uint32_t(off)) incl[q] += o;
+      }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t e = warp + 32u * q;
+      if (e < E) {
+        if (lane < W) wprefix[uint64_t(e) * W + lane] = incl[q] - pc[q];
+        if (lane == 31) cnt_s[e] = incl[q];
+      }
+    }
+  }
+  for (uint32_t e = warp; (W > 32 || E > 256) && e < E; e += 32) {
     uint32_t running = 0;
     for (uint32_t w0 = 0; w0 < W; w0 += 32) {
       const uint32_t w = w0 + lane;
@@ -497,18 +646,49 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return red[32];
 }
 
-__global__ void __launch_bounds__(256) quant_scatter_kernel(QuantScatterArgs a) {
+// One CTA per token, one thread per 16-element NVFP4 block (H/16 threads): the
+// token's global scale from the block-wide amax, each block encoded by its own
+// thread, the four scale bytes of a 64-element k-block gathered by shuffles, and
+// the encoded row stored into every slot's compacted row.
+__global__ void __launch_bounds__(1024) quant_scatter_kernel(QuantScatterArgs a) {
   __shared__ float red[33];
-  const uint32_t t = blockIdx.x, kb = threadIdx.x;
-  const uint32_t KB = a.H / 64;
-  const bool active = kb < KB;
-  float v[64];
+  __shared__ uint32_t s_row[32], s_prow[32];
+  const uint32_t t = blockIdx.x, b16 = threadIdx.x;
+  const uint32_t KB = a.H / 64, B16 = a.H / 16;
+  const bool active = b16 < B16;
+  // the compacted row and scale row of each slot: one thread per slot, its two
+  // dependent loads overlapping the row loads below
+  if (b16 < a.top_k) {
+    const uint32_t slot = b16, i = t * a.top_k + slot;
+    const uint32_t e = a.route_experts[i];
+    uint32_t row = 0xffffffffu, prow = 0xffffffffu;
+    if (e < a.E) {
+      const uint32_t W = (a.T + 31) / 32;
+      const uint32_t word = a.bitmap[uint64_t(e) * W + t / 32];
+      const uint32_t rank =
+          a.wprefix[uint64_t(e) * W + t / 32] + __popc(word & ((1u << (t % 32)) - 1u));
+      // scale-factor row: every n tile of a.nt rows owns a whole 128-row atom
+      prow = a.poffs[e] + (rank / a.nt) * 128 + rank % a.nt;
+      row = a.offsets[e] + rank;  // compacted row
+      if (prow >= a.sf_row_cap || row >= a.T * a.top_k) row = prow = 0xffffffffu;
+    }
+    s_row[slot] = row;
+    s_prow[slot] = prow;
+    if (row != 0xffffffffu) {
+      a.row_token[row] = t;
+      a.row_slot[row] = slot;
+      a.row_weight[row] = a.route_weights[i];
+      a.row_prow[row] = prow;
+      a.route_row[i] = row;
+    }
+  }
+  float v[16];
   float amax = 0.f;
   bool finite = true;
   if (active) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.x + uint64_t(t) * a.H + kb * 64);
+    const uint4* src = reinterpret_cast<const uint4*>(a.x + uint64_t(t) * a.H + b16 * 16);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < 2; ++q) {
       const uint4 u = src[q];
       const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -518,56 +698,50 @@ __global__ void __launch_bounds__(256) quant_scatter_kernel(QuantScatterArgs a) 
       }
     }
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 16; ++i) {
       finite = finite && isfinite(v[i]);
       amax = fmaxf(amax, fabsf(v[i]));
     }
   }
   if (!finite) atomicOr(a.status, kStatusNonFiniteInput);
-  amax = block_max(amax, red);
-  if (!active) return;
+  amax = block_max(amax, red);  // its barriers also publish s_row / s_prow
   const float gscale = global_scale_of(amax);
-  uint2 packed[4];
-  uint32_t sfw = 0;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
-  const uint32_t W = (a.T + 31) / 32;
+  uint2 packed = make_uint2(0, 0);
+  uint32_t sc = 0;
+  if (active) sc = nvfp4_block(v, gscale, &packed);
+  // the 4 scale bytes of k-block b16 / 4 (B16 % 4 == 0, so the 4 threads share a warp)
+  const uint32_t lane = threadIdx.x & 31, q0 = lane & ~3u;
+  const uint32_t sfw = __shfl_sync(0xffffffffu, sc, q0) | (__shfl_sync(0xffffffffu, sc, q0 + 1) << 8) |
+                       (__shfl_sync(0xffffffffu, sc, q0 + 2) << 16) |
+                       (__shfl_sync(0xffffffffu, sc, q0 + 3) << 24);
+  if (!active) return;
   for (uint32_t slot = 0; slot < a.top_k; ++slot) {
-    const uint32_t i = t * a.top_k + slot;
-    const uint32_t e = a.route_experts[i];
-    if (e >= a.E) continue;
-    const uint32_t word = a.bitmap[uint64_t(e) * W + t / 32];
-    const uint32_t rank = a.wprefix[uint64_t(e) * W + t / 32] + __popc(word & ((1u << (t % 32)) - 1u));
-    // scale-factor row: every n tile of a.nt rows owns a whole 128-row atom
-    const uint32_t prow = a.poffs[e] + (rank / a.nt) * 128 + rank % a.nt;
-    const uint32_t row = a.offsets[e] + rank;  // compacted row
-    if (prow >= a.sf_row_cap || row >= a.T * a.top_k) continue;
-    uint4* dst = reinterpret_cast<uint4*>(a.xq + uint64_t(row) * (a.H / 2) + kb * 32);
-    dst[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
-    dst[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
-    *reinterpret_cast<uint32_t*>(a.xsf + sf_offset(prow, kb, 0, KB)) = sfw;
-    if (kb == 0) {
-      a.row_token[row] = t;
-      a.row_slot[row] = slot;
-      a.row_weight[row] = a.route_weights[i];
-      a.row_gscale[row] = gscale;
-      a.row_prow[row] = prow;
-      a.route_row[i] = row;
-    }
+    const uint32_t row = s_row[slot], prow = s_prow[slot];
+    if (row == 0xffffffffu) continue;
+    reinterpret_cast<uint2*>(a.xq + uint64_t(row) * (a.H / 2))[b16] = packed;
+    if ((b16 & 3) == 0)
+      *reinterpret_cast<uint32_t*>(a.xsf + sf_offset(prow, b16 / 4, 0, KB)) = sfw;
+    if (b16 == 0) a.row_gscale[row] = gscale;
   }
 }
 
 // ---------------------------------------------------------------------------
-// FC2 input: NVFP4-quantise each assignment's h row (K = I).  Threads of one
-// row are KB2 = I/64 consecutive lanes (I <= 2048), amax by a segmented
-// butterfly.
+// FC2 input: NVFP4-quantise each assignment's h row (K = I).  One thread per
+// 16-element block: a row's R = I/16 threads are consecutive (R = 16..128,
+// 128-thread blocks); its amax is a butterfly over min(R, 32) lanes, then over
+// the row's warps through shared memory when R > 32.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) fc2_quant_kernel(Fc2QuantArgs a) {
-  const uint32_t KB2 = a.I / 64;
-  const uint32_t rows_per_block = 256 / KB2;
-  const uint32_t r_local = threadIdx.x / KB2, kb = threadIdx.x % KB2;
+  __shared__ float wmax[8];
+  const uint32_t R = a.I / 16;
+  const uint32_t rows_per_block = blockDim.x / R;
+  const uint32_t r_local = threadIdx.x / R, b16 = threadIdx.x % R;
   const uint32_t row = blockIdx.x * rows_per_block + r_local;
+  // rows below a.count (the plane's capacity) are readable whatever the live
+  // count, so the h loads, the scale row and the count are all in flight at once
+  const bool in_plane = row < a.count;
   const uint32_t count = a.count_ptr ? min(*a.count_ptr, a.count) : a.count;
+  const uint32_t prow = in_plane ? a.row_prow[row] : 0xffffffffu;
   bool active = row < count;
   if (active && a.skip_codec != nullptr) {
     uint32_t lo = 0, hi = a.E;  // expert of the row: offsets[lo] <= row < offsets[hi]
@@ -577,13 +751,13 @@ __global__ void __launch_bounds__(256) fc2_quant_kernel(Fc2QuantArgs a) {
     }
     active = a.skip_codec[lo] != 1;
   }
-  float v[64];
+  float v[16];
   float amax = 0.f;
   bool finite = true;
-  if (active) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.h + uint64_t(row) * a.I + kb * 64);
+  if (in_plane) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.h + uint64_t(row) * a.I + b16 * 16);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < 2; ++q) {
       const uint4 u = src[q];
       const uint32_t wds[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -593,27 +767,36 @@ __global__ void __launch_bounds__(256) fc2_quant_kernel(Fc2QuantArgs a) {
       }
     }
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
+    for (int i = 0; i < 16; ++i) {
       finite = finite && isfinite(v[i]);
       amax = fmaxf(amax, fabsf(v[i]));
     }
   }
-  for (uint32_t off = 1; off < KB2; off <<= 1)
+  const uint32_t span = R < 32 ? R : 32;
+  for (uint32_t off = 1; off < span; off <<= 1)
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if (R > 32) {  // a row spans R/32 warps: combine them
+    const uint32_t warp = threadIdx.x >> 5, first = r_local * (R / 32);
+    if ((threadIdx.x & 31) == 0) wmax[warp] = amax;
+    __syncthreads();
+    amax = wmax[first];
+    for (uint32_t w = 1; w < R / 32; ++w) amax = fmaxf(amax, wmax[first + w]);
+  }
+  const float gscale = global_scale_of(amax);
+  uint2 packed = make_uint2(0, 0);
+  uint32_t sc = 0;
+  if (active) sc = nvfp4_block(v, gscale, &packed);
+  const uint32_t lane = threadIdx.x & 31, q0 = lane & ~3u;
+  const uint32_t sfw = __shfl_sync(0xffffffffu, sc, q0) | (__shfl_sync(0xffffffffu, sc, q0 + 1) << 8) |
+                       (__shfl_sync(0xffffffffu, sc, q0 + 2) << 16) |
+                       (__shfl_sync(0xffffffffu, sc, q0 + 3) << 24);
   if (!active) return;
   if (!finite && a.status) atomicOr(a.status, kStatusNonFiniteInput);
-  const uint32_t prow = a.row_prow[row];
   if (prow >= a.sf_row_cap) return;
-  const float gscale = global_scale_of(amax);
-  uint2 packed[4];
-  uint32_t sfw = 0;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) sfw |= nvfp4_block(&v[g * 16], gscale, &packed[g]) << (8 * g);
-  uint4* dst = reinterpret_cast<uint4*>(a.hq + uint64_t(row) * (a.I / 2) + kb * 32);
-  dst[0] = make_uint4(packed[0].x, packed[0].y, packed[1].x, packed[1].y);
-  dst[1] = make_uint4(packed[2].x, packed[2].y, packed[3].x, packed[3].y);
-  *reinterpret_cast<uint32_t*>(a.hsf + sf_offset(prow, kb, 0, KB2)) = sfw;
-  if (kb == 0) a.gscale[row] = gscale;
+  reinterpret_cast<uint2*>(a.hq + uint64_t(row) * (a.I / 2))[b16] = packed;
+  if ((b16 & 3) == 0)
+    *reinterpret_cast<uint32_t*>(a.hsf + sf_offset(prow, b16 / 4, 0, a.I / 64)) = sfw;
+  if (b16 == 0) a.gscale[row] = gscale;
 }
 
 // Compacted-order route arrays (reference ABI) from the device compaction.
@@ -798,52 +981,57 @@ __global__ void slot_reduce_kernel(SlotArgs a) {
 // order is the reference oracle's compacted accumulation order
 // (routed_fc2.rs:63-86); routed + shared follows routed_fc2.rs:250-256.
 // ---------------------------------------------------------------------------
-__global__ void combine_kernel(const float* __restrict__ plane, const uint16_t* __restrict__ experts,
-                               const float* __restrict__ shared, uint32_t shared_splits,
-                               float* __restrict__ shared_out, float* __restrict__ out, uint32_t T,
-                               uint32_t H, uint32_t top_k) {
+// Deterministic combine: out[t] = the token's slot rows summed in ascending
+// expert order, then the shared expert (its split-K slices summed in slice
+// order).  The slot keys (expert << 8 | slot, so equal experts keep slot order)
+// are ordered by a 19-comparator sorting network in registers, then the eight
+// slot rows load together in that order.  top_k <= 8, shared_splits <= 16.
+__device__ __forceinline__ void kswap(uint32_t (&k)[8], int i, int j) {
+  const uint32_t lo = min(k[i], k[j]), hi = max(k[i], k[j]);
+  k[i] = lo, k[j] = hi;
+}
+
+__device__ __forceinline__ void add4(float4& a, const float4& b) {
+  a.x = __fadd_rn(a.x, b.x);
+  a.y = __fadd_rn(a.y, b.y);
+  a.z = __fadd_rn(a.z, b.z);
+  a.w = __fadd_rn(a.w, b.w);
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(
+    const float* __restrict__ plane, const uint16_t* __restrict__ experts,
+    const float* __restrict__ shared, uint32_t shared_splits, float* __restrict__ shared_out,
+    float* __restrict__ out, uint32_t T, uint32_t H, uint32_t top_k) {
   const uint32_t t = blockIdx.y;
   const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (t >= T || c >= H) return;
-  uint32_t order[8];
-  uint32_t ex[8];
-  for (uint32_t s = 0; s < top_k; ++s) {
-    ex[s] = experts[uint64_t(t) * top_k + s];
-    order[s] = s;
-  }
-  for (uint32_t i = 1; i < top_k; ++i) {
-    const uint32_t o = order[i];
-    uint32_t j = i;
-    while (j > 0 && ex[order[j - 1]] > ex[o]) {
-      order[j] = order[j - 1];
-      --j;
-    }
-    order[j] = o;
-  }
-  float4 acc = *reinterpret_cast<const float4*>(plane + (uint64_t(t) * top_k + order[0]) * H + c);
-  for (uint32_t k = 1; k < top_k; ++k) {
-    const float4 v = *reinterpret_cast<const float4*>(plane + (uint64_t(t) * top_k + order[k]) * H + c);
-    acc.x = __fadd_rn(acc.x, v.x);
-    acc.y = __fadd_rn(acc.y, v.y);
-    acc.z = __fadd_rn(acc.z, v.z);
-    acc.w = __fadd_rn(acc.w, v.w);
-  }
+  uint32_t key[8];
+#pragma unroll
+  for (uint32_t s = 0; s < 8; ++s)
+    key[s] = s < top_k ? (uint32_t(experts[uint64_t(t) * top_k + s]) << 8) | s : 0xffffffffu;
+  kswap(key, 0, 2), kswap(key, 1, 3), kswap(key, 4, 6), kswap(key, 5, 7);
+  kswap(key, 0, 4), kswap(key, 1, 5), kswap(key, 2, 6), kswap(key, 3, 7);
+  kswap(key, 0, 1), kswap(key, 2, 3), kswap(key, 4, 5), kswap(key, 6, 7);
+  kswap(key, 2, 4), kswap(key, 3, 5);
+  kswap(key, 1, 4), kswap(key, 3, 6);
+  kswap(key, 1, 2), kswap(key, 3, 4), kswap(key, 5, 6);
+  float4 v[8];
+#pragma unroll
+  for (uint32_t k = 0; k < 8; ++k)
+    if (k < top_k)
+      v[k] = *reinterpret_cast<const float4*>(plane + (uint64_t(t) * top_k + (key[k] & 0xffu)) * H + c);
+  float4 acc = v[0];
+#pragma unroll
+  for (uint32_t k = 1; k < 8; ++k)
+    if (k < top_k) add4(acc, v[k]);
   if (shared) {
-    // shared expert = sum of its split-K partial planes in slice order
     const uint64_t stride = uint64_t(T) * H;
-    float4 s = *reinterpret_cast<const float4*>(shared + uint64_t(t) * H + c);
-    for (uint32_t k = 1; k < shared_splits; ++k) {
-      const float4 v = *reinterpret_cast<const float4*>(shared + k * stride + uint64_t(t) * H + c);
-      s.x = __fadd_rn(s.x, v.x);
-      s.y = __fadd_rn(s.y, v.y);
-      s.z = __fadd_rn(s.z, v.z);
-      s.w = __fadd_rn(s.w, v.w);
-    }
-    if (shared_out) *reinterpret_cast<float4*>(shared_out + uint64_t(t) * H + c) = s;
-    acc.x = __fadd_rn(acc.x, s.x);
-    acc.y = __fadd_rn(acc.y, s.y);
-    acc.z = __fadd_rn(acc.z, s.z);
-    acc.w = __fadd_rn(acc.w, s.w);
+    const float* sp = shared + uint64_t(t) * H + c;
+    float4 sum = *reinterpret_cast<const float4*>(sp);
+#pragma unroll 4
+    for (uint32_t k = 1; k < shared_splits; ++k) add4(sum, *reinterpret_cast<const float4*>(sp + k * stride));
+    if (shared_out) *reinterpret_cast<float4*>(shared_out + uint64_t(t) * H + c) = sum;
+    add4(acc, sum);
   }
   *reinterpret_cast<float4*>(out + uint64_t(t) * H + c) = acc;
 }
@@ -964,9 +1152,16 @@ cudaError_t launch_router_select(const float* partial, const float* bias, uint32
                                  cudaStream_t stream) {
   // two tokens (warps) per CTA: the per-token selection is a latency chain, so
   // tokens are spread over as many SMs as possible
-  router_select_kernel<<<(T + 1) / 2, 64, 0, stream>>>(partial, bias, T, E, groups, topk_groups,
-                                                        top_k, route_scale, experts, weights,
-                                                        bitmap, bitmap_stride, status);
+  const uint32_t gs = groups ? E / groups : 0;
+  const bool runs = E % 8 == 0 && E <= 256 && gs % 8 == 0 && ((gs / 8) & (gs / 8 - 1)) == 0;
+  if (runs)
+    router_select_runs_kernel<<<(T + 1) / 2, 64, 0, stream>>>(
+        partial, bias, T, E, groups, topk_groups, top_k, route_scale, experts, weights, bitmap,
+        bitmap_stride, status);
+  else
+    router_select_kernel<<<(T + 1) / 2, 64, 0, stream>>>(partial, bias, T, E, groups, topk_groups,
+                                                          top_k, route_scale, experts, weights,
+                                                          bitmap, bitmap_stride, status);
   return cudaPeekAtLastError();
 }
 
@@ -1003,16 +1198,21 @@ cudaError_t launch_compat_prepare(const CompatPrepareArgs& a, cudaStream_t strea
 }
 
 cudaError_t launch_quant_scatter(const QuantScatterArgs& a, cudaStream_t stream) {
-  const uint32_t threads = (a.H / 64 + 31) / 32 * 32;
+  const uint32_t threads = (a.H / 16 + 31) / 32 * 32;  // H <= 16384
+  if (threads > 1024 || a.top_k > 32) return cudaErrorInvalidValue;
   quant_scatter_kernel<<<a.T, threads, 0, stream>>>(a);
   return cudaPeekAtLastError();
 }
 
 cudaError_t launch_fc2_quant(const Fc2QuantArgs& a, cudaStream_t stream) {
-  const uint32_t rows_per_block = 256 / (a.I / 64);
+  // one thread per 16-element block; 128-thread blocks (one row when I = 2048)
+  const uint32_t R = a.I / 16;
+  if (R < 16 || R > 128 || (R & (R - 1))) return cudaErrorInvalidValue;
+  const uint32_t threads = 128;
+  const uint32_t rows_per_block = threads / R;
   const uint32_t blocks = (a.count + rows_per_block - 1) / rows_per_block;
   if (blocks == 0) return cudaSuccess;
-  fc2_quant_kernel<<<blocks, 256, 0, stream>>>(a);
+  fc2_quant_kernel<<<blocks, threads, 0, stream>>>(a);
   return cudaPeekAtLastError();
 }
 
@@ -1041,6 +1241,8 @@ cudaError_t launch_slot_reduce(const SlotArgs& a, cudaStream_t stream) {
 cudaError_t launch_combine(const float* plane, const uint16_t* experts, const float* shared,
                            uint32_t shared_splits, float* shared_out, float* out, uint32_t T,
                            uint32_t H, uint32_t top_k, cudaStream_t stream) {
+  if (top_k > 8 || (shared && (shared_splits == 0 || shared_splits > 16)))
+    return cudaErrorInvalidValue;
   dim3 grid((H / 4 + 255) / 256, T);
   combine_kernel<<<grid, 256, 0, stream>>>(plane, experts, shared, shared_splits, shared_out, out,
                                            T, H, top_k);
