@@ -488,20 +488,29 @@ __global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
             src_d = r_dst[r];
           }
         }
+        // columns (token rows) in groups of 8; groups past the tile's last row are
+        // skipped (warp-uniform), which at decode -- 1 to 4 rows per expert --
+        // removes most of the per-item epilogue work
+        const uint32_t live = t.rows - ch * 32;  // > 0 for every processed chunk
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float s = __fmul_rn(scale_a, __shfl_sync(0xffffffffu, src_s, j));
-          const float gj = __fmul_rn(__uint_as_float(g[j]), s);
-          const float uj = DUAL ? __fmul_rn(__uint_as_float(u[j]), s) : 0.0f;
-          if (EPI == kEpiSwiGLU) {
-            g[j] = __float_as_uint(__fmul_rn(silu(gj), DUAL ? uj : 1.0f));
-          } else if (EPI == kEpiRoutedPlane || EPI == kEpiRoutedAtomic) {
-            const float rw = __shfl_sync(0xffffffffu, src_w, j);
-            g[j] = __float_as_uint(__fmul_rn(rw, gj));
-            if (DUAL) u[j] = __float_as_uint(__fmul_rn(rw, uj));
-          } else {
-            g[j] = __float_as_uint(gj);
-            if (DUAL) u[j] = __float_as_uint(uj);
+        for (int q = 0; q < 4; ++q) {
+          if (!ET::kOn && uint32_t(8 * q) >= live) break;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int j = 8 * q + jj;
+            const float s = __fmul_rn(scale_a, __shfl_sync(0xffffffffu, src_s, j));
+            const float gj = __fmul_rn(__uint_as_float(g[j]), s);
+            const float uj = DUAL ? __fmul_rn(__uint_as_float(u[j]), s) : 0.0f;
+            if (EPI == kEpiSwiGLU) {
+              g[j] = __float_as_uint(__fmul_rn(silu(gj), DUAL ? uj : 1.0f));
+            } else if (EPI == kEpiRoutedPlane || EPI == kEpiRoutedAtomic) {
+              const float rw = __shfl_sync(0xffffffffu, src_w, j);
+              g[j] = __float_as_uint(__fmul_rn(rw, gj));
+              if (DUAL) u[j] = __float_as_uint(__fmul_rn(rw, uj));
+            } else {
+              g[j] = __float_as_uint(gj);
+              if (DUAL) u[j] = __float_as_uint(uj);
+            }
           }
         }
         if constexpr (ET::kOn) {
@@ -552,8 +561,8 @@ __global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            if (uint32_t(j) >= live) break;  // warp-uniform
             const uint32_t rd = __shfl_sync(0xffffffffu, src_d, j);
-            if (ch * 32 + j >= t.rows) continue;
             const float v0 = __uint_as_float(g[j]);
             const float v1 = __uint_as_float(u[j]);
             if (EPI == kEpiSwiGLU) {
