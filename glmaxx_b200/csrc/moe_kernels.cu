@@ -279,11 +279,9 @@ __global__ void __launch_bounds__(256) router_select_runs_kernel(
     p[c][0] = mine ? src[0] : make_float4(0.f, 0.f, 0.f, 0.f);
     p[c][1] = mine ? src[1] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
-  if (mine) {
-    b0 = reinterpret_cast<const float4*>(bias + e0)[0];
-    b1 = reinterpret_cast<const float4*>(bias + e0)[1];
-  }
+  float bj[8];  // scalar loads: the bias is only required to be 4-byte aligned
+#pragma unroll
+  for (int j = 0; j < 8; ++j) bj[j] = mine ? bias[e0 + j] : 0.f;
   float L[8] = {p[0][0].x, p[0][0].y, p[0][0].z, p[0][0].w,
                 p[0][1].x, p[0][1].y, p[0][1].z, p[0][1].w};
 #pragma unroll
@@ -293,7 +291,6 @@ __global__ void __launch_bounds__(256) router_select_runs_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) L[j] = __fadd_rn(L[j], q[j]);
   }
-  const float bj[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
   float sc[8];
   uint32_t key[8];
   bool bad = false;

@@ -65,7 +65,11 @@ def _router_case(T, H, E, groups, topk_groups, seed):
     return x, w, bias
 
 
-@pytest.mark.parametrize("T,E,groups,topk_groups", [(64, 256, 8, 4), (8, 16, 1, 1), (333, 256, 8, 4)])
+# (40, 40, 10, 3): groups of 4 experts, which are not whole lane runs, take the
+# general selection kernel; the others take the lane-run kernel (groups of 8, 16,
+# 32 experts).
+@pytest.mark.parametrize("T,E,groups,topk_groups", [(64, 256, 8, 4), (8, 16, 1, 1), (333, 256, 8, 4),
+                                                    (40, 40, 10, 3), (24, 96, 3, 2)])
 def test_gpu_router_compact_bit_exact(T, E, groups, topk_groups):
     H, K = 6144, 8
     dev = cuda()
