@@ -211,13 +211,20 @@ struct SideStream {
 };
 thread_local SideStream g_side[64];
 
-cudaError_t side_stream(SideStream** out) {
+// *out stays null (the shared expert then runs in order on the launch stream)
+// when the side stream does not exist yet and the launch stream is capturing:
+// creating streams and events is left to an uncaptured launch.
+cudaError_t side_stream(cudaStream_t launch, SideStream** out) {
+  *out = nullptr;
   int dev = 0;
   cudaError_t st = cudaGetDevice(&dev);
   if (st != cudaSuccess) return st;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   SideStream& s = g_side[dev];
   if (s.stream == nullptr) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if ((st = cudaStreamIsCapturing(launch, &cap)) != cudaSuccess) return st;
+    if (cap != cudaStreamCaptureStatusNone) return cudaSuccess;
     if ((st = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking)) != cudaSuccess) return st;
     if ((st = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming)) != cudaSuccess) return st;
     if ((st = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming)) != cudaSuccess) return st;
@@ -308,10 +315,12 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   SideStream* side = nullptr;
   cudaStream_t sstream = stream;  // the shared expert's stream
   if (p.shared) {
-    CHECK(side_stream(&side));
-    sstream = side->stream;
-    CHECK(cudaEventRecord(side->fork, stream));
-    CHECK(cudaStreamWaitEvent(sstream, side->fork, 0));
+    CHECK(side_stream(stream, &side));
+    if (side) {
+      sstream = side->stream;
+      CHECK(cudaEventRecord(side->fork, stream));
+      CHECK(cudaStreamWaitEvent(sstream, side->fork, 0));
+    }
   }
   // shared expert (bf16) on the side stream, and the output initialisation it
   // provides outside plane mode
@@ -367,7 +376,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
       g2.args.out = p.plane_mode ? at<void>(ws, p.sbuf) : static_cast<void*>(out);
       CHECK(launch_gemm(kShared2Bf16N128, g2, info.sms, sstream));
     }
-    CHECK(cudaEventRecord(side->join, sstream));
+    if (side) CHECK(cudaEventRecord(side->join, sstream));
   }
 
   // 1. router (or caller routes) -> dense routes + token-in-expert bitmap
@@ -500,7 +509,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   if (!p.shared && !p.plane_mode) {
     CHECK(cudaMemsetAsync(out, 0, uint64_t(r.T) * p.H * 4, stream));
   }
-  if (p.shared && !p.plane_mode) CHECK(cudaStreamWaitEvent(stream, side->join, 0));
+  if (side && !p.plane_mode) CHECK(cudaStreamWaitEvent(stream, side->join, 0));
   // 7. grouped FC2 with the routing-weighted combine
   CHECK(mark(kStageFc2, stream));
   if (p.nvfp4) {
@@ -540,7 +549,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
   }
   // 8. deterministic combine (plane mode): ascending-expert sum + shared
   CHECK(mark(kStageCombine, stream));
-  if (p.shared && p.plane_mode) CHECK(cudaStreamWaitEvent(stream, side->join, 0));
+  if (side && p.plane_mode) CHECK(cudaStreamWaitEvent(stream, side->join, 0));
   if (p.plane_mode) {
     const float* shared_in = !p.shared ? nullptr
                              : (p.decode ? at<float>(ws, p.sparts2) : at<float>(ws, p.sbuf));

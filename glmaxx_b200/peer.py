@@ -148,7 +148,10 @@ class PeerGroup:
     # ------------------------------------------------------------ lifetime
     def reset_signals(self) -> None:
         """Zero this rank's signal buffer, then wait for every rank (after a
-        peer timeout, or before the first finish)."""
+        peer timeout, or before the first finish).  Every rank's finish kernels
+        have ended before any buffer is zeroed."""
+        if self.device is not None or torch.cuda.is_initialized():
+            torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         self.backend.zero(self.base, self.signal_bytes)
         dist.barrier(group=self.group)

@@ -312,3 +312,41 @@ def test_gpu_layer_in_cuda_graph_matches_eager(path, T):
             assert torch.equal(got, ref)
         else:
             assert_layer_close(got.cpu().numpy(), ref.cpu().numpy(), "graph vs eager")
+
+
+def test_gpu_layer_first_launch_under_capture():
+    """The side stream of the shared expert is created by an uncaptured launch;
+    a thread whose first layer launch is captured runs the shared expert in order
+    on the launch stream instead, with the same results."""
+    import threading
+
+    cfg = MoEConfig(tp=4, rank=2)
+    dev = cuda()
+    w = synth.make_rank_weights(cfg, seed=21, device=dev)
+    T = 64
+    layer = RoutedMoE(cfg, w, T)
+    x = synth.make_input(T, cfg.hidden, seed=21, device=dev)
+    out = torch.empty((T, cfg.hidden), dtype=torch.float32, device=dev)
+    # the workspace is allocated outside the capture by a first eager call on
+    # this thread; the captured launch happens on a fresh thread
+    ref = layer(x).clone()
+    torch.cuda.synchronize()
+    errors = []
+
+    def capture_and_replay():
+        try:
+            torch.cuda.set_device(dev)
+            s = torch.cuda.Stream(device=dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                layer(x, out)
+            g.replay()
+            torch.cuda.synchronize()
+        except Exception as e:  # noqa: BLE001
+            errors.append(repr(e))
+
+    th = threading.Thread(target=capture_and_replay)
+    th.start()
+    th.join()
+    assert errors == []
+    assert torch.equal(out, ref)
