@@ -533,18 +533,50 @@ def run_ours(args):
     stage_avg = {s: statistics.mean(v) for s, v in stage_ms.items()}
 
     # ------------------------------------------------------------------ e2e
+    # Every step uploads its input from pinned host memory and downloads its
+    # fp32 output, inside the timed region.  As in a serving loop, the transfers
+    # of neighbouring steps overlap the compute: step i+1's input lands in a
+    # staging buffer on an upload stream while step i runs, and a device-to-device
+    # copy feeds the graph's input buffer; step i's output is snapshotted on the
+    # device and downloaded on a download stream while step i+1 runs (the two
+    # directions use separate copy engines).  The first upload and the last
+    # download are not overlapped.
     x_host = x.cpu().pin_memory()
     out_host = torch.empty((T, HIDDEN), dtype=torch.float32).pin_memory()
     x_dev = x  # the graph reads this buffer
+    x_stage = torch.empty_like(x)
+    out_stage = torch.empty((T, HIDDEN), dtype=torch.float32, device=dev)
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    x_ready, x_free = torch.cuda.Event(), torch.cuda.Event()
+    o_ready, o_free = torch.cuda.Event(), torch.cuda.Event()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
-            x_dev.copy_(x_host, non_blocking=True)
+        up.wait_event(e0)
+        with torch.cuda.stream(up):
+            x_stage.copy_(x_host, non_blocking=True)
+            x_ready.record(up)
+        for i in range(args.steps):
+            stream.wait_event(x_ready)
+            x_dev.copy_(x_stage, non_blocking=True)
+            x_free.record(stream)
+            with torch.cuda.stream(up):
+                up.wait_event(x_free)
+                if i + 1 < args.steps:
+                    x_stage.copy_(x_host, non_blocking=True)
+                    x_ready.record(up)
             step()
-            out_host.copy_(out, non_blocking=True)
+            if i > 0:
+                stream.wait_event(o_free)
+            out_stage.copy_(out, non_blocking=True)
+            o_ready.record(stream)
+            with torch.cuda.stream(down):
+                down.wait_event(o_ready)
+                out_host.copy_(out_stage, non_blocking=True)
+                o_free.record(down)
+        stream.wait_event(o_free)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
@@ -662,7 +694,9 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": T * HIDDEN * 2, "d2h_bytes_per_step": T * HIDDEN * 4,
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms,
+                    "transfers": "pinned host buffers; each step's upload and download on "
+                                 "copy streams overlap the neighbouring steps' compute"},
             "gpu_launches": None if kernels_per_step is None else kernels_per_step * args.steps,
             "clocks": clock_info,
         }
