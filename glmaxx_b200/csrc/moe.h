@@ -154,6 +154,9 @@ cudaError_t launch_slot_reduce(const SlotArgs& a, cudaStream_t stream);
 cudaError_t launch_combine(const float* plane, const uint16_t* experts, const float* shared,
                            uint32_t shared_splits, float* shared_out, float* out, uint32_t T,
                            uint32_t H, uint32_t top_k, cudaStream_t stream);
+// Bulk L2 prefetch of [a, a + a_bytes) and [b, b + b_bytes) (16-byte aligned).
+cudaError_t launch_l2_prefetch(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes,
+                               cudaStream_t stream);
 cudaError_t launch_swiglu_finish(const float* parts, uint32_t splits, uint32_t T, uint32_t I,
                                  uint16_t* h, cudaStream_t stream);
 cudaError_t launch_pack(const void* src, int src_bf16, uint32_t batch, uint32_t N, uint32_t K,

@@ -1033,6 +1033,24 @@ __global__ void __launch_bounds__(256) combine_kernel(
   *reinterpret_cast<float4*>(out + uint64_t(t) * H + c) = acc;
 }
 
+// L2 prefetch of two byte ranges: each thread issues one bulk prefetch of up to
+// 32 KB (addresses and sizes 16-byte aligned).  No data reaches the SM.
+constexpr uint64_t kPrefetchChunk = 32768;
+__global__ void l2_prefetch_kernel(const uint8_t* a, uint64_t a_bytes, const uint8_t* b,
+                                   uint64_t b_bytes) {
+  const uint64_t na = (a_bytes + kPrefetchChunk - 1) / kPrefetchChunk;
+  const uint64_t nb = (b_bytes + kPrefetchChunk - 1) / kPrefetchChunk;
+  for (uint64_t i = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; i < na + nb;
+       i += uint64_t(gridDim.x) * blockDim.x) {
+    const bool in_a = i < na;
+    const uint64_t off = (in_a ? i : i - na) * kPrefetchChunk;
+    const uint64_t total = in_a ? a_bytes : b_bytes;
+    const uint32_t size = static_cast<uint32_t>(min(kPrefetchChunk, total - off));
+    const uint8_t* ptr = (in_a ? a : b) + off;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr), "r"(size) : "memory");
+  }
+}
+
 // Shared-expert FC1 finish after split-K: gate/up = sums of the slice partials
 // (parts[s][t][0..I) gate, [I..2I) up, slice order), h = bf16(silu(gate) * up).
 __global__ void swiglu_finish_kernel(const float* __restrict__ parts, uint32_t splits, uint32_t T,
@@ -1243,6 +1261,21 @@ cudaError_t launch_combine(const float* plane, const uint16_t* experts, const fl
   dim3 grid((H / 4 + 255) / 256, T);
   combine_kernel<<<grid, 256, 0, stream>>>(plane, experts, shared, shared_splits, shared_out, out,
                                            T, H, top_k);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t launch_l2_prefetch(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes,
+                               cudaStream_t stream) {
+  if (reinterpret_cast<uintptr_t>(a) % 16 || reinterpret_cast<uintptr_t>(b) % 16 || a_bytes % 16 ||
+      b_bytes % 16)
+    return cudaErrorInvalidValue;
+  const uint64_t n = (a_bytes + kPrefetchChunk - 1) / kPrefetchChunk +
+                     (b_bytes + kPrefetchChunk - 1) / kPrefetchChunk;
+  if (n == 0) return cudaSuccess;
+  const uint64_t want = (n + 127) / 128;
+  const uint32_t blocks = static_cast<uint32_t>(want < 64 ? want : 64);
+  l2_prefetch_kernel<<<blocks, 128, 0, stream>>>(static_cast<const uint8_t*>(a), a_bytes,
+                                                static_cast<const uint8_t*>(b), b_bytes);
   return cudaPeekAtLastError();
 }
 
