@@ -37,7 +37,8 @@ constexpr int kXBBytes = kXNT * 128;         // 128 token rows x 128 B of K
 constexpr int kXTrellisRowBytes = 8 * 96;    // 8 consecutive n-tiles of one k-tile row
 constexpr int kXTBytes = 4 * kXTrellisRowBytes;
 constexpr int kXStageBytes = kXABytes + kXBBytes + kXTBytes;  // 35,840 (a multiple of 1024)
-constexpr int kXDecoders = 8;               // decoder warps (one n-tile of the A tile each)
+constexpr int kXDecoders = 16;              // decoder warps: n-tile dw % 8, k-tile half dw / 8
+constexpr int kXKtPerDecoder = 4 * 8 / kXDecoders;  // k-tiles of the stage per decoder
 constexpr int kXThreads = (6 + kXDecoders) * 32;
 constexpr int kXSmem = kXStageBytes * kXStages + 1024 + 512;
 static_assert(kXStageBytes % 1024 == 0, "stage alignment");
@@ -192,12 +193,14 @@ __global__ void __launch_bounds__(kXThreads, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------------------------------------ decoders
-    // Decoder dw writes n-tile dw of the 128-row A tile for the 4 k-tiles of the
-    // stage.  Lane l owns weights 8l..8l+7 of a tile: rows (k) lrb + (w&1) +
+    // Decoder dw writes n-tile dw % 8 of the 128-row A tile for k-tiles
+    // kXKtPerDecoder * (dw / 8) .. of the stage's four (two decoders per n-tile,
+    // so that twice the warps hide the decode's latency chains).  Lane l owns
+    // weights 8l..8l+7 of a tile: rows (k) lrb + (w&1) +
     // 8((w>>1)&1), column (n) lcb + 8((w>>2)&1); weights w and w+1 are k, k+1 of
-    // one n, one 4-byte store into the swizzled row n.  The 12 trellis words of
-    // the stage are read before any decode, so their latencies overlap.
-    const uint32_t dw = warp - 6;
+    // one n, one 4-byte store into the swizzled row n.  The decoder's trellis
+    // words of the stage are read before any decode, so their latencies overlap.
+    const uint32_t dw = (warp - 6) % 8, kt0 = (warp - 6) / 8 * kXKtPerDecoder;
     const Exl3LaneWindow lw = exl3_lane_window(lane);
     const uint32_t lcb = 2 * ((lane >> 3) & 3) + ((lane >> 2) & 1);
     const uint32_t lrb = 2 * (lane & 3);
@@ -215,16 +218,17 @@ __global__ void __launch_bounds__(kXThreads, 1)
         }
         const uint32_t* ts = reinterpret_cast<const uint32_t*>(stage_t(stage));
         uint8_t* a = stage_a(stage);
-        uint32_t wd[4][3];
+        uint32_t wd[kXKtPerDecoder][3];
 #pragma unroll
-        for (int ktl = 0; ktl < 4; ++ktl)
+        for (int kk = 0; kk < kXKtPerDecoder; ++kk)
 #pragma unroll
           for (int j = 0; j < 3; ++j)
-            wd[ktl][j] = ts[(ktl * kXTrellisRowBytes + dw * 96) / 4 + widx[j]];
+            wd[kk][j] = ts[((kt0 + kk) * kXTrellisRowBytes + dw * 96) / 4 + widx[j]];
 #pragma unroll
-        for (int ktl = 0; ktl < 4; ++ktl) {
+        for (int kk = 0; kk < kXKtPerDecoder; ++kk) {
+          const uint32_t ktl = kt0 + kk;
           uint16_t w16[8];
-          exl3_decode_span(wd[ktl], lw.off, w16);
+          exl3_decode_span(wd[kk], lw.off, w16);
 #pragma unroll
           for (int w = 0; w < 8; w += 2) {
             const uint32_t n = dw * 16 + lcb + 8 * ((w >> 2) & 1);
