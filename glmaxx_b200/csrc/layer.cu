@@ -540,11 +540,15 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     GemmArgs& a = g.args;
     a.tiles = tiles;
     a.tile_count = tile_count;
-    // two adjacent 128-row M tiles per item share one B tile (twice the weight
-    // bytes per pipeline stage, half the B-tile and scale-copy work per FLOP)
-    a.m_tiles = p.H / 256;
-    a.m_stride = 256;
-    a.up_row_offset = 128;
+    // Decode and plane mode: two adjacent 128-row M tiles per item share one B
+    // tile (twice the weight bytes per pipeline stage, half the B-tile and
+    // scale-copy work per FLOP).  Prefill with the atomic combine: one M tile per
+    // item, whose two accumulator buffers let the MMA run through the atomic
+    // epilogue (FC2 1.34 -> 1.21 ms at T=8192).
+    const bool single = !p.decode && !p.plane_mode;
+    a.m_tiles = single ? p.H / 128 : p.H / 256;
+    a.m_stride = single ? 128 : 256;
+    a.up_row_offset = single ? 0 : 128;
     a.k_chunks = p.I / 256;
     a.kblocks = p.I / 64;
     a.ldo = p.H;
@@ -560,7 +564,7 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     a.row_weight = q.row_weight;
     a.status = status;
     CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair
-                             : (p.plane_mode ? kFc2PrefillFp4PairPlane : kFc2PrefillFp4Pair),
+                             : (p.plane_mode ? kFc2PrefillFp4PairPlane : kFc2PrefillFp4),
                       g, info.sms, stream));
   }
   // 8. deterministic combine (plane mode): ascending-expert sum + shared
