@@ -126,8 +126,6 @@ cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStr
       return run<true, false, 128, 4, kEpiRoutedAtomic>(g, num_sms, stream);
     case kFc2PrefillFp4Store:
       return run<true, false, 128, 4, kEpiStoreF32>(g, num_sms, stream);
-    case kFc2PrefillFp4Pair:
-      return run<true, true, 128, 3, kEpiRoutedAtomic>(g, num_sms, stream);
     case kFc2PrefillFp4PairPlane:
       return run<true, true, 128, 3, kEpiRoutedPlane>(g, num_sms, stream);
     case kShared1Bf16N64:
