@@ -195,6 +195,8 @@ SIGNATURES = {
     "glmaxx_exl3_gemv_launch": (ctypes.c_int32, [u64, u64, u32, u32, u32, u32, u64, _P]),
     "glmaxx_graph_exec_launch": (ctypes.c_int32, [u64, u64]),
     "glmaxx_graph_exec_destroy": (ctypes.c_int32, [u64]),
+    "glmaxx_stream_begin_capture": (ctypes.c_int32, [u64]),
+    "glmaxx_stream_end_capture": (ctypes.c_int32, [u64, _U64P]),
     "glmaxx_event_create": (ctypes.c_int32, [_U64P]),
     "glmaxx_event_record": (ctypes.c_int32, [u64, u64]),
     "glmaxx_event_synchronize": (ctypes.c_int32, [u64]),

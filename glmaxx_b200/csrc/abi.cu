@@ -689,6 +689,22 @@ int32_t glmaxx_graph_exec_destroy(uint64_t graph_exec) {
   if (graph_exec == 0) return GLMAXX_ERR_NULL;
   return int32_t(cudaGraphExecDestroy(reinterpret_cast<cudaGraphExec_t>(graph_exec)));
 }
+int32_t glmaxx_stream_begin_capture(uint64_t stream) {
+  if (stream == 0) return GLMAXX_ERR_NULL;
+  return int32_t(cudaStreamBeginCapture(reinterpret_cast<cudaStream_t>(stream),
+                                        cudaStreamCaptureModeThreadLocal));
+}
+int32_t glmaxx_stream_end_capture(uint64_t stream, uint64_t* graph_exec) {
+  if (stream == 0 || graph_exec == nullptr) return GLMAXX_ERR_NULL;
+  cudaGraph_t graph = nullptr;
+  cudaError_t st = cudaStreamEndCapture(reinterpret_cast<cudaStream_t>(stream), &graph);
+  if (st != cudaSuccess) return int32_t(st);
+  cudaGraphExec_t exec = nullptr;
+  st = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (st == cudaSuccess) *graph_exec = reinterpret_cast<uint64_t>(exec);
+  return int32_t(st);
+}
 int32_t glmaxx_event_create(uint64_t* event) {
   if (event == nullptr) return GLMAXX_ERR_NULL;
   cudaEvent_t e = nullptr;

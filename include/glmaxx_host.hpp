@@ -1,0 +1,632 @@
+// C++ host runtime of the routed-MoE path over the C ABI of libglmaxx_sm100.so
+// (glmaxx_kernel.h).  It is the counterpart, in C++17, of the reference's Rust
+// binding layer crates/glm-cuda/src/ffi.rs and abi.rs: an owner-thread rank
+// context (NativeRankContext::bind, ffi.rs:185-298), move-only device buffer,
+// stream, event and graph handles (ffi.rs:649-790), the KernelError kinds
+// (abi.rs:686-698), the ABI validation entry (validate_native_moe_abi,
+// ffi.rs:3227-3245), and the operator this library adds for the whole rank-local
+// step: RoutedMoeStep, its per-row-bucket graphs (the engine's GraphKey
+// verifier_row_bucket, crates/glm-engine/src/graph.rs:13-80, with the buckets of
+// crates/glm-cli/src/profile.rs:10-11), and PeerFinish, the fused tensor-parallel
+// reduce over CUDA IPC mappings.
+//
+// Header-only: it calls only the extern "C" functions of glmaxx_kernel.h, so a
+// C++ engine links libglmaxx_sm100.so and includes this file.  Every failure
+// raises KernelError; no call falls back to another implementation.
+#pragma once
+
+#include <algorithm>
+#include <array>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <utility>
+#include <vector>
+
+#include "glmaxx_kernel.h"
+
+namespace glmaxx {
+namespace host {
+
+// ------------------------------------------------------------------ errors
+enum class ErrorKind {
+  Abi,
+  Path,
+  Shape,
+  Null,
+  Alignment,
+  Overflow,
+  Workspace,
+  Driver,
+  Async,
+  DeviceValidation,
+  Topology,
+};
+
+inline const char* error_kind_name(ErrorKind k) {
+  switch (k) {
+    case ErrorKind::Abi: return "Abi";
+    case ErrorKind::Path: return "Path";
+    case ErrorKind::Shape: return "Shape";
+    case ErrorKind::Null: return "Null";
+    case ErrorKind::Alignment: return "Alignment";
+    case ErrorKind::Overflow: return "Overflow";
+    case ErrorKind::Workspace: return "Workspace";
+    case ErrorKind::Driver: return "Driver";
+    case ErrorKind::Async: return "Async";
+    case ErrorKind::DeviceValidation: return "DeviceValidation";
+    case ErrorKind::Topology: return "Topology";
+  }
+  return "?";
+}
+
+class KernelError : public std::runtime_error {
+ public:
+  KernelError(ErrorKind kind, int64_t code = 0, uint64_t required = 0, uint64_t provided = 0)
+      : std::runtime_error(std::string(error_kind_name(kind)) + "(" + std::to_string(code) + ")"),
+        kind_(kind), code_(code), required_(required), provided_(provided) {}
+  ErrorKind kind() const { return kind_; }
+  int64_t code() const { return code_; }           // status, async error or device word
+  uint64_t required() const { return required_; }  // Workspace
+  uint64_t provided() const { return provided_; }
+
+ private:
+  ErrorKind kind_;
+  int64_t code_;
+  uint64_t required_, provided_;
+};
+
+// A non-zero status of an extern "C" call is a Driver error carrying it
+// (ffi.rs:3170-3176).
+inline void check(int32_t status) {
+  if (status != 0) throw KernelError(ErrorKind::Driver, status);
+}
+
+inline uint64_t checked_add(uint64_t a, uint64_t b) {
+  if (a > UINT64_MAX - b) throw KernelError(ErrorKind::Overflow);
+  return a + b;
+}
+
+// ------------------------------------------------------------------ handles
+class NativeStream {
+ public:
+  static NativeStream create() {
+    uint64_t s = 0;
+    check(glmaxx_stream_create(&s));
+    return NativeStream(s);
+  }
+  NativeStream() = default;
+  NativeStream(NativeStream&& o) noexcept : s_(std::exchange(o.s_, 0)) {}
+  NativeStream& operator=(NativeStream&& o) noexcept {
+    std::swap(s_, o.s_);
+    return *this;
+  }
+  NativeStream(const NativeStream&) = delete;
+  NativeStream& operator=(const NativeStream&) = delete;
+  ~NativeStream() {
+    if (s_) glmaxx_stream_destroy(s_);
+  }
+  uint64_t get() const { return s_; }
+  void synchronize() const { check(glmaxx_stream_synchronize(s_)); }
+
+ private:
+  explicit NativeStream(uint64_t s) : s_(s) {}
+  uint64_t s_ = 0;
+};
+
+class NativeEvent {
+ public:
+  static NativeEvent create() {
+    uint64_t e = 0;
+    check(glmaxx_event_create(&e));
+    if (e == 0) throw KernelError(ErrorKind::Driver, -1);
+    return NativeEvent(e);
+  }
+  NativeEvent(NativeEvent&& o) noexcept : e_(std::exchange(o.e_, 0)) {}
+  NativeEvent& operator=(NativeEvent&& o) noexcept {
+    std::swap(e_, o.e_);
+    return *this;
+  }
+  NativeEvent(const NativeEvent&) = delete;
+  NativeEvent& operator=(const NativeEvent&) = delete;
+  ~NativeEvent() {
+    if (e_) glmaxx_event_destroy(e_);
+  }
+  void record(uint64_t stream) const { check(glmaxx_event_record(e_, stream)); }
+  void synchronize() const { check(glmaxx_event_synchronize(e_)); }
+  float elapsed_ms(const NativeEvent& end) const {
+    float ms = 0.0f;
+    check(glmaxx_event_elapsed_ms(e_, end.e_, &ms));
+    return ms;
+  }
+
+ private:
+  explicit NativeEvent(uint64_t e) : e_(e) {}
+  uint64_t e_ = 0;
+};
+
+// An executable graph of the work captured on a stream between begin() and
+// end() (glmaxx_stream_begin_capture / glmaxx_stream_end_capture).
+class NativeGraph {
+ public:
+  static void begin(uint64_t stream) { check(glmaxx_stream_begin_capture(stream)); }
+  static NativeGraph end(uint64_t stream) {
+    uint64_t exec = 0;
+    check(glmaxx_stream_end_capture(stream, &exec));
+    return NativeGraph(exec);
+  }
+  NativeGraph() = default;
+  NativeGraph(NativeGraph&& o) noexcept : g_(std::exchange(o.g_, 0)) {}
+  NativeGraph& operator=(NativeGraph&& o) noexcept {
+    std::swap(g_, o.g_);
+    return *this;
+  }
+  NativeGraph(const NativeGraph&) = delete;
+  NativeGraph& operator=(const NativeGraph&) = delete;
+  ~NativeGraph() {
+    if (g_) glmaxx_graph_exec_destroy(g_);
+  }
+  void launch(uint64_t stream) const { check(glmaxx_graph_exec_launch(g_, stream)); }
+  bool valid() const { return g_ != 0; }
+
+ private:
+  explicit NativeGraph(uint64_t g) : g_(g) {}
+  uint64_t g_ = 0;
+};
+
+// Device allocation with range-checked copies (ffi.rs:649-724).
+class NativeBuffer {
+ public:
+  static NativeBuffer allocate(uint64_t bytes) {
+    if (bytes == 0) throw KernelError(ErrorKind::Shape);
+    uint64_t p = 0;
+    check(glmaxx_device_alloc(bytes, &p));
+    return NativeBuffer(p, bytes);
+  }
+  static NativeBuffer upload(const void* host, uint64_t bytes, uint64_t stream) {
+    NativeBuffer b = allocate(bytes);
+    b.upload_at(host, bytes, 0, stream);
+    return b;
+  }
+  NativeBuffer() = default;
+  NativeBuffer(NativeBuffer&& o) noexcept
+      : p_(std::exchange(o.p_, 0)), bytes_(std::exchange(o.bytes_, 0)) {}
+  NativeBuffer& operator=(NativeBuffer&& o) noexcept {
+    std::swap(p_, o.p_);
+    std::swap(bytes_, o.bytes_);
+    return *this;
+  }
+  NativeBuffer(const NativeBuffer&) = delete;
+  NativeBuffer& operator=(const NativeBuffer&) = delete;
+  ~NativeBuffer() {
+    if (p_) glmaxx_device_free(p_);
+  }
+  uint64_t ptr() const { return p_; }
+  uint64_t bytes() const { return bytes_; }
+  void upload_at(const void* host, uint64_t bytes, uint64_t offset, uint64_t stream) const {
+    if (checked_add(offset, bytes) > bytes_) throw KernelError(ErrorKind::Shape);
+    check(glmaxx_memcpy_h2d(p_ + offset, host, bytes, stream));
+  }
+  void download_at(void* host, uint64_t bytes, uint64_t offset, uint64_t stream) const {
+    if (checked_add(offset, bytes) > bytes_) throw KernelError(ErrorKind::Shape);
+    check(glmaxx_memcpy_d2h(host, p_ + offset, bytes, stream));
+  }
+  void copy_within(uint64_t src_offset, uint64_t dst_offset, uint64_t bytes, uint64_t stream) const {
+    if (checked_add(src_offset, bytes) > bytes_ || checked_add(dst_offset, bytes) > bytes_)
+      throw KernelError(ErrorKind::Shape);
+    check(glmaxx_memcpy_d2d(p_ + dst_offset, p_ + src_offset, bytes, stream));
+  }
+  void zero(uint64_t stream) const { check(glmaxx_memset_zero(p_, bytes_, stream)); }
+
+ private:
+  NativeBuffer(uint64_t p, uint64_t b) : p_(p), bytes_(b) {}
+  uint64_t p_ = 0, bytes_ = 0;
+};
+
+// ------------------------------------------------------------------ rank context
+struct NativeDeviceIdentity {
+  uint32_t visible_devices = 0;
+  uint32_t device_index = 0;
+  uint32_t compute_capability = 0;
+  uint32_t multiprocessor_count = 0;
+  uint64_t total_memory_bytes = 0;
+  std::array<uint8_t, 16> device_uuid{};
+};
+
+// One rank's device and non-blocking stream, bound on and owned by the calling
+// thread; every method checks that it runs on that thread (ffi.rs:185-298).
+// ranks: the tensor-parallel degree (1, 2, 4 or 8; the reference fixes 4); the
+// rank's device is device `rank`, of compute capability 10.x.
+class NativeRankContext {
+ public:
+  static NativeRankContext bind(uint32_t rank, uint32_t ranks) {
+    if (!(ranks == 1 || ranks == 2 || ranks == 4 || ranks == 8) || rank >= ranks)
+      throw KernelError(ErrorKind::Topology);
+    int32_t visible = 0;
+    check(glmaxx_device_count(&visible));
+    if (visible < int32_t(ranks)) throw KernelError(ErrorKind::Topology);
+    int32_t cc = 0, sms = 0;
+    uint64_t total = 0;
+    NativeDeviceIdentity id;
+    check(glmaxx_device_bind(int32_t(rank), &cc, &sms, &total, id.device_uuid.data()));
+    if (cc / 10 != 10 || sms <= 0 || total == 0) throw KernelError(ErrorKind::Topology);
+    id.visible_devices = uint32_t(visible);
+    id.device_index = rank;
+    id.compute_capability = uint32_t(cc);
+    id.multiprocessor_count = uint32_t(sms);
+    id.total_memory_bytes = total;
+    return NativeRankContext(id, NativeStream::create());
+  }
+  NativeRankContext(NativeRankContext&&) = default;
+  NativeRankContext& operator=(NativeRankContext&&) = default;
+  const NativeDeviceIdentity& identity() const { return id_; }
+  uint64_t stream() const {
+    require_owner();
+    return stream_.get();
+  }
+  void synchronize() const {
+    require_owner();
+    stream_.synchronize();
+  }
+  uint64_t free_memory_bytes() const {
+    require_owner();
+    uint64_t free_b = 0, total_b = 0;
+    check(glmaxx_device_memory_info(&free_b, &total_b));
+    if (free_b == 0 || total_b != id_.total_memory_bytes || free_b > total_b)
+      throw KernelError(ErrorKind::Topology);
+    return free_b;
+  }
+  void require_owner() const {
+    if (std::this_thread::get_id() != owner_) throw KernelError(ErrorKind::Topology);
+  }
+
+ private:
+  NativeRankContext(NativeDeviceIdentity id, NativeStream s)
+      : id_(id), stream_(std::move(s)), owner_(std::this_thread::get_id()) {}
+  NativeDeviceIdentity id_;
+  NativeStream stream_;
+  std::thread::id owner_;
+};
+
+// The reference workspace formulas for the fixed TP4 geometry
+// (crates/glm-cuda/src/abi.rs:454-559), which the library's workspace queries
+// must reproduce.
+inline uint64_t reference_fc1_workspace_bytes(uint64_t a) {
+  const uint64_t p = (a + 127) / 128 * 128;
+  return a * 6144 * 2 + p * 3072 + p * 384 + a * 4 + a * 1024 * 4 + 257 * 4;
+}
+inline uint64_t reference_fc2_workspace_bytes(uint64_t rows, uint64_t a) {
+  const uint64_t p = (a + 127) / 128 * 128;
+  return p * 256 + p * 32 + a * 4 + a * 6144 * 4 + a * 6144 * 2 + rows * 6144 * 4 +
+         rows * 8 * 4 + 4;
+}
+
+// Checks, without a device, that the loaded library is this ABI and that its
+// routed FC1/FC2 workspace sizes for (rows, assignments) are the reference's
+// (ffi.rs:3227-3235).
+inline void validate_native_moe_abi(uint32_t rows, uint32_t assignments) {
+  const char* abi = glmaxx_kernel_abi();
+  if (abi == nullptr || std::string(abi) != "glmaxx.sm100.nvfp4.routed_moe.v3")
+    throw KernelError(ErrorKind::Abi);
+  if (rows == 0 || assignments == 0 || uint64_t(assignments) > uint64_t(rows) * 8)
+    throw KernelError(ErrorKind::Shape);
+  const uint64_t fc1 = glmaxx_nvfp4_routed_fc1_workspace_bytes(assignments);
+  const uint64_t fc2 = glmaxx_nvfp4_routed_fc2_workspace_bytes(rows, assignments);
+  if (fc1 != reference_fc1_workspace_bytes(assignments))
+    throw KernelError(ErrorKind::Workspace, 1, reference_fc1_workspace_bytes(assignments), fc1);
+  if (fc2 != reference_fc2_workspace_bytes(rows, assignments))
+    throw KernelError(ErrorKind::Workspace, 2, reference_fc2_workspace_bytes(rows, assignments),
+                      fc2);
+}
+
+// ------------------------------------------------------------------ the step
+// Geometry of one rank's routed-MoE layer (tensor-parallel shard).
+struct MoeGeometry {
+  uint32_t max_tokens = 0;
+  uint32_t hidden = 6144;
+  uint32_t experts = 256;
+  uint32_t local_intermediate = 2048;  // 2048 / tp
+  uint32_t top_k = 8;
+  uint32_t groups = 8;
+  uint32_t topk_groups = 4;
+  float route_scale = 2.5f;
+  uint32_t shared_intermediate = 2048;  // 0: no shared expert
+};
+
+// Device addresses of one rank's weights, in the layouts glmaxx_kernel.h
+// documents for glmaxx_moe_layer_descriptor.  exl3 (optional) is a host struct
+// that must outlive the step.
+struct MoeWeights {
+  uint64_t router_weight_bf16 = 0, router_bias_f32 = 0;
+  uint64_t w13_values = 0, w13_scales = 0, w13_global_f32 = 0;
+  uint64_t w2_values = 0, w2_scales = 0, w2_global_f32 = 0;
+  uint64_t shared13_bf16 = 0, shared2_bf16 = 0;
+  const glmaxx_moe_exl3_experts* exl3 = nullptr;
+};
+
+// One rank's routed-MoE step (glmaxx_moe_layer_launch): owns the route arrays,
+// the validation word and the workspace, sized for max_tokens on both paths.
+// The step runs on the caller's stream; launches on one step object must not
+// overlap on the device.
+class RoutedMoeStep {
+ public:
+  RoutedMoeStep(const NativeRankContext& ctx, const MoeGeometry& g, const MoeWeights& w)
+      : geom_(g), w_(w) {
+    ctx.require_owner();
+    if (g.max_tokens == 0 || g.top_k == 0) throw KernelError(ErrorKind::Shape);
+    route_experts_ = NativeBuffer::allocate(uint64_t(g.max_tokens) * g.top_k * 2);
+    route_weights_ = NativeBuffer::allocate(uint64_t(g.max_tokens) * g.top_k * 4);
+    status_ = NativeBuffer::allocate(16);
+    uint64_t need = 0;
+    for (uint32_t path : {0u, uint32_t(GLMAXX_FC1_PREFILL_GROUPED)}) {
+      glmaxx_moe_layer_descriptor d = descriptor(g.max_tokens, 0, 0, path, 0, 0);
+      const uint64_t b = glmaxx_moe_layer_workspace_bytes(&d);
+      if (b == 0) throw KernelError(ErrorKind::Shape);
+      need = std::max(need, b);
+    }
+    workspace_ = NativeBuffer::allocate(need);
+  }
+
+  const MoeGeometry& geometry() const { return geom_; }
+  uint64_t workspace_bytes() const { return workspace_.bytes(); }
+  uint64_t route_experts_u16() const { return route_experts_.ptr(); }
+  uint64_t route_weights_f32() const { return route_weights_.ptr(); }
+
+  // out[tokens][hidden] fp32 = routed + shared partial of x[tokens][hidden] bf16.
+  // path: 0 auto (decode up to 256 tokens), GLMAXX_FC1_DECODE_PERSISTENT or
+  // GLMAXX_FC1_PREFILL_GROUPED.
+  void launch(uint64_t input_bf16, uint64_t output_f32, uint32_t tokens, uint64_t stream,
+              uint32_t path = 0) {
+    if (tokens == 0 || tokens > geom_.max_tokens) throw KernelError(ErrorKind::Shape);
+    if (input_bf16 == 0 || output_f32 == 0) throw KernelError(ErrorKind::Null);
+    glmaxx_moe_layer_descriptor d =
+        descriptor(tokens, input_bf16, output_f32, path, workspace_.ptr(), workspace_.bytes());
+    int32_t async_error = 0;
+    const int32_t st =
+        glmaxx_moe_layer_launch(&d, reinterpret_cast<void*>(static_cast<uintptr_t>(stream)),
+                                &async_error);
+    if (st == GLMAXX_ERR_NULL) throw KernelError(ErrorKind::Null, st);
+    if (st == GLMAXX_ERR_DESCRIPTOR) throw KernelError(ErrorKind::Shape, st);
+    if (st == GLMAXX_ERR_WRONG_ARCH) throw KernelError(ErrorKind::Abi, st);
+    check(st);
+    if (async_error != 0) throw KernelError(ErrorKind::Async, async_error);
+  }
+
+  // The device validation word of the last launch (waits for `stream`); a
+  // non-zero word raises DeviceValidation with it.
+  void check_device_status(uint64_t stream) const {
+    uint32_t word = 0;
+    status_.download_at(&word, 4, 0, stream);
+    check(glmaxx_stream_synchronize(stream));
+    if (word != 0) throw KernelError(ErrorKind::DeviceValidation, word);
+  }
+
+ private:
+  glmaxx_moe_layer_descriptor descriptor(uint32_t tokens, uint64_t x, uint64_t out, uint32_t path,
+                                         uint64_t ws, uint64_t ws_bytes) const {
+    glmaxx_moe_layer_descriptor d;
+    std::memset(&d, 0, sizeof(d));
+    d.abi_version = GLMAXX_MOE_LAYER_ABI_VERSION;
+    d.struct_bytes = sizeof(d);
+    d.flags = (geom_.shared_intermediate ? uint32_t(GLMAXX_MOE_SHARED_EXPERT) : 0u) |
+              (w_.exl3 ? uint32_t(GLMAXX_MOE_EXL3_EXPERTS) : 0u);
+    d.path = path;
+    d.tokens = tokens;
+    d.hidden = geom_.hidden;
+    d.experts = geom_.experts;
+    d.local_intermediate = geom_.local_intermediate;
+    d.top_k = geom_.top_k;
+    d.groups = geom_.groups;
+    d.topk_groups = geom_.topk_groups;
+    d.route_scale = geom_.route_scale;
+    d.shared_intermediate = geom_.shared_intermediate;
+    d.input_bf16 = x;
+    d.router_weight_bf16 = w_.router_weight_bf16;
+    d.router_bias_f32 = w_.router_bias_f32;
+    d.w13_values = w_.w13_values;
+    d.w13_scales = w_.w13_scales;
+    d.w13_global_f32 = w_.w13_global_f32;
+    d.w2_values = w_.w2_values;
+    d.w2_scales = w_.w2_scales;
+    d.w2_global_f32 = w_.w2_global_f32;
+    d.shared13_bf16 = w_.shared13_bf16;
+    d.shared2_bf16 = w_.shared2_bf16;
+    d.route_experts_u16 = route_experts_.ptr();
+    d.route_weights_f32 = route_weights_.ptr();
+    d.output_f32 = out;
+    d.validation_error_u32 = status_.ptr();
+    d.workspace = ws;
+    d.workspace_bytes = ws_bytes;
+    d.sequence = 1;
+    d.exl3_experts = reinterpret_cast<uint64_t>(w_.exl3);
+    return d;
+  }
+
+  MoeGeometry geom_;
+  MoeWeights w_;
+  NativeBuffer route_experts_, route_weights_, status_, workspace_;
+};
+
+// ------------------------------------------------------------------ row buckets
+constexpr std::array<uint32_t, 8> kDecodeRows = {1, 2, 4, 8, 16, 32, 64, 128};
+constexpr std::array<uint32_t, 5> kPrefillRows = {256, 512, 1024, 2048, 3072};
+
+// The smallest bucket holding `rows` rows (sorted buckets); Shape past the last.
+inline uint32_t bucket_for(uint32_t rows, const std::vector<uint32_t>& buckets) {
+  if (rows == 0) throw KernelError(ErrorKind::Shape);
+  for (uint32_t b : buckets)
+    if (b >= rows) return b;
+  throw KernelError(ErrorKind::Shape);
+}
+
+inline std::vector<uint32_t> reference_buckets() {
+  std::vector<uint32_t> b(kDecodeRows.begin(), kDecodeRows.end());
+  b.insert(b.end(), kPrefillRows.begin(), kPrefillRows.end());
+  return b;
+}
+
+// One executable graph of a RoutedMoeStep per row bucket over persistent,
+// bucket-sized input and output buffers.  run() copies T rows in, zeroes the
+// rows up to the bucket that an earlier call left behind, and replays the
+// bucket's graph; real rows equal an unpadded launch (bit for bit on the decode
+// path: every stage is per row and the split-K layout depends on ceil(T/64)).
+class BucketedMoeGraphs {
+ public:
+  BucketedMoeGraphs(RoutedMoeStep& step, std::vector<uint32_t> buckets)
+      : step_(step), buckets_(std::move(buckets)) {
+    std::sort(buckets_.begin(), buckets_.end());
+    if (buckets_.empty() || buckets_.back() > step.geometry().max_tokens)
+      throw KernelError(ErrorKind::Shape);
+    const uint64_t rows = buckets_.back(), h = step.geometry().hidden;
+    x_ = NativeBuffer::allocate(rows * h * 2);
+    out_ = NativeBuffer::allocate(rows * h * 4);
+  }
+
+  uint64_t output_f32() const { return out_.ptr(); }
+  size_t captured() const { return graphs_.size(); }
+
+  // x_bf16: device rows [rows][hidden]; returns the device address of the fp32
+  // output rows (valid until the next run).
+  uint64_t run(uint64_t x_bf16, uint32_t rows, uint64_t stream) {
+    const uint32_t b = bucket_for(rows, buckets_);
+    const uint64_t h = step_.geometry().hidden;
+    if (dirty_ == 0) x_.zero(stream);
+    check(glmaxx_memcpy_d2d(x_.ptr(), x_bf16, uint64_t(rows) * h * 2, stream));
+    if (dirty_ > rows)
+      check(glmaxx_memset_zero(x_.ptr() + uint64_t(rows) * h * 2, uint64_t(dirty_ - rows) * h * 2,
+                               stream));
+    dirty_ = rows;
+    auto it = graphs_.find(b);
+    if (it == graphs_.end()) {
+      // an uncaptured launch first sizes nothing new (the step's workspace is
+      // fixed) but creates the library's side stream outside the capture
+      step_.launch(x_.ptr(), out_.ptr(), b, stream);
+      NativeGraph::begin(stream);
+      try {
+        step_.launch(x_.ptr(), out_.ptr(), b, stream);
+      } catch (...) {
+        uint64_t discard = 0;
+        glmaxx_stream_end_capture(stream, &discard);
+        if (discard) glmaxx_graph_exec_destroy(discard);
+        throw;
+      }
+      it = graphs_.emplace(b, NativeGraph::end(stream)).first;
+    }
+    it->second.launch(stream);
+    return out_.ptr();
+  }
+
+ private:
+  RoutedMoeStep& step_;
+  std::vector<uint32_t> buckets_;
+  NativeBuffer x_, out_;
+  std::map<uint32_t, NativeGraph> graphs_;
+  uint32_t dirty_ = 0;
+};
+
+// ------------------------------------------------------------------ peer finish
+// The fused tensor-parallel reduce of the ranks' partials over CUDA IPC
+// (glmaxx_moe_finish_peer_launch).  Each rank allocates one block holding a
+// 256-byte signal buffer and the named slots at the same offsets on every rank;
+// the engine's control channel carries local_handle() to the other ranks, and
+// open() maps theirs.  Collective: every rank calls finish() at the same point
+// of its stream.
+class PeerFinish {
+ public:
+  // slot_bytes: the byte size of each named buffer, in order (e.g. partial,
+  // output); every slot is 256-byte aligned.
+  PeerFinish(const NativeRankContext& ctx, uint32_t rank, uint32_t ranks,
+             std::vector<uint64_t> slot_bytes)
+      : rank_(rank), ranks_(ranks) {
+    ctx.require_owner();
+    if (ranks == 0 || ranks > 8 || rank >= ranks) throw KernelError(ErrorKind::Topology);
+    offsets_.push_back(256);
+    uint64_t off = 256;
+    for (uint64_t b : slot_bytes) {
+      if (b == 0) throw KernelError(ErrorKind::Shape);
+      off = checked_add(off, (b + 255) / 256 * 256);
+      offsets_.push_back(off);
+    }
+    block_ = NativeBuffer::allocate(off);
+    block_.zero(ctx.stream());
+    ctx.synchronize();
+    bases_.assign(ranks, 0);
+    bases_[rank] = block_.ptr();
+  }
+  PeerFinish(const PeerFinish&) = delete;
+  PeerFinish& operator=(const PeerFinish&) = delete;
+  ~PeerFinish() {
+    for (uint32_t r = 0; r < ranks_; ++r)
+      if (r != rank_ && bases_[r]) glmaxx_ipc_close(bases_[r]);
+  }
+
+  std::array<uint8_t, 64> local_handle() const {
+    std::array<uint8_t, 64> h{};
+    check(glmaxx_ipc_handle(block_.ptr(), h.data()));
+    return h;
+  }
+  // handles[r]: rank r's local_handle() (this rank's entry is ignored).
+  void open(const std::vector<std::array<uint8_t, 64>>& handles) {
+    if (handles.size() != ranks_) throw KernelError(ErrorKind::Shape);
+    for (uint32_t r = 0; r < ranks_; ++r) {
+      if (r == rank_ || bases_[r]) continue;
+      uint64_t p = 0;
+      check(glmaxx_ipc_open(handles[r].data(), &p));
+      bases_[r] = p;
+    }
+  }
+  // Device address of slot `slot` on rank `r` as mapped here.
+  uint64_t slot(uint32_t slot, uint32_t r) const {
+    if (slot + 1 >= offsets_.size() || r >= ranks_ || bases_[r] == 0)
+      throw KernelError(ErrorKind::Shape);
+    return bases_[r] + offsets_[slot];
+  }
+  uint64_t local(uint32_t s) const { return slot(s, rank_); }
+
+  // out (slot out_slot, fp32) = residual (optional, bf16 or fp32 device
+  // address) + sum over ranks of slot partial_slot, in rank order, on every rank.
+  // two_shot: each rank reduces a slice and writes it into every rank's output.
+  void finish(uint32_t partial_slot, uint32_t out_slot, uint64_t elements, uint64_t stream,
+              bool two_shot, uint64_t residual_f32 = 0, uint64_t residual_bf16 = 0,
+              uint64_t status_u32 = 0) const {
+    std::vector<uint64_t> parts(ranks_), sigs(ranks_), outs(ranks_);
+    for (uint32_t r = 0; r < ranks_; ++r) {
+      parts[r] = slot(partial_slot, r);
+      sigs[r] = bases_[r];
+      outs[r] = slot(out_slot, r);
+    }
+    glmaxx_moe_finish_descriptor d;
+    std::memset(&d, 0, sizeof(d));
+    d.abi_version = GLMAXX_MOE_FINISH_ABI_VERSION;
+    d.struct_bytes = sizeof(d);
+    d.ranks = ranks_;
+    d.elements = elements;
+    d.residual_f32 = residual_f32;
+    d.residual_bf16 = residual_bf16;
+    d.partials_f32 = reinterpret_cast<uint64_t>(parts.data());
+    d.output_f32 = outs[rank_];
+    glmaxx_moe_peer_descriptor p;
+    std::memset(&p, 0, sizeof(p));
+    p.abi_version = GLMAXX_MOE_PEER_ABI_VERSION;
+    p.struct_bytes = sizeof(p);
+    p.flags = two_shot ? GLMAXX_MOE_PEER_TWO_SHOT : GLMAXX_MOE_PEER_ONE_SHOT;
+    p.rank = rank_;
+    p.signals_u32 = reinterpret_cast<uint64_t>(sigs.data());
+    p.outputs_f32 = two_shot ? reinterpret_cast<uint64_t>(outs.data()) : 0;
+    p.status_u32 = status_u32;
+    check(glmaxx_moe_finish_peer_launch(&d, &p,
+                                        reinterpret_cast<void*>(static_cast<uintptr_t>(stream))));
+  }
+
+ private:
+  uint32_t rank_, ranks_;
+  std::vector<uint64_t> offsets_;  // [0] signal buffer end / first slot, then slot ends
+  NativeBuffer block_;
+  std::vector<uint64_t> bases_;
+};
+
+}  // namespace host
+}  // namespace glmaxx

@@ -454,6 +454,11 @@ int32_t glmaxx_exl3_projection_launch(const struct glmaxx_exl3_descriptor* descr
                                       void* cuda_stream, int32_t* asynchronous_error);
 int32_t glmaxx_graph_exec_launch(uint64_t graph_exec, uint64_t stream);
 int32_t glmaxx_graph_exec_destroy(uint64_t graph_exec);
+/* Stream capture (new): begin capturing `stream` (thread-local capture mode); end
+ * it and instantiate the captured work into an executable graph for
+ * glmaxx_graph_exec_launch / glmaxx_graph_exec_destroy. */
+int32_t glmaxx_stream_begin_capture(uint64_t stream);
+int32_t glmaxx_stream_end_capture(uint64_t stream, uint64_t* graph_exec);
 int32_t glmaxx_event_create(uint64_t* event);
 int32_t glmaxx_event_record(uint64_t event, uint64_t stream);
 int32_t glmaxx_event_synchronize(uint64_t event);
