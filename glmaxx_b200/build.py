@@ -2,9 +2,10 @@
 
     python -m glmaxx_b200.build [--force]
 
-Compiles every csrc/*.cu for `-gencode arch=compute_100a,code=sm_100a` in
-parallel and links them into glmaxx_b200/libglmaxx_sm100.so next to this file,
-so the built library travels with the source tree.
+Compiles every csrc/*.cu for `-gencode arch=compute_100a,code=sm_100a` and
+every host-only csrc/*.cpp with g++, in parallel, and links them into
+glmaxx_b200/libglmaxx_sm100.so next to this file, so the built library travels
+with the source tree.
 """
 from __future__ import annotations
 
@@ -34,12 +35,16 @@ def _nvcc() -> str:
 
 
 def _sources():
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _deps():
-    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) +
-                  [ROOT / "include" / "glmaxx_kernel.h", Path(__file__)])
+    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")) + list(CSRC.glob("*.cuh")) +
+                  list(CSRC.glob("*.h")) + list((ROOT / "include").glob("*.h")) + [Path(__file__)])
+
+
+def _cuda_include() -> str:
+    return str(Path(_nvcc()).resolve().parent.parent / "include")
 
 
 def up_to_date() -> bool:
@@ -60,10 +65,15 @@ def build(force: bool = False, verbose: bool = False) -> Path:
 
     def compile_one(src: Path) -> Path:
         obj = BUILD / (src.stem + ".o")
-        cmd = [nvcc, *host_cc, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
+        if src.suffix == ".cpp":
+            cxx = host_cc[1] if host_cc else (shutil.which("g++") or "g++")
+            cmd = [cxx, "-O3", "-std=c++17", "-fPIC", "-Wall", "-Wextra", f"-I{ROOT / 'include'}",
+                   f"-I{CSRC}", f"-I{_cuda_include()}", "-c", str(src), "-o", str(obj)]
+        else:
+            cmd = [nvcc, *host_cc, *ARCH, *FLAGS, "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True, env=env)
         if r.returncode != 0:
-            raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stderr}")
+            raise RuntimeError(f"compile failed on {src.name}:\n{r.stderr}")
         if verbose and r.stderr.strip():
             print(r.stderr)
         return obj
@@ -71,7 +81,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(compile_one, _sources()))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *host_cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart"]
+    cmd = [nvcc, *host_cc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcudart",
+           "-Xlinker", "-lpthread"]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
