@@ -46,6 +46,10 @@ WORKLOADS = {
     "exl3": {"tokens": 32, "zipf": False, "bound": "hbm", "codec": "exl3",
              "metric": "routed-MoE layer tokens/s (EXL3 3-bit decode T=32, 256 experts, top-8)",
              "name": "EXL3 trellis decode T=32 (BASELINE configs[3])"},
+    "load": {"tokens": 0, "zipf": False, "bound": "host-sha256",
+             "metric": "rank-file load GB/s (verify + place one TP4 layer of 256 NVFP4 experts, "
+                       "router and shared expert in HBM)",
+             "name": "native .g5n reader, one TP4 rank file of one MoE layer"},
     "hybrid": {"tokens": 2048, "zipf": True, "bound": "hbm", "codec": "hybrid", "layers": 4,
                "metric": "4-layer routed-MoE stack tokens/s (2048 tokens, 64 NVFP4 + 192 EXL3 "
                          "experts, Zipf routing, bf16 residual)",
@@ -834,9 +838,201 @@ def run_reference(args):
     }), flush=True)
 
 
+LOAD_LAYER = 3
+LOAD_SAMPLE_EXPERTS = 16  # the CPU arms verify a 16-expert layer file (~90 MB)
+
+
+def write_layer_file(path: Path, experts: int, rank: int, seed: int) -> int:
+    """One TP4 rank file of one MoE layer: router (bf16 [E, 6144]) and fp32 bias,
+    per expert NVFP4 gate/up [1024, 6144] and down [6144, 512] (seeded random
+    codes, E4M3 scales 0x30..0x3f, global scale = amax / 2688), bf16 shared
+    expert shard.  Written by the product RankFileBuilder; returns the file size."""
+    import numpy as np
+
+    from glmaxx_b200 import rank_file as R
+    from glmaxx_b200.moe import MoEConfig
+
+    cfg = MoEConfig(experts=experts, tp=4, rank=rank)
+    H, Ir, Isr = cfg.hidden, cfg.local_intermediate, cfg.local_shared
+    rng = np.random.default_rng(seed)
+    pre = f"model.layers.{LOAD_LAYER}.mlp"
+    recs = []
+
+    def add(name, role, expert, axis, flags, payload):
+        recs.append(R.TensorRecord(len(recs), name, role, LOAD_LAYER, expert, axis, flags, payload))
+
+    def plain(n, k, dtype="bf16"):
+        eb = 4 if dtype == "fp32" else 2
+        return R.PlainTensor(dtype, 2 if k else 1, (n, k or 1, 1, 1), (n, k or 1, 1, 1),
+                             rng.integers(0, 256, n * (k or 1) * eb, dtype=np.uint8))
+
+    def nvfp4(n, k, e):
+        amax = np.float32(1.0 + 0.01 * e)
+        return R.Nvfp4Tensor(n, k, n, k, float(amax / np.float32(2688.0)), float(amax),
+                             rng.integers(0, 256, n * k // 2, dtype=np.uint8),
+                             rng.integers(0x30, 0x40, n * k // 16, dtype=np.uint8))
+
+    add(f"{pre}.gate.weight", R.ROLE_ROUTER_WEIGHT, -1, -1, 1, plain(experts, H))
+    add(f"{pre}.gate.e_score_correction_bias", R.ROLE_ROUTER_BIAS, -1, -1, 1,
+        plain(experts, 0, "fp32"))
+    for e in range(experts):
+        add(f"{pre}.experts.{e}.gate_up_proj.weight", R.ROLE_ROUTED_GATE_UP, e, 0, 0b1010,
+            nvfp4(2 * Ir, H, e))
+        add(f"{pre}.experts.{e}.down_proj.weight", R.ROLE_ROUTED_DOWN, e, 1, 0b1100,
+            nvfp4(H, Ir, e))
+    for role, n, k, name, axis, flags in ((R.ROLE_SHARED_GATE, Isr, H, "gate_proj", 0, 0b10010),
+                                          (R.ROLE_SHARED_UP, Isr, H, "up_proj", 0, 0b10010),
+                                          (R.ROLE_SHARED_DOWN, H, Isr, "down_proj", 1, 0b10100)):
+        add(f"{pre}.shared_experts.{name}.weight", role, -1, axis, flags, plain(n, k))
+    manifest = ('{"rank":%d,"schema":"bench-layer"}' % rank).encode()
+    return R.RankFileBuilder(rank, manifest, tensors=recs).write(path, bytes(range(16)))
+
+
+def oracle_load_rate(path: Path) -> tuple[float, float]:
+    """The CPU restatement of the reader (oracle/rank_file.py: open + verify,
+    one thread) over one file: (GB/s of payload, seconds)."""
+    from oracle import rank_file as OR
+    data = path.read_bytes()
+    t0 = time.perf_counter()
+    rd = OR.Reader(data)
+    rd.verify()
+    dt = time.perf_counter() - t0
+    return (rd.pay_region[1] - rd.pay_region[0]) / dt / 1e9, dt
+
+
+def run_load(args):
+    """Rank-file load: the native reader verifies one TP4 rank file of one full
+    MoE layer (~1.4 GB) and places every plane in HBM (load_moe_layers).  Wall
+    clock around synchronised calls: the path is host-driven (read, SHA-256,
+    pinned staging, cudaMemcpyAsync).  The file is page-cache resident."""
+    import shutil
+
+    import torch
+
+    from glmaxx_b200 import rank_file as R
+    from glmaxx_b200.moe import MoEConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    wl = WORKLOADS["load"]
+    tmp = Path(tempfile.mkdtemp(prefix="g5n-bench-"))
+    try:
+        cfg = MoEConfig(tp=4, rank=rank % 4)
+        path = tmp / f"glm52-native-v0-rank{cfg.rank}.g5n"
+        t0 = time.perf_counter()
+        size = write_layer_file(path, EXPERTS, cfg.rank, args.seed + rank)
+        write_s = time.perf_counter() - t0
+        # serial floor: one thread's SHA-256 over the payload; the PCIe copy for context
+        buf = torch.empty(512 << 20, dtype=torch.uint8).numpy()
+        buf[:] = 7
+        sha_gbs = max(buf.nbytes / (lambda t: (R.sha256(buf), time.perf_counter() - t)[1])(
+            time.perf_counter()) / 1e9 for _ in range(3))
+        pinned = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+        dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h2d = []
+        for _ in range(3):
+            e0.record()
+            dst.copy_(pinned, non_blocking=True)
+            e1.record()
+            e1.synchronize()
+            h2d.append(pinned.numel() / (e0.elapsed_time(e1) * 1e-3) / 1e9)
+        del pinned, dst
+        with R.NativeRankReader.open(path) as rd:
+            payload = rd.file_payload_bytes()
+            t = time.perf_counter()
+            rd.verify()
+            verify_gbs = payload / (time.perf_counter() - t) / 1e9
+            warm, steps = 3, max(1, min(args.steps, 8))
+            for _ in range(warm):
+                loaded, _ = R.load_moe_layers(rd, cfg, [LOAD_LAYER], device=dev)
+                del loaded
+            uuid = None
+            try:
+                uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+            except Exception:  # noqa: BLE001
+                pass
+            clocks = ClockSampler(uuid)
+            clocks.start()
+            wall, native, placed = [], [], 0
+            for _ in range(steps):
+                torch.cuda.synchronize()
+                t = time.perf_counter()
+                loaded, proof = R.load_moe_layers(rd, cfg, [LOAD_LAYER], device=dev)
+                torch.cuda.synchronize()
+                wall.append(time.perf_counter() - t)
+                native.append(proof.elapsed_nanoseconds * 1e-9)
+                placed = proof.device_bytes
+                del loaded
+            clock_info = clocks.stop()
+        value = payload / statistics.median(native) / 1e9
+        e2e = payload / statistics.median(wall) / 1e9
+        cpu = None
+        if not args.no_cpu_baseline and rank == 0:
+            small = tmp / "sample.g5n"
+            write_layer_file(small, LOAD_SAMPLE_EXPERTS, cfg.rank, args.seed + 99)
+            rate, secs = oracle_load_rate(small)
+            cpu = {"value": rate, "unit": "GB/s", "cores": 1, "kind": "port",
+                   "sample": f"oracle reader (open + verify) over a {LOAD_SAMPLE_EXPERTS}-expert "
+                             f"layer file ({small.stat().st_size / 1e6:.0f} MB, {secs:.1f} s)"}
+        if rank == 0:
+            print(json.dumps({
+                "metric": wl["metric"], "value": value, "unit": "GB/s", "n_gpus": world,
+                "steps": steps, "warmup": warm, "ms_per_step": statistics.median(native) * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+                "data": "synthetic (seeded NVFP4 codes and scales, written by RankFileBuilder)",
+                "config": {"workload": wl["name"], "file_bytes": size, "payload_bytes": payload,
+                           "tensors": 2 * EXPERTS + 5, "write_s": round(write_s, 2),
+                           "page_cache": "resident (file just written)",
+                           "timing": "wall clock around synchronised calls (host-driven path)"},
+                "roofline": {"bound": wl["bound"], "achieved": value, "peak": sha_gbs,
+                             "unit": "GB/s", "frac": value / sha_gbs, "traffic": None,
+                             "peak_kind": "one host thread's SHA-256 rate measured here (the "
+                                          "whole-payload digest is one serial stream)",
+                             "h2d_pinned_gbs": statistics.median(h2d),
+                             "verify_only_gbs": verify_gbs},
+                "cpu_baseline": cpu,
+                "e2e": {"value": e2e, "unit": "GB/s", "h2d_bytes_per_step": placed,
+                        "d2h_bytes_per_step": 0,
+                        "note": "load_moe_layers: allocation, zero fill, verify, placement"},
+                "gpu_launches": 0, "clocks": clock_info}), flush=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
+def run_load_reference(args):
+    """Reference arm of the load workload: the reader's CPU restatement (the
+    reference reader is Rust; no toolchain here) over the sample file."""
+    import shutil
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    tmp = Path(tempfile.mkdtemp(prefix="g5n-ref-"))
+    try:
+        path = tmp / "sample.g5n"
+        write_layer_file(path, LOAD_SAMPLE_EXPERTS, 0, args.seed + 99)
+        rates = [oracle_load_rate(path)[0] for _ in range(max(1, min(args.steps, 3)))]
+        v = statistics.median(rates)
+        print(json.dumps({
+            "impl": "reference", "metric": WORKLOADS["load"]["metric"], "value": v,
+            "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(rates),
+            "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8", "data": "synthetic", "config": {"workload": WORKLOADS["load"]["name"]},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"{LOAD_SAMPLE_EXPERTS}-expert layer file"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.workload == "load":
+        run_load_reference(args) if args.impl == "reference" else run_load(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

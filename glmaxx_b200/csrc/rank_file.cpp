@@ -40,7 +40,7 @@
 
 static_assert(sizeof(glmaxx_rank_file_info) == 328, "glmaxx_rank_file_info layout");
 static_assert(sizeof(glmaxx_rank_tensor_info) == 136, "glmaxx_rank_tensor_info layout");
-static_assert(sizeof(glmaxx_rank_placement) == 32, "glmaxx_rank_placement layout");
+static_assert(sizeof(glmaxx_rank_placement) == 56, "glmaxx_rank_placement layout");
 static_assert(sizeof(glmaxx_rank_payload_proof) == 88, "glmaxx_rank_payload_proof layout");
 static_assert(sizeof(glmaxx_rank_sink) == 40, "glmaxx_rank_sink layout");
 
@@ -54,7 +54,7 @@ constexpr uint64_t kPayloadAlignment = 256;
 constexpr uint64_t kControlRegionMax = 1ull << 30;
 constexpr uint64_t kControlTotalMax = 512ull << 20;
 constexpr uint64_t kChunkBytes = 8ull << 20;
-constexpr int kSlots = 6;
+constexpr int kSlots = 8;
 constexpr uint16_t kValueLayout = 0x1201;
 constexpr uint16_t kScaleLayout = 0x1201;
 constexpr uint32_t kMcgMultiplier = 0xCBAC1FEDu;
@@ -503,6 +503,64 @@ bool valid_utf8(const uint8_t* p, size_t n) {
   return true;
 }
 
+// Stream staging kept with the file handle between loads: kSlots chunk
+// buffers (pinned once a device load has run), their copy-done events and the
+// pinned NVFP4 global-scale words.  Loads on one handle take its mutex.
+struct Staging {
+  std::mutex mu;
+  bool pinned = false;
+  uint8_t* slot[kSlots] = {};
+  cudaEvent_t done[kSlots] = {};
+  float* scales = nullptr;
+  size_t scales_n = 0;
+
+  ~Staging() { release(); }
+  void release() {
+    for (int i = 0; i < kSlots; ++i) {
+      if (done[i]) cudaEventDestroy(done[i]);
+      if (slot[i]) {
+        if (pinned)
+          cudaFreeHost(slot[i]);
+        else
+          std::free(slot[i]);
+      }
+      done[i] = nullptr;
+      slot[i] = nullptr;
+    }
+    if (scales) cudaFreeHost(scales);
+    scales = nullptr;
+    scales_n = 0;
+    pinned = false;
+  }
+  // Chunk buffers for a load; pinned ones (and events, scale words) when the
+  // load copies to the device.
+  void ensure(bool device, size_t tensors) {
+    if (device && !pinned) release();
+    for (int i = 0; i < kSlots; ++i) {
+      if (slot[i]) continue;
+      if (device) {
+        if (const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&slot[i]), kChunkBytes,
+                                                cudaHostAllocDefault))
+          fail(int32_t(e));
+        if (const cudaError_t e = cudaEventCreateWithFlags(&done[i], cudaEventDisableTiming))
+          fail(int32_t(e));
+      } else {
+        slot[i] = static_cast<uint8_t*>(std::aligned_alloc(4096, kChunkBytes));
+        if (!slot[i]) fail(GLMAXX_RANK_ERR_NVFP4_ALLOCATION);
+      }
+    }
+    pinned |= device;
+    if (device && scales_n < tensors) {
+      if (scales) cudaFreeHost(scales);
+      scales = nullptr;
+      if (const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&scales),
+                                              tensors * sizeof(float), cudaHostAllocDefault))
+        fail(int32_t(e));
+      scales_n = tensors;
+    }
+  }
+};
+
 }  // namespace
 }  // namespace glmaxx::rankfile
 
@@ -521,6 +579,7 @@ struct glmaxx_rank_file {
   std::vector<uint8_t> metadata_bytes;
   std::vector<Nvfp4Meta> nv;
   std::vector<Exl3Meta> ex;
+  mutable Staging staging;
 
   ~glmaxx_rank_file() {
     if (fd >= 0) ::close(fd);
@@ -824,6 +883,18 @@ class Loader {
           (p.dst[0] || p.dst[1] || p.dst[2]))
         fail(GLMAXX_RANK_ERR_ARGUMENT);
       if (is_plain(codec) && (p.dst[1] || p.dst[2])) fail(GLMAXX_RANK_ERR_ARGUMENT);
+      // every destination holds its whole plane
+      const Descriptor& d = f.d[p.tensor_index];
+      uint64_t need[3] = {d.payload_bytes, 0, 0};
+      if (is_nvfp4(codec)) {
+        need[1] = d.aux_bytes;
+        need[2] = 4;
+      } else if (codec == GLMAXX_CODEC_EXL3_SOURCE) {
+        need[1] = 2ull * f.ex[p.tensor_index].logical_k;
+        need[2] = 2ull * f.ex[p.tensor_index].logical_n;
+      }
+      for (int j = 0; j < 3; ++j)
+        if (p.dst[j] && p.dst_bytes[j] < need[j]) fail(GLMAXX_RANK_ERR_ARGUMENT);
       place_[p.tensor_index] = &p;
       device_ |= !host_ && (p.dst[0] || p.dst[1] || p.dst[2]);
     }
@@ -837,18 +908,7 @@ class Loader {
     tensor_error_.assign(n, 0);
   }
 
-  ~Loader() {
-    for (Slot& s : slots_) {
-      if (s.done) cudaEventDestroy(s.done);
-      if (s.data) {
-        if (pinned_)
-          cudaFreeHost(s.data);
-        else
-          std::free(s.data);
-      }
-    }
-    if (scales_host_) cudaFreeHost(scales_host_);
-  }
+  ~Loader() = default;
 
   void run(glmaxx_rank_payload_proof* proof);
 
@@ -876,7 +936,6 @@ class Loader {
   bool host_;
   const glmaxx_rank_sink* sink_;
   bool device_ = false;
-  bool pinned_ = false;
   int device_id_ = 0;
   std::vector<const glmaxx_rank_placement*> place_;
   std::vector<TensorWork> work_;
@@ -994,7 +1053,7 @@ void Loader::finish_tensor(size_t t) {
 
 void Loader::release(Slot& s, bool copied) {
   std::unique_lock<std::mutex> lock(mu_);
-  s.copies |= copied;
+  s.copies |= copied && !host_;  // host destinations are complete when memcpy returns
   if (--s.pending == 0) {
     if (s.copies && !host_) {
       const cudaError_t e = cudaEventRecord(s.done, stream_);
@@ -1079,28 +1138,16 @@ void Loader::run(glmaxx_rank_payload_proof* proof) {
   const auto t_start = clock::now();
   f_.ensure_unchanged();
   const size_t n = f_.d.size();
+  std::unique_lock<std::mutex> staging_lock(f_.staging.mu);
   if (device_) {
-    int32_t e = cuda_code(cudaGetDevice(&device_id_));
-    if (e) fail(e);
-    pinned_ = true;
-    if ((e = cuda_code(cudaHostAlloc(reinterpret_cast<void**>(&scales_host_), n * sizeof(float),
-                                     cudaHostAllocDefault))))
-      fail(e);
-  } else {
-    scales_host_ = nullptr;
+    if (const int32_t e = cuda_code(cudaGetDevice(&device_id_))) fail(e);
   }
-  for (Slot& s : slots_) {
-    if (pinned_) {
-      const int32_t e = cuda_code(cudaHostAlloc(reinterpret_cast<void**>(&s.data), kChunkBytes,
-                                                cudaHostAllocDefault));
-      if (e) fail(e);
-      if (const int32_t e2 = cuda_code(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming)))
-        fail(e2);
-    } else {
-      s.data = static_cast<uint8_t*>(std::aligned_alloc(4096, kChunkBytes));
-      if (!s.data) fail(GLMAXX_RANK_ERR_NVFP4_ALLOCATION);
-    }
+  f_.staging.ensure(device_, n);
+  for (int i = 0; i < kSlots; ++i) {
+    slots_[i].data = f_.staging.slot[i];
+    slots_[i].done = f_.staging.done[i];
   }
+  scales_host_ = f_.staging.scales;
   // NVFP4 global scales first: kernel-consumed control values (format-v0.md section 15)
   for (size_t t = 0; t < n; ++t)
     if (place_[t] && is_nvfp4(f_.d[t].codec_id) && place_[t]->dst[2]) {

@@ -78,7 +78,8 @@ class TensorInfo(ctypes.Structure):
 
 
 class Placement(ctypes.Structure):
-    _fields_ = [("tensor_index", _u32), ("reserved", _u32), ("dst", _u64 * 3)]
+    _fields_ = [("tensor_index", _u32), ("reserved", _u32), ("dst", _u64 * 3),
+                ("dst_bytes", _u64 * 3)]
 
 
 class PayloadProof(ctypes.Structure):
@@ -218,6 +219,23 @@ def _descriptor(t: TensorInfo) -> TensorDescriptor:
         t.exl3_projection)
 
 
+def _destination(a) -> tuple[int, int]:
+    """(address, capacity in bytes) of a placement destination."""
+    if a is None or (isinstance(a, int) and a == 0):
+        return 0, 0
+    if isinstance(a, tuple):
+        return int(a[0]), int(a[1])
+    if isinstance(a, np.ndarray):
+        if not a.flags["C_CONTIGUOUS"]:
+            raise ValueError("placement destination must be contiguous")
+        return a.ctypes.data, a.nbytes
+    if hasattr(a, "data_ptr"):  # torch tensor
+        if not a.is_contiguous():
+            raise ValueError("placement destination must be contiguous")
+        return a.data_ptr(), a.numel() * a.element_size()
+    raise TypeError("placement destination: tensor, array, (address, bytes) or None")
+
+
 def _canonical_json(raw: bytes) -> bool:
     """The manifest's bytes equal its compact, key-sorted serialisation
     (validate_rank_manifest's canonical check, rank_manifest.rs:152-157)."""
@@ -318,14 +336,18 @@ class NativeRankReader:
     def load(self, placements, stream=None, *, exl3_source: bool = False,
              host: bool = False) -> PayloadProof:
         """verify_and_stream with a direct-upload sink: each placement is
-        (tensor_index, dst0, dst1, dst2) with device addresses (host addresses
-        when host=True).  Returns after every copy completed; on an error the
-        destinations hold tentative bytes."""
+        (tensor_index, dst0, dst1, dst2) where a destination is a torch tensor
+        or numpy array (its storage and byte size), an (address, bytes) pair,
+        or None to skip -- device memory, or host memory when host=True.  A
+        destination smaller than its plane is refused before any copy.
+        Returns after every copy completed; on an error the destinations hold
+        tentative bytes."""
         arr = (Placement * max(1, len(placements)))()
         for i, (t, *dst) in enumerate(placements):
             arr[i].tensor_index = t
             for j, a in enumerate(dst):
-                arr[i].dst[j] = int(a)
+                ptr, nbytes = _destination(a)
+                arr[i].dst[j], arr[i].dst_bytes[j] = ptr, nbytes
         flags = (LOAD_EXL3_SOURCE if exl3_source else 0) | (LOAD_HOST_DESTINATIONS if host else 0)
         if stream is None and placements and not host:
             import torch
@@ -738,8 +760,9 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
 
     def shape(i, n, k):
         d = reader.descriptors[i]
-        if tuple(d.logical_shape[:2]) != (n, k):
-            raise ValueError(f"{d.name}: shape {d.logical_shape[:2]} != {(n, k)}")
+        if tuple(d.logical_shape[:2]) != (n, k) or tuple(d.padded_shape[:2]) != (n, k):
+            raise ValueError(f"{d.name}: shape {d.logical_shape[:2]} (padded "
+                             f"{d.padded_shape[:2]}) != {(n, k)}")
         return d
 
     for layer in layers:
@@ -753,7 +776,7 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
             raise ValueError(f"layer {layer}: bias shape")
         router_w = torch.empty((E, H), dtype=torch.bfloat16, device=device)
         bias = torch.empty(E, dtype=torch.float32, device=device)
-        placements += [(rw, router_w.data_ptr(), 0, 0), (rb, bias.data_ptr(), 0, 0)]
+        placements += [(rw, router_w, None, None), (rb, bias, None, None)]
 
         codec = torch.zeros(E, dtype=torch.uint8)
         for e in range(E):
@@ -790,10 +813,8 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
                     raise ValueError(f"layer {layer} expert {e}: routed weights must be NVFP4 1D")
                 amax13[e], amax2[e] = d13.global_amax, d2.global_amax
                 placements += [
-                    (i13, w13.values[e].data_ptr(), w13.scales[e].data_ptr(),
-                     w13.global_scale[e:e + 1].data_ptr()),
-                    (i2, w2.values[e].data_ptr(), w2.scales[e].data_ptr(),
-                     w2.global_scale[e:e + 1].data_ptr())]
+                    (i13, w13.values[e], w13.scales[e], w13.global_scale[e:e + 1]),
+                    (i2, w2.values[e], w2.scales[e], w2.global_scale[e:e + 1])]
             else:
                 for proj, role, trellis, suh, svh, kn in (
                         (EXL3_GATE, ROLE_ROUTED_GATE_UP, ex.gate_trellis, ex.gate_suh,
@@ -804,8 +825,7 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
                          ex.down_svh, (H, Ir))):
                     i = one(role, layer, e, proj)
                     shape(i, *kn)
-                    placements.append((i, trellis[e].data_ptr(), suh[e].data_ptr(),
-                                       svh[e].data_ptr()))
+                    placements.append((i, trellis[e], suh[e], svh[e]))
         if w13 is not None:
             w13.global_amax.copy_(torch.from_numpy(amax13))
             w2.global_amax.copy_(torch.from_numpy(amax2))
@@ -819,8 +839,8 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
                 shape(i, n, k)
             shared13 = torch.empty((2 * Isr, H), dtype=torch.bfloat16, device=device)
             shared2 = torch.empty((H, Isr), dtype=torch.bfloat16, device=device)
-            placements += [(ig, shared13[:Isr].data_ptr(), 0, 0),
-                           (iu, shared13[Isr:].data_ptr(), 0, 0), (idn, shared2.data_ptr(), 0, 0)]
+            placements += [(ig, shared13[:Isr], None, None), (iu, shared13[Isr:], None, None),
+                           (idn, shared2, None, None)]
         out[layer] = RankWeights(router_w, bias, w13, w2, shared13, shared2, ex)
     if not host:
         torch.cuda.synchronize(device)  # zero fills and amax copies precede the streamed planes

@@ -175,11 +175,14 @@ typedef struct glmaxx_rank_tensor_info {
  *   NVFP4 (0x0100/0x0101): dst[0] = value plane, dst[1] = swizzled scale plane,
  *                          dst[2] = fp32 global scale (4 bytes)
  *   EXL3  (0x0200):        dst[0] = trellis words, dst[1] = suh (K fp16),
- *                          dst[2] = svh (N fp16); the codebook marker is checked */
+ *                          dst[2] = svh (N fp16); the codebook marker is checked
+ * dst_bytes[i] is the capacity at dst[i]; a placement whose plane is larger
+ * than its capacity is refused (GLMAXX_RANK_ERR_ARGUMENT) before any copy. */
 typedef struct glmaxx_rank_placement {
   uint32_t tensor_index;
   uint32_t reserved;
   uint64_t dst[3];
+  uint64_t dst_bytes[3];
 } glmaxx_rank_placement;
 
 /* RankPayloadProof (native_reader.rs:653-662) plus the load's own accounting. */

@@ -299,9 +299,7 @@ def test_host_placement_bytes(tmp_path):
         gscale = np.zeros(1, np.float32)
         trellis = np.zeros(rd.descriptors[2].payload_bytes, np.uint8)
         suh, svh = np.zeros(128, np.uint16), np.zeros(128, np.uint16)
-        a = lambda x: x.ctypes.data  # noqa: E731
-        placements = [(0, a(plain)), (1, a(values), a(scales), a(gscale)),
-                      (2, a(trellis), a(suh), a(svh))]
+        placements = [(0, plain), (1, values, scales, gscale), (2, trellis, suh, svh)]
         with pytest.raises(R.RankFileError) as e:  # EXL3 source needs the explicit flag
             rd.load(placements, host=True)
         assert e.value.kind == "Argument"
@@ -315,8 +313,14 @@ def test_host_placement_bytes(tmp_path):
         assert suh.tobytes() == aux[4:260] and svh.tobytes() == aux[260:]
         assert proof.device_bytes == 16 + values.nbytes + scales.nbytes + 4 + trellis.nbytes + 512
         with pytest.raises(R.RankFileError) as e:  # one placement per tensor
-            rd.load([(0, a(plain)), (0, a(plain))], host=True)
+            rd.load([(0, plain), (0, plain)], host=True)
         assert e.value.kind == "Argument"
+        for short in ([(0, plain[:15])], [(1, values, scales[:-1], None)],
+                      [(1, None, None, gscale.view(np.uint8)[:3])],
+                      [(2, None, suh[:127], None)]):  # every destination holds its plane
+            with pytest.raises(R.RankFileError) as e:
+                rd.load(short, host=True, exl3_source=True)
+            assert e.value.kind == "Argument"
 
 
 def _descriptor_start(b):
@@ -617,7 +621,7 @@ def test_unsafe_files_and_sink_failure(tmp_path):
         rd.verify()  # the reader stays usable
 
 
-def _big_family(experts=8, seed=5):
+def _big_family(experts=16, seed=5):
     """NVFP4 gate/up shards at the TP4 shape [1024, 6144] (3.1 MB values each),
     so planes straddle the 8 MiB stream chunks and several workers run."""
     rng = np.random.default_rng(seed)
@@ -637,7 +641,7 @@ def test_multichunk_stream_and_placement(tmp_path):
     specs = _big_family()
     conv = OR.conversion_uuid([(r, manifest(r, "big"), specs) for r in range(4)])
     data = OR.build(0, manifest(0, "big"), specs, conv)
-    assert len(data) > 3 * R.STREAM_CHUNK_BYTES
+    assert len(data) > 6 * R.STREAM_CHUNK_BYTES  # more chunks than staging slots: slots reused
     product = to_product(0, manifest(0, "big"), specs, (bytes(32),) * 5)
     assert product.build(conv) == data
     path = tmp_path / "big.g5n"
@@ -646,8 +650,7 @@ def test_multichunk_stream_and_placement(tmp_path):
     with R.NativeRankReader.open(path) as rd:
         bufs = [(np.zeros(d.payload_bytes, np.uint8), np.zeros(d.aux_bytes, np.uint8))
                 for d in rd.descriptors]
-        proof = rd.load([(i, v.ctypes.data, s.ctypes.data, 0) for i, (v, s) in enumerate(bufs)],
-                        host=True)
+        proof = rd.load([(i, v, s, None) for i, (v, s) in enumerate(bufs)], host=True)
         assert proof.stream_chunks == -(-rd.file_payload_bytes() // R.STREAM_CHUNK_BYTES)
         for i, (v, s) in enumerate(bufs):
             assert v.tobytes() == bytes(o.planes(i)[0]) and s.tobytes() == bytes(o.planes(i)[1])
@@ -683,6 +686,6 @@ def test_rank_file_abi_exports_and_layouts():
         assert fn.argtypes is not None or n == "glmaxx_sha256_accelerated", n
     assert ctypes.sizeof(R.RankFileInfo) == 328
     assert ctypes.sizeof(R.TensorInfo) == 136
-    assert ctypes.sizeof(R.Placement) == 32
+    assert ctypes.sizeof(R.Placement) == 56
     assert ctypes.sizeof(R.PayloadProof) == 88
     assert ctypes.sizeof(R._Sink) == 40
