@@ -8,7 +8,9 @@
 // step: RoutedMoeStep, its per-row-bucket graphs (the engine's GraphKey
 // verifier_row_bucket, crates/glm-engine/src/graph.rs:13-80, with the buckets of
 // crates/glm-cli/src/profile.rs:10-11), and PeerFinish, the fused tensor-parallel
-// reduce over CUDA IPC mappings.
+// reduce over CUDA IPC mappings.  NativeRankFile and RankLayerWeights read
+// .g5n rank files (glmaxx_rank_file.h; the reference's NativeRankReader,
+// crates/glm-format/src/native_reader.rs) straight into a step's weights.
 //
 // Header-only: it calls only the extern "C" functions of glmaxx_kernel.h, so a
 // C++ engine links libglmaxx_sm100.so and includes this file.  Every failure
@@ -27,6 +29,7 @@
 #include <vector>
 
 #include "glmaxx_kernel.h"
+#include "glmaxx_rank_file.h"
 
 namespace glmaxx {
 namespace host {
@@ -626,6 +629,196 @@ class PeerFinish {
   std::vector<uint64_t> offsets_;  // [0] signal buffer end / first slot, then slot ends
   NativeBuffer block_;
   std::vector<uint64_t> bases_;
+};
+
+// ------------------------------------------------------------------ rank files
+// A reader error: code is a GLMAXX_RANK_ERR_* value (or a cudaError_t), kind()
+// the reference variant it mirrors (RankFileError, Nvfp4Error, Exl3Error or the
+// reader's I/O / UnsafeFile / Changed / Sink arms, native_reader.rs:664-671).
+class RankFileError : public std::runtime_error {
+ public:
+  explicit RankFileError(int32_t code)
+      : std::runtime_error(std::string("RankFile(") + glmaxx_rank_file_error_name(code) + ")"),
+        code_(code) {}
+  int32_t code() const { return code_; }
+  const char* kind() const { return glmaxx_rank_file_error_name(code_); }
+
+ private:
+  int32_t code_;
+};
+
+inline void check_rank(int32_t status) {
+  if (status != 0) throw RankFileError(status);
+}
+
+// One opened, validated rank file (NativeRankReader::open, native_reader.rs:
+// 119-335); move-only.  verify / load read the payload once (verify_and_stream).
+class NativeRankFile {
+ public:
+  static NativeRankFile open(const std::string& path) {
+    glmaxx_rank_file* h = nullptr;
+    check_rank(glmaxx_rank_file_open(path.c_str(), &h));
+    NativeRankFile f(h);
+    check_rank(glmaxx_rank_file_info_get(h, &f.info_));
+    f.tensors_.resize(f.info_.tensor_count);
+    for (uint32_t i = 0; i < f.info_.tensor_count; ++i)
+      check_rank(glmaxx_rank_file_tensor(h, i, &f.tensors_[i]));
+    return f;
+  }
+  NativeRankFile(NativeRankFile&& o) noexcept
+      : h_(std::exchange(o.h_, nullptr)), info_(o.info_), tensors_(std::move(o.tensors_)) {}
+  NativeRankFile& operator=(NativeRankFile&& o) noexcept {
+    std::swap(h_, o.h_);
+    std::swap(info_, o.info_);
+    std::swap(tensors_, o.tensors_);
+    return *this;
+  }
+  NativeRankFile(const NativeRankFile&) = delete;
+  NativeRankFile& operator=(const NativeRankFile&) = delete;
+  ~NativeRankFile() {
+    if (h_) glmaxx_rank_file_close(h_);
+  }
+
+  const glmaxx_rank_file* handle() const { return h_; }
+  const glmaxx_rank_file_info& info() const { return info_; }
+  size_t tensor_count() const { return tensors_.size(); }
+  const glmaxx_rank_tensor_info& tensor(size_t i) const {
+    if (i >= tensors_.size()) throw RankFileError(GLMAXX_RANK_ERR_TENSOR_ID);
+    return tensors_[i];
+  }
+  std::string tensor_name(size_t i) const {
+    const glmaxx_rank_tensor_info& t = tensor(i);
+    return std::string(t.name, t.name_bytes);
+  }
+  std::vector<uint8_t> codec_metadata(size_t i) const {
+    const uint8_t* p = nullptr;
+    uint64_t n = 0;
+    check_rank(glmaxx_rank_file_codec_metadata(h_, uint32_t(i), &p, &n));
+    return std::vector<uint8_t>(p, p + n);
+  }
+  // Tensors of one role, layer and expert (-1: not expert-specific); EXL3
+  // projection 1/2/3 or 0 for any.  Selection is by role id, never by name
+  // (format-v0.md section 18).
+  std::vector<size_t> find(uint16_t role, int16_t layer, int16_t expert,
+                           uint8_t projection = 0) const {
+    std::vector<size_t> out;
+    for (size_t i = 0; i < tensors_.size(); ++i) {
+      const glmaxx_rank_tensor_info& t = tensors_[i];
+      if (t.role_id == role && t.layer_id == layer && t.expert_id == expert &&
+          (projection == 0 || t.exl3_projection == projection))
+        out.push_back(i);
+    }
+    return out;
+  }
+  glmaxx_rank_payload_proof verify() const { return load({}, 0, 0); }
+  glmaxx_rank_payload_proof load(const std::vector<glmaxx_rank_placement>& placements,
+                                 uint64_t stream, uint32_t flags = 0) const {
+    glmaxx_rank_payload_proof proof;
+    check_rank(glmaxx_rank_file_verify_and_stream(
+        h_, placements.empty() ? nullptr : placements.data(), uint32_t(placements.size()), flags,
+        reinterpret_cast<void*>(static_cast<uintptr_t>(stream)), &proof));
+    return proof;
+  }
+  // validate_rank_set (native_reader.rs:543-588): ranks 0..3 in order.
+  static void validate_set(const std::array<const NativeRankFile*, 4>& files) {
+    const glmaxx_rank_file* h[4];
+    for (int r = 0; r < 4; ++r) h[r] = files[r] ? files[r]->h_ : nullptr;
+    check_rank(glmaxx_rank_file_validate_set(h));
+  }
+
+ private:
+  explicit NativeRankFile(glmaxx_rank_file* h) : h_(h) { std::memset(&info_, 0, sizeof(info_)); }
+  glmaxx_rank_file* h_ = nullptr;
+  glmaxx_rank_file_info info_;
+  std::vector<glmaxx_rank_tensor_info> tensors_;
+};
+
+// One NVFP4 MoE layer of a rank file placed in new device buffers, laid out as
+// MoeWeights documents: router [E, H] bf16 (role 0x0301), bias [E] fp32
+// (0x0302), per expert NVFP4 gate/up [2*I_r, H] (0x0501) and down [H, I_r]
+// (0x0502) with their global scales, shared gate/up/down bf16 (0x0601-0x0603).
+// Shapes must equal the geometry (logical and padded); one verified pass over
+// the file.
+class RankLayerWeights {
+ public:
+  static constexpr uint16_t kRouterWeight = 0x0301, kRouterBias = 0x0302, kGateUp = 0x0501,
+                            kDown = 0x0502, kSharedGate = 0x0601, kSharedUp = 0x0602,
+                            kSharedDown = 0x0603;
+
+  static RankLayerWeights load(const NativeRankFile& file, const MoeGeometry& g, int16_t layer,
+                               uint64_t stream) {
+    const uint64_t E = g.experts, H = g.hidden, Ir = g.local_intermediate,
+                   Is = g.shared_intermediate;
+    RankLayerWeights w;
+    w.router_ = NativeBuffer::allocate(E * H * 2);
+    w.bias_ = NativeBuffer::allocate(E * 4);
+    w.w13v_ = NativeBuffer::allocate(E * 2 * Ir * H / 2);
+    w.w13s_ = NativeBuffer::allocate(E * 2 * Ir * H / 16);
+    w.w13g_ = NativeBuffer::allocate(E * 4);
+    w.w2v_ = NativeBuffer::allocate(E * H * Ir / 2);
+    w.w2s_ = NativeBuffer::allocate(E * H * Ir / 16);
+    w.w2g_ = NativeBuffer::allocate(E * 4);
+    std::vector<glmaxx_rank_placement> pl;
+    auto one = [&](uint16_t role, int16_t expert, uint16_t codec, uint64_t n, uint64_t k) {
+      const std::vector<size_t> idx = file.find(role, layer, expert);
+      if (idx.size() != 1) throw KernelError(ErrorKind::Shape, role);
+      const glmaxx_rank_tensor_info& t = file.tensor(idx[0]);
+      const uint64_t ln = t.logical_shape[0], lk = t.ndim > 1 ? t.logical_shape[1] : 1;
+      const uint64_t pn = t.padded_shape[0], pk = t.ndim > 1 ? t.padded_shape[1] : 1;
+      if (t.codec_id != codec || ln != n || lk != k || pn != n || pk != k)
+        throw KernelError(ErrorKind::Shape, role);
+      glmaxx_rank_placement p;
+      std::memset(&p, 0, sizeof(p));
+      p.tensor_index = uint32_t(idx[0]);
+      pl.push_back(p);
+      return &pl.back();
+    };
+    auto put = [](glmaxx_rank_placement* p, int j, const NativeBuffer& b, uint64_t offset,
+                  uint64_t bytes) {
+      p->dst[j] = b.ptr() + offset;
+      p->dst_bytes[j] = bytes;
+    };
+    pl.reserve(5 + 2 * E);  // put() writes through one()'s pointer before the next push
+    put(one(kRouterWeight, -1, GLMAXX_CODEC_BF16, E, H), 0, w.router_, 0, E * H * 2);
+    put(one(kRouterBias, -1, GLMAXX_CODEC_FP32, E, 1), 0, w.bias_, 0, E * 4);
+    for (uint64_t e = 0; e < E; ++e) {
+      glmaxx_rank_placement* p = one(kGateUp, int16_t(e), GLMAXX_CODEC_NVFP4_1D, 2 * Ir, H);
+      put(p, 0, w.w13v_, e * Ir * H, Ir * H);
+      put(p, 1, w.w13s_, e * 2 * Ir * H / 16, 2 * Ir * H / 16);
+      put(p, 2, w.w13g_, e * 4, 4);
+      p = one(kDown, int16_t(e), GLMAXX_CODEC_NVFP4_1D, H, Ir);
+      put(p, 0, w.w2v_, e * H * Ir / 2, H * Ir / 2);
+      put(p, 1, w.w2s_, e * H * Ir / 16, H * Ir / 16);
+      put(p, 2, w.w2g_, e * 4, 4);
+    }
+    if (Is) {
+      w.sh13_ = NativeBuffer::allocate(2 * Is * H * 2);
+      w.sh2_ = NativeBuffer::allocate(H * Is * 2);
+      put(one(kSharedGate, -1, GLMAXX_CODEC_BF16, Is, H), 0, w.sh13_, 0, Is * H * 2);
+      put(one(kSharedUp, -1, GLMAXX_CODEC_BF16, Is, H), 0, w.sh13_, Is * H * 2, Is * H * 2);
+      put(one(kSharedDown, -1, GLMAXX_CODEC_BF16, H, Is), 0, w.sh2_, 0, H * Is * 2);
+    }
+    w.proof_ = file.load(pl, stream);
+    w.weights_.router_weight_bf16 = w.router_.ptr();
+    w.weights_.router_bias_f32 = w.bias_.ptr();
+    w.weights_.w13_values = w.w13v_.ptr();
+    w.weights_.w13_scales = w.w13s_.ptr();
+    w.weights_.w13_global_f32 = w.w13g_.ptr();
+    w.weights_.w2_values = w.w2v_.ptr();
+    w.weights_.w2_scales = w.w2s_.ptr();
+    w.weights_.w2_global_f32 = w.w2g_.ptr();
+    w.weights_.shared13_bf16 = Is ? w.sh13_.ptr() : 0;
+    w.weights_.shared2_bf16 = Is ? w.sh2_.ptr() : 0;
+    return w;
+  }
+  const MoeWeights& weights() const { return weights_; }
+  const glmaxx_rank_payload_proof& proof() const { return proof_; }
+
+ private:
+  RankLayerWeights() { std::memset(&proof_, 0, sizeof(proof_)); }
+  NativeBuffer router_, bias_, w13v_, w13s_, w13g_, w2v_, w2s_, w2g_, sh13_, sh2_;
+  MoeWeights weights_;
+  glmaxx_rank_payload_proof proof_;
 };
 
 }  // namespace host

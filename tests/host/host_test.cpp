@@ -1,14 +1,19 @@
 // Test program of the C++ host runtime (include/glmaxx_host.hpp), driven by
 // tests/test_host_cpp.py.
 //
-//   host_test cpu          checks that need no device; exit 0 when all pass
-//   host_test gpu <dir>    runs one rank's routed-MoE step through RoutedMoeStep and
-//                          BucketedMoeGraphs on seeded weights and writes every input
-//                          and output to <dir> for the oracle comparison
+//   host_test cpu            checks that need no device; exit 0 when all pass
+//   host_test gpu <dir>      runs one rank's routed-MoE step through RoutedMoeStep and
+//                            BucketedMoeGraphs on seeded weights and writes every input
+//                            and output to <dir> for the oracle comparison
+//   host_test rankfile <dir> NativeRankFile over <dir>/rank{0..3}.g5n (device-free):
+//                            set validation, verify, lookup, host placement, errors
+//   host_test rankgpu <file> <dir>  RankLayerWeights::load of layer 3 (16 experts, TP4
+//                            geometry) and one RoutedMoeStep on it; writes x and out
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
+#include <iterator>
 #include <string>
 #include <vector>
 
@@ -203,6 +208,89 @@ int run_gpu(const std::string& dir) {
   return failures ? 1 : 0;
 }
 
+std::vector<uint8_t> read_file(const std::string& path) {
+  std::ifstream f(path, std::ios::binary);
+  return std::vector<uint8_t>((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+}
+
+template <typename F>
+std::string rank_error_kind(F&& f) {
+  try {
+    f();
+  } catch (const RankFileError& e) {
+    return e.kind();
+  }
+  return "none";
+}
+
+int run_rankfile(const std::string& dir) {
+  std::vector<NativeRankFile> files;
+  for (int r = 0; r < 4; ++r) files.push_back(NativeRankFile::open(dir + "/rank" + std::to_string(r) + ".g5n"));
+  NativeRankFile::validate_set({&files[0], &files[1], &files[2], &files[3]});
+  EXPECT(rank_error_kind([&] {
+           NativeRankFile::validate_set({&files[1], &files[0], &files[2], &files[3]});
+         }) == std::string("RankSet"));
+  for (int r = 0; r < 4; ++r) {
+    const NativeRankFile& f = files[r];
+    EXPECT(f.info().rank == uint32_t(r) && f.tensor_count() == 3);
+    EXPECT(f.tensor_name(1) == "model.test.nvfp4.weight");
+    EXPECT(f.find(0x0501, 3, 0).size() == 1 && f.find(0x0501, 78, 0, 1).size() == 1);
+    EXPECT(f.codec_metadata(1).size() == 128 && f.codec_metadata(2).size() == 96);
+    const glmaxx_rank_payload_proof v = f.verify();
+    EXPECT(v.tensor_count == 3 && std::memcmp(v.payload_sha256, f.info().payload_sha256, 32) == 0);
+    // the plain tensor placed in host memory equals its bytes in the file
+    const glmaxx_rank_tensor_info& t = f.tensor(0);
+    std::vector<uint8_t> dst(t.payload_bytes, 0xAB);
+    glmaxx_rank_placement p;
+    std::memset(&p, 0, sizeof(p));
+    p.tensor_index = 0;
+    p.dst[0] = reinterpret_cast<uint64_t>(dst.data());
+    p.dst_bytes[0] = dst.size();
+    f.load({p}, 0, GLMAXX_RANK_LOAD_HOST_DESTINATIONS);
+    const std::vector<uint8_t> bytes = read_file(dir + "/rank" + std::to_string(r) + ".g5n");
+    EXPECT(std::memcmp(dst.data(), bytes.data() + t.payload_offset, dst.size()) == 0);
+    p.dst_bytes[0] = dst.size() - 1;  // a destination one byte short
+    EXPECT(rank_error_kind([&] { f.load({p}, 0, GLMAXX_RANK_LOAD_HOST_DESTINATIONS); }) ==
+           std::string("Argument"));
+  }
+  EXPECT(rank_error_kind([&] { NativeRankFile::open(dir + "/truncated.g5n"); }) ==
+         std::string("Truncated"));
+  EXPECT(rank_error_kind([&] { NativeRankFile::open(dir + "/missing.g5n"); }) == std::string("Io"));
+  std::printf("host rankfile checks: %d failure(s)\n", failures);
+  return failures ? 1 : 0;
+}
+
+int run_rankgpu(const std::string& file, const std::string& dir) {
+  NativeRankContext ctx = NativeRankContext::bind(0, 1);
+  const uint64_t s = ctx.stream();
+  MoeGeometry g;
+  g.max_tokens = 64;
+  g.experts = 16;
+  g.groups = 1;
+  g.topk_groups = 1;
+  g.local_intermediate = 512;
+  g.shared_intermediate = 512;
+  const NativeRankFile f = NativeRankFile::open(file);
+  const RankLayerWeights w = RankLayerWeights::load(f, g, 3, s);
+  EXPECT(w.proof().payload_bytes == f.info().payload_bytes);
+  RoutedMoeStep step(ctx, g, w.weights());
+  const uint32_t T = 40;
+  Lcg rng(11);
+  std::vector<uint16_t> x(uint64_t(T) * g.hidden);
+  for (auto& v : x) v = to_bf16(float(rng.normal()));
+  NativeBuffer d_x = NativeBuffer::upload(x.data(), x.size() * 2, s);
+  NativeBuffer d_out = NativeBuffer::allocate(uint64_t(T) * g.hidden * 4);
+  step.launch(d_x.ptr(), d_out.ptr(), T, s);
+  step.check_device_status(s);
+  std::vector<float> out(uint64_t(T) * g.hidden);
+  d_out.download_at(out.data(), out.size() * 4, 0, s);
+  ctx.synchronize();
+  dump(dir + "/x.bin", x);
+  dump(dir + "/out.bin", out);
+  std::printf("host rankgpu run: %d failure(s)\n", failures);
+  return failures ? 1 : 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -210,10 +298,15 @@ int main(int argc, char** argv) {
   try {
     if (mode == "cpu") return run_cpu();
     if (mode == "gpu" && argc > 2) return run_gpu(argv[2]);
+    if (mode == "rankfile" && argc > 2) return run_rankfile(argv[2]);
+    if (mode == "rankgpu" && argc > 3) return run_rankgpu(argv[2], argv[3]);
   } catch (const KernelError& e) {
     std::fprintf(stderr, "KernelError %s\n", e.what());
     return 2;
+  } catch (const RankFileError& e) {
+    std::fprintf(stderr, "RankFileError %s\n", e.what());
+    return 3;
   }
-  std::fprintf(stderr, "usage: host_test cpu | gpu <dir>\n");
+  std::fprintf(stderr, "usage: host_test cpu | gpu <dir> | rankfile <dir> | rankgpu <file> <dir>\n");
   return 64;
 }

@@ -66,3 +66,45 @@ def test_host_runtime_step_matches_oracle(host_test, tmp_path):
     ulp = 2.0 ** (np.floor(np.log2(np.abs(ref).max())) - 7)
     err = float(np.abs(got - ref).max())
     assert err <= 4 * ulp, (err, ulp)
+
+
+def test_host_runtime_rank_files(host_test, tmp_path):
+    """NativeRankFile over four product-written rank files (the reader test
+    fixture of native_reader.rs:1189-1268), device-free."""
+    from glmaxx_b200 import rank_file as R
+    from tests.test_rank_file import family, to_product
+    fam = family("reader")
+    builders = [to_product(r, m, s, ident) for r, m, s, ident in fam]
+    conv = R.RankFileBuilder.derive_conversion_uuid(builders)
+    for b in builders:
+        b.write(tmp_path / f"rank{b.rank}.g5n", conv)
+    (tmp_path / "truncated.g5n").write_bytes((tmp_path / "rank0.g5n").read_bytes()[:4000])
+    r = subprocess.run([str(host_test), "rankfile", str(tmp_path)], capture_output=True, text=True,
+                       timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "0 failure(s)" in r.stdout
+
+
+@pytest.mark.gpu
+def test_host_runtime_layer_from_rank_file(host_test, tmp_path):
+    """RankLayerWeights::load + RoutedMoeStep on a written layer file give the
+    same output as the Python loader's layer on the same input."""
+    import torch
+
+    from glmaxx_b200 import rank_file as R
+    from glmaxx_b200 import synth
+    from glmaxx_b200.moe import MoEConfig, RoutedMoE
+    from tests.gpu_util import assert_layer_close
+    cfg = MoEConfig(experts=16, groups=1, topk_groups=1, tp=4, rank=0)
+    w = synth.make_rank_weights(cfg, seed=31, device="cuda")
+    path = tmp_path / "layer.g5n"
+    R.RankFileBuilder(0, b"{}", tensors=R.moe_layer_records(w, cfg, 3)).write(path, bytes(16))
+    r = subprocess.run([str(host_test), "rankgpu", str(path), str(tmp_path)], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    T, H = 40, cfg.hidden
+    x = torch.from_numpy(np.fromfile(tmp_path / "x.bin", dtype=np.uint16).astype(np.int16)
+                         ).view(torch.bfloat16).reshape(T, H).cuda()
+    got = np.fromfile(tmp_path / "out.bin", dtype=np.float32).reshape(T, H)
+    ref = RoutedMoE(cfg, w, T)(x).cpu().numpy()
+    assert_layer_close(got, ref, "C++ rank-file layer")
