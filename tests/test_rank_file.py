@@ -689,3 +689,44 @@ def test_rank_file_abi_exports_and_layouts():
     assert ctypes.sizeof(R.Placement) == 56
     assert ctypes.sizeof(R.PayloadProof) == 88
     assert ctypes.sizeof(R._Sink) == 40
+
+
+def _resign_all(b: bytearray) -> None:
+    """Recompute every digest after an edit: each descriptor's plane and
+    metadata digests, the metadata region digest, then the header."""
+    d0, n = struct.unpack_from("<Q", b, 56)[0], struct.unpack_from("<I", b, 32)[0]
+    for i in range(n):
+        d = d0 + 256 * i
+        try:
+            for which in ("primary", "aux"):
+                _rehash_plane(b, d, which)
+            mo, mb = struct.unpack_from("<QQ", b, d + 104)
+            b[d + 192:d + 224] = hashlib.sha256(bytes(b[mo:mo + mb])).digest()
+        except struct.error:
+            return
+    OR.resign_header(b)
+
+
+@pytest.mark.parametrize("resign", [False, True])
+def test_fuzzed_files_same_verdict(tmp_path, resign):
+    """Seeded single-byte edits anywhere in the reader fixture (control regions,
+    descriptors, metadata, planes, padding): the native reader and the oracle
+    reach the same verdict on every file."""
+    _, files = oracle_files(family("reader"))
+    base = files[0]
+    rng = np.random.default_rng(1234 + resign)
+    seen = {}
+    for trial in range(160):
+        b = bytearray(base)
+        pos = int(rng.integers(0, len(b)))
+        b[pos] ^= int(rng.integers(1, 256))
+        if resign and pos >= 4096:
+            try:
+                _resign_all(b)
+            except Exception:  # noqa: BLE001 -- an edited offset may point anywhere
+                pass
+        want = oracle_verdict(bytes(b))
+        got = native_verdict(tmp_path, bytes(b), f"fuzz{trial}.g5n")
+        assert got == want, (trial, pos, got, want)
+        seen[want] = seen.get(want, 0) + 1
+    assert len(seen) >= (4 if resign else 3), seen
