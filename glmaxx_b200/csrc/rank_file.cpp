@@ -509,6 +509,7 @@ bool valid_utf8(const uint8_t* p, size_t n) {
 struct Staging {
   std::mutex mu;
   bool pinned = false;
+  int device = -1;  // device of the events (pinned staging only)
   uint8_t* slot[kSlots] = {};
   cudaEvent_t done[kSlots] = {};
   float* scales = nullptr;
@@ -531,14 +532,16 @@ struct Staging {
     scales = nullptr;
     scales_n = 0;
     pinned = false;
+    device = -1;
   }
   // Chunk buffers for a load; pinned ones (and events, scale words) when the
-  // load copies to the device.
-  void ensure(bool device, size_t tensors) {
-    if (device && !pinned) release();
+  // load copies to device dev.  Events belong to one device, so staging made
+  // for another device is rebuilt.
+  void ensure(bool to_device, int dev, size_t tensors) {
+    if (to_device && (!pinned || device != dev)) release();
     for (int i = 0; i < kSlots; ++i) {
       if (slot[i]) continue;
-      if (device) {
+      if (to_device) {
         if (const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&slot[i]), kChunkBytes,
                                                 cudaHostAllocDefault))
           fail(int32_t(e));
@@ -549,8 +552,11 @@ struct Staging {
         if (!slot[i]) fail(GLMAXX_RANK_ERR_NVFP4_ALLOCATION);
       }
     }
-    pinned |= device;
-    if (device && scales_n < tensors) {
+    if (to_device) {
+      pinned = true;
+      device = dev;
+    }
+    if (to_device && scales_n < tensors) {
       if (scales) cudaFreeHost(scales);
       scales = nullptr;
       if (const cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&scales),
@@ -1064,6 +1070,9 @@ void Loader::release(Slot& s, bool copied) {
 }
 
 void Loader::whole_worker() {
+  // it may be a chunk's last consumer, which records the copy event: same device
+  if (device_)
+    if (const cudaError_t e = cudaSetDevice(device_id_)) fatal_.store(int32_t(e));
   for (uint64_t k = 0;; ++k) {
     Slot* s;
     {
@@ -1078,7 +1087,8 @@ void Loader::whole_worker() {
 }
 
 void Loader::plane_worker(int wi) {
-  if (device_ && cudaSetDevice(device_id_) != cudaSuccess) fatal_.store(GLMAXX_RANK_ERR_SINK);
+  if (device_)
+    if (const cudaError_t e = cudaSetDevice(device_id_)) fatal_.store(int32_t(e));
   const size_t n = f_.d.size();
   size_t next = size_t(wi);  // this worker's next unfinished tensor
   uint64_t peak = 0;
@@ -1142,7 +1152,7 @@ void Loader::run(glmaxx_rank_payload_proof* proof) {
   if (device_) {
     if (const int32_t e = cuda_code(cudaGetDevice(&device_id_))) fail(e);
   }
-  f_.staging.ensure(device_, n);
+  f_.staging.ensure(device_, device_id_, n);
   for (int i = 0; i < kSlots; ++i) {
     slots_[i].data = f_.staging.slot[i];
     slots_[i].done = f_.staging.done[i];
