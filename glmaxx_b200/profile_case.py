@@ -1,11 +1,15 @@
 """Run a few routed-MoE layer steps of a chosen shape (the target of ncu captures).
 
     python -m glmaxx_b200.profile_case --experts 64 --tokens 64 --steps 3 [--tp 1] [--path 1]
+        [--codec nvfp4|exl3|hybrid]
 
 Per step the layer launches, in order: router_logits, router_select, compact,
 quant_scatter, FC1 grouped GEMM, fc2_quant, shared FC1 GEMM, shared FC2 GEMM,
 FC2 grouped GEMM, combine.  With --experts < 256 the expert weights of one
-step stay a few GB, which keeps an `ncu --set full` capture small.
+step stay a few GB, which keeps an `ncu --set full` capture small.  With
+--codec exl3 the routed experts are EXL3 3-bit trellises (the decode-fused
+projection for experts with few rows, the trellis-decoding tensor-core GEMM
+for many); hybrid makes a quarter of them NVFP4.
 """
 from __future__ import annotations
 
@@ -27,12 +31,21 @@ def main():
     p.add_argument("--path", type=int, default=0)
     p.add_argument("--shared", type=int, default=2048)
     p.add_argument("--seed", type=int, default=7)
+    p.add_argument("--codec", choices=["nvfp4", "exl3", "hybrid"], default="nvfp4")
     a = p.parse_args()
     groups = 8 if a.experts % 8 == 0 and a.experts >= 64 else 1
     cfg = MoEConfig(experts=a.experts, groups=groups, topk_groups=min(4, groups),
                     shared_intermediate=a.shared, tp=a.tp)
     dev = torch.device("cuda:0")
-    w = synth.make_rank_weights(cfg, seed=a.seed, device=dev)
+    if a.codec == "nvfp4":
+        w = synth.make_rank_weights(cfg, seed=a.seed, device=dev)
+    else:
+        mask = None
+        if a.codec == "hybrid":
+            g = torch.Generator().manual_seed(a.seed)
+            mask = torch.zeros(a.experts, dtype=torch.bool)
+            mask[torch.randperm(a.experts, generator=g)[:a.experts // 4]] = True
+        w = synth.make_exl3_rank_weights(cfg, seed=a.seed, device=dev, nvfp4_experts=mask)
     x = synth.make_input(a.tokens, cfg.hidden, seed=a.seed, device=dev)
     layer = RoutedMoE(cfg, w, a.tokens)
     out = torch.empty((a.tokens, cfg.hidden), dtype=torch.float32, device=dev)
@@ -44,6 +57,7 @@ def main():
     status = layer.device_status()
     touched = int(torch.unique(layer.routes(a.tokens)[0].long()).numel())
     print(json.dumps({"experts": a.experts, "tokens": a.tokens, "tp": a.tp, "steps": a.steps,
+                      "codec": a.codec,
                       "touched_experts": touched, "status": status,
                       "abi": abi.abi_string()}))
     if status:
