@@ -22,6 +22,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <thread>
@@ -733,12 +734,15 @@ class NativeRankFile {
   std::vector<glmaxx_rank_tensor_info> tensors_;
 };
 
-// One NVFP4 MoE layer of a rank file placed in new device buffers, laid out as
+// One MoE layer of a rank file placed in new device buffers, laid out as
 // MoeWeights documents: router [E, H] bf16 (role 0x0301), bias [E] fp32
-// (0x0302), per expert NVFP4 gate/up [2*I_r, H] (0x0501) and down [H, I_r]
-// (0x0502) with their global scales, shared gate/up/down bf16 (0x0601-0x0603).
-// Shapes must equal the geometry (logical and padded); one verified pass over
-// the file.
+// (0x0302), per expert either NVFP4 gate/up [2*I_r, H] (0x0501) and down
+// [H, I_r] (0x0502) with their global scales, or EXL3 gate, up (0x0501,
+// K = H, N = I_r) and down (0x0502, K = I_r, N = H) trellises with suh / svh;
+// shared gate/up/down bf16 (0x0601-0x0603).  A hybrid layer gets a codec
+// vector (1 = EXL3) and zero NVFP4 planes with global scale 1 for its EXL3
+// experts; an all-EXL3 layer has no NVFP4 slabs.  Shapes must equal the
+// geometry (logical and padded); one verified pass over the file.
 class RankLayerWeights {
  public:
   static constexpr uint16_t kRouterWeight = 0x0301, kRouterBias = 0x0302, kGateUp = 0x0501,
@@ -750,22 +754,46 @@ class RankLayerWeights {
     const uint64_t E = g.experts, H = g.hidden, Ir = g.local_intermediate,
                    Is = g.shared_intermediate;
     RankLayerWeights w;
+    std::vector<uint8_t> codec(E, 0);
+    for (uint64_t e = 0; e < E; ++e) {
+      const std::vector<size_t> gu = file.find(kGateUp, layer, int16_t(e));
+      if (!gu.empty() && file.tensor(gu[0]).codec_id == GLMAXX_CODEC_EXL3_SOURCE) codec[e] = 1;
+    }
+    const bool any_exl3 = std::count(codec.begin(), codec.end(), 1) > 0;
+    const bool any_nvfp4 = std::count(codec.begin(), codec.end(), 0) > 0;
     w.router_ = NativeBuffer::allocate(E * H * 2);
     w.bias_ = NativeBuffer::allocate(E * 4);
-    w.w13v_ = NativeBuffer::allocate(E * 2 * Ir * H / 2);
-    w.w13s_ = NativeBuffer::allocate(E * 2 * Ir * H / 16);
-    w.w13g_ = NativeBuffer::allocate(E * 4);
-    w.w2v_ = NativeBuffer::allocate(E * H * Ir / 2);
-    w.w2s_ = NativeBuffer::allocate(E * H * Ir / 16);
-    w.w2g_ = NativeBuffer::allocate(E * 4);
+    if (any_nvfp4) {
+      w.w13v_ = NativeBuffer::allocate(E * 2 * Ir * H / 2);
+      w.w13s_ = NativeBuffer::allocate(E * 2 * Ir * H / 16);
+      w.w2v_ = NativeBuffer::allocate(E * H * Ir / 2);
+      w.w2s_ = NativeBuffer::allocate(E * H * Ir / 16);
+      const std::vector<float> ones(E, 1.0f);  // EXL3 experts' NVFP4 global scale
+      w.w13g_ = NativeBuffer::upload(ones.data(), E * 4, stream);
+      w.w2g_ = NativeBuffer::upload(ones.data(), E * 4, stream);
+      if (any_exl3)
+        for (const NativeBuffer* b : {&w.w13v_, &w.w13s_, &w.w2v_, &w.w2s_}) b->zero(stream);
+    }
+    const uint64_t words = (H / 16) * (Ir / 16) * 48;  // per projection; K*N/16*3 halves
+    if (any_exl3) {
+      for (NativeBuffer* b : {&w.gate_tr_, &w.up_tr_, &w.down_tr_}) *b = NativeBuffer::allocate(E * words * 2);
+      for (NativeBuffer* b : {&w.gate_suh_, &w.up_suh_, &w.down_svh_}) *b = NativeBuffer::allocate(E * H * 2);
+      for (NativeBuffer* b : {&w.gate_svh_, &w.up_svh_, &w.down_suh_}) *b = NativeBuffer::allocate(E * Ir * 2);
+      if (any_nvfp4) {
+        w.codec_ = NativeBuffer::upload(codec.data(), E, stream);
+        for (NativeBuffer* b : {&w.gate_tr_, &w.up_tr_, &w.down_tr_}) b->zero(stream);
+      }
+    }
     std::vector<glmaxx_rank_placement> pl;
-    auto one = [&](uint16_t role, int16_t expert, uint16_t codec, uint64_t n, uint64_t k) {
-      const std::vector<size_t> idx = file.find(role, layer, expert);
+    pl.reserve(5 + 3 * E);  // put() writes through one()'s pointer before the next push
+    auto one = [&](uint16_t role, int16_t expert, uint16_t codec_id, uint64_t n, uint64_t k,
+                   uint8_t projection = 0) {
+      const std::vector<size_t> idx = file.find(role, layer, expert, projection);
       if (idx.size() != 1) throw KernelError(ErrorKind::Shape, role);
       const glmaxx_rank_tensor_info& t = file.tensor(idx[0]);
       const uint64_t ln = t.logical_shape[0], lk = t.ndim > 1 ? t.logical_shape[1] : 1;
       const uint64_t pn = t.padded_shape[0], pk = t.ndim > 1 ? t.padded_shape[1] : 1;
-      if (t.codec_id != codec || ln != n || lk != k || pn != n || pk != k)
+      if (t.codec_id != codec_id || ln != n || lk != k || pn != n || pk != k)
         throw KernelError(ErrorKind::Shape, role);
       glmaxx_rank_placement p;
       std::memset(&p, 0, sizeof(p));
@@ -778,18 +806,36 @@ class RankLayerWeights {
       p->dst[j] = b.ptr() + offset;
       p->dst_bytes[j] = bytes;
     };
-    pl.reserve(5 + 2 * E);  // put() writes through one()'s pointer before the next push
     put(one(kRouterWeight, -1, GLMAXX_CODEC_BF16, E, H), 0, w.router_, 0, E * H * 2);
     put(one(kRouterBias, -1, GLMAXX_CODEC_FP32, E, 1), 0, w.bias_, 0, E * 4);
     for (uint64_t e = 0; e < E; ++e) {
-      glmaxx_rank_placement* p = one(kGateUp, int16_t(e), GLMAXX_CODEC_NVFP4_1D, 2 * Ir, H);
-      put(p, 0, w.w13v_, e * Ir * H, Ir * H);
-      put(p, 1, w.w13s_, e * 2 * Ir * H / 16, 2 * Ir * H / 16);
-      put(p, 2, w.w13g_, e * 4, 4);
-      p = one(kDown, int16_t(e), GLMAXX_CODEC_NVFP4_1D, H, Ir);
-      put(p, 0, w.w2v_, e * H * Ir / 2, H * Ir / 2);
-      put(p, 1, w.w2s_, e * H * Ir / 16, H * Ir / 16);
-      put(p, 2, w.w2g_, e * 4, 4);
+      if (codec[e] == 0) {
+        glmaxx_rank_placement* p = one(kGateUp, int16_t(e), GLMAXX_CODEC_NVFP4_1D, 2 * Ir, H);
+        put(p, 0, w.w13v_, e * Ir * H, Ir * H);
+        put(p, 1, w.w13s_, e * 2 * Ir * H / 16, 2 * Ir * H / 16);
+        put(p, 2, w.w13g_, e * 4, 4);
+        p = one(kDown, int16_t(e), GLMAXX_CODEC_NVFP4_1D, H, Ir);
+        put(p, 0, w.w2v_, e * H * Ir / 2, H * Ir / 2);
+        put(p, 1, w.w2s_, e * H * Ir / 16, H * Ir / 16);
+        put(p, 2, w.w2g_, e * 4, 4);
+      } else {  // EXL3 source projections: descriptor shape [N, K]
+        struct Proj {
+          uint16_t role;
+          uint8_t projection;
+          uint64_t n, k;
+          const NativeBuffer &tr, &suh, &svh;
+        };
+        const Proj projs[3] = {{kGateUp, 1, Ir, H, w.gate_tr_, w.gate_suh_, w.gate_svh_},
+                               {kGateUp, 2, Ir, H, w.up_tr_, w.up_suh_, w.up_svh_},
+                               {kDown, 3, H, Ir, w.down_tr_, w.down_suh_, w.down_svh_}};
+        for (const Proj& pr : projs) {
+          glmaxx_rank_placement* p =
+              one(pr.role, int16_t(e), GLMAXX_CODEC_EXL3_SOURCE, pr.n, pr.k, pr.projection);
+          put(p, 0, pr.tr, e * words * 2, words * 2);
+          put(p, 1, pr.suh, e * pr.k * 2, pr.k * 2);
+          put(p, 2, pr.svh, e * pr.n * 2, pr.n * 2);
+        }
+      }
     }
     if (Is) {
       w.sh13_ = NativeBuffer::allocate(2 * Is * H * 2);
@@ -798,25 +844,50 @@ class RankLayerWeights {
       put(one(kSharedUp, -1, GLMAXX_CODEC_BF16, Is, H), 0, w.sh13_, Is * H * 2, Is * H * 2);
       put(one(kSharedDown, -1, GLMAXX_CODEC_BF16, H, Is), 0, w.sh2_, 0, H * Is * 2);
     }
-    w.proof_ = file.load(pl, stream);
-    w.weights_.router_weight_bf16 = w.router_.ptr();
-    w.weights_.router_bias_f32 = w.bias_.ptr();
-    w.weights_.w13_values = w.w13v_.ptr();
-    w.weights_.w13_scales = w.w13s_.ptr();
-    w.weights_.w13_global_f32 = w.w13g_.ptr();
-    w.weights_.w2_values = w.w2v_.ptr();
-    w.weights_.w2_scales = w.w2s_.ptr();
-    w.weights_.w2_global_f32 = w.w2g_.ptr();
-    w.weights_.shared13_bf16 = Is ? w.sh13_.ptr() : 0;
-    w.weights_.shared2_bf16 = Is ? w.sh2_.ptr() : 0;
+    w.proof_ = file.load(pl, stream, any_exl3 ? GLMAXX_RANK_LOAD_EXL3_SOURCE : 0);
+    MoeWeights& m = w.weights_;
+    m.router_weight_bf16 = w.router_.ptr();
+    m.router_bias_f32 = w.bias_.ptr();
+    m.w13_values = w.w13v_.ptr();
+    m.w13_scales = w.w13s_.ptr();
+    m.w13_global_f32 = w.w13g_.ptr();
+    m.w2_values = w.w2v_.ptr();
+    m.w2_scales = w.w2s_.ptr();
+    m.w2_global_f32 = w.w2g_.ptr();
+    m.shared13_bf16 = Is ? w.sh13_.ptr() : 0;
+    m.shared2_bf16 = Is ? w.sh2_.ptr() : 0;
+    if (any_exl3) {
+      // heap-held: the step keeps this host struct's address (MoeWeights::exl3)
+      w.exl3_.reset(new glmaxx_moe_exl3_experts());
+      glmaxx_moe_exl3_experts& x = *w.exl3_;
+      std::memset(&x, 0, sizeof(x));
+      x.abi_version = GLMAXX_MOE_EXL3_ABI_VERSION;
+      x.struct_bytes = sizeof(x);
+      x.bits = 3;
+      x.codec_u8 = any_nvfp4 ? w.codec_.ptr() : 0;
+      x.gate_trellis_u16 = w.gate_tr_.ptr();
+      x.up_trellis_u16 = w.up_tr_.ptr();
+      x.down_trellis_u16 = w.down_tr_.ptr();
+      x.gate_suh_f16 = w.gate_suh_.ptr();
+      x.gate_svh_f16 = w.gate_svh_.ptr();
+      x.up_suh_f16 = w.up_suh_.ptr();
+      x.up_svh_f16 = w.up_svh_.ptr();
+      x.down_suh_f16 = w.down_suh_.ptr();
+      x.down_svh_f16 = w.down_svh_.ptr();
+      m.exl3 = w.exl3_.get();
+    }
     return w;
   }
   const MoeWeights& weights() const { return weights_; }
   const glmaxx_rank_payload_proof& proof() const { return proof_; }
+  bool exl3() const { return exl3_ != nullptr; }
 
  private:
   RankLayerWeights() { std::memset(&proof_, 0, sizeof(proof_)); }
   NativeBuffer router_, bias_, w13v_, w13s_, w13g_, w2v_, w2s_, w2g_, sh13_, sh2_;
+  NativeBuffer codec_, gate_tr_, up_tr_, down_tr_, gate_suh_, gate_svh_, up_suh_, up_svh_,
+      down_suh_, down_svh_;
+  std::unique_ptr<glmaxx_moe_exl3_experts> exl3_;
   MoeWeights weights_;
   glmaxx_rank_payload_proof proof_;
 };

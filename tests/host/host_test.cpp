@@ -273,6 +273,7 @@ int run_rankgpu(const std::string& file, const std::string& dir) {
   const NativeRankFile f = NativeRankFile::open(file);
   const RankLayerWeights w = RankLayerWeights::load(f, g, 3, s);
   EXPECT(w.proof().payload_bytes == f.info().payload_bytes);
+  std::printf("layer codec: %s\n", w.exl3() ? "exl3/hybrid" : "nvfp4");
   RoutedMoeStep step(ctx, g, w.weights());
   const uint32_t T = 40;
   Lcg rng(11);

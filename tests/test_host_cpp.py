@@ -86,9 +86,11 @@ def test_host_runtime_rank_files(host_test, tmp_path):
 
 
 @pytest.mark.gpu
-def test_host_runtime_layer_from_rank_file(host_test, tmp_path):
-    """RankLayerWeights::load + RoutedMoeStep on a written layer file give the
-    same output as the Python loader's layer on the same input."""
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_host_runtime_layer_from_rank_file(host_test, tmp_path, hybrid):
+    """RankLayerWeights::load + RoutedMoeStep on a written layer file (NVFP4, or
+    half the experts EXL3) give the same output as the layer run on the
+    generated weights, on the same input."""
     import torch
 
     from glmaxx_b200 import rank_file as R
@@ -96,7 +98,12 @@ def test_host_runtime_layer_from_rank_file(host_test, tmp_path):
     from glmaxx_b200.moe import MoEConfig, RoutedMoE
     from tests.gpu_util import assert_layer_close
     cfg = MoEConfig(experts=16, groups=1, topk_groups=1, tp=4, rank=0)
-    w = synth.make_rank_weights(cfg, seed=31, device="cuda")
+    if hybrid:
+        mask = torch.zeros(cfg.experts, dtype=torch.bool)
+        mask[::2] = True
+        w = synth.make_exl3_rank_weights(cfg, seed=31, device="cuda", nvfp4_experts=mask)
+    else:
+        w = synth.make_rank_weights(cfg, seed=31, device="cuda")
     path = tmp_path / "layer.g5n"
     R.RankFileBuilder(0, b"{}", tensors=R.moe_layer_records(w, cfg, 3)).write(path, bytes(16))
     r = subprocess.run([str(host_test), "rankgpu", str(path), str(tmp_path)], capture_output=True,
@@ -107,4 +114,5 @@ def test_host_runtime_layer_from_rank_file(host_test, tmp_path):
                          ).view(torch.bfloat16).reshape(T, H).cuda()
     got = np.fromfile(tmp_path / "out.bin", dtype=np.float32).reshape(T, H)
     ref = RoutedMoE(cfg, w, T)(x).cpu().numpy()
+    assert ("exl3/hybrid" if hybrid else "nvfp4") in r.stdout
     assert_layer_close(got, ref, "C++ rank-file layer")
