@@ -583,6 +583,7 @@ struct glmaxx_rank_file {
   std::vector<Descriptor> d;
   std::vector<std::string> names;
   std::vector<uint8_t> metadata_bytes;
+  std::vector<uint8_t> manifest_bytes;
   std::vector<Nvfp4Meta> nv;
   std::vector<Exl3Meta> ex;
   mutable Staging staging;
@@ -684,7 +685,7 @@ void glmaxx_rank_file::open(const char* p) {
       payload.start != align_up(metadata.end, kAlignment) || payload.end != file_bytes)
     fail(GLMAXX_RANK_ERR_REGION);
 
-  const std::vector<uint8_t> manifest_bytes = read_control(manifest);
+  manifest_bytes = read_control(manifest);
   const std::vector<uint8_t> descriptor_bytes = read_control(descriptor);
   const std::vector<uint8_t> string_bytes = read_control(strings);
   metadata_bytes = read_control(metadata);
@@ -1316,6 +1317,14 @@ int32_t glmaxx_rank_file_codec_metadata(const glmaxx_rank_file* f, uint32_t inde
   if (index >= f->d.size()) return GLMAXX_RANK_ERR_TENSOR_ID;
   *bytes = f->codec_metadata(index);
   *length = f->d[index].codec_metadata_bytes;
+  return GLMAXX_RANK_OK;
+}
+
+int32_t glmaxx_rank_file_manifest(const glmaxx_rank_file* f, const uint8_t** bytes,
+                                  uint64_t* length) {
+  if (!f || !bytes || !length) return GLMAXX_RANK_ERR_NULL;
+  *bytes = f->manifest_bytes.data();
+  *length = f->manifest_bytes.size();
   return GLMAXX_RANK_OK;
 }
 

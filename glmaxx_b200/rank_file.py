@@ -114,6 +114,7 @@ def _load() -> ctypes.CDLL:
             ("glmaxx_rank_file_info_get", _i32, [vp, pp(RankFileInfo)]),
             ("glmaxx_rank_file_tensor", _i32, [vp, _u32, pp(TensorInfo)]),
             ("glmaxx_rank_file_codec_metadata", _i32, [vp, _u32, pp(vp), pp(_u64)]),
+            ("glmaxx_rank_file_manifest", _i32, [vp, pp(vp), pp(_u64)]),
             ("glmaxx_rank_file_verify_and_stream", _i32,
              [vp, pp(Placement), _u32, _u32, vp, pp(PayloadProof)]),
             ("glmaxx_rank_file_verify_and_stream_sink", _i32, [vp, pp(_Sink), pp(PayloadProof)]),
@@ -276,14 +277,9 @@ class NativeRankReader:
         h = ctypes.c_void_p()
         _check(_load().glmaxx_rank_file_open(str(path).encode(), ctypes.byref(h)))
         reader = cls(path, h)
-        with open(path, "rb") as f:
-            header = f.read(HEADER_BYTES)
-            off, n = struct.unpack_from("<QQ", header, 40)
-            f.seek(off)
-            manifest = f.read(n)
-        if hashlib.sha256(manifest).digest() != reader.manifest_sha256:
-            reader.close()
-            raise RankFileError(-1003)  # the file changed after the native open
+        p, n = ctypes.c_void_p(), _u64()
+        _check(_load().glmaxx_rank_file_manifest(h, ctypes.byref(p), ctypes.byref(n)))
+        manifest = ctypes.string_at(p, n.value) if n.value else b""
         if not _canonical_json(manifest):
             reader.close()
             raise RankFileError(0, "Manifest(NonCanonical)")

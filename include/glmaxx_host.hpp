@@ -691,6 +691,13 @@ class NativeRankFile {
     const glmaxx_rank_tensor_info& t = tensor(i);
     return std::string(t.name, t.name_bytes);
   }
+  // The manifest bytes, digest-checked at open (JSON, not interpreted here).
+  std::string manifest() const {
+    const uint8_t* p = nullptr;
+    uint64_t n = 0;
+    check_rank(glmaxx_rank_file_manifest(h_, &p, &n));
+    return std::string(reinterpret_cast<const char*>(p), n);
+  }
   std::vector<uint8_t> codec_metadata(size_t i) const {
     const uint8_t* p = nullptr;
     uint64_t n = 0;

@@ -219,6 +219,9 @@ int32_t glmaxx_rank_file_tensor(const glmaxx_rank_file* file, uint32_t index,
                                 glmaxx_rank_tensor_info* out);
 int32_t glmaxx_rank_file_codec_metadata(const glmaxx_rank_file* file, uint32_t index,
                                         const uint8_t** bytes, uint64_t* length);
+/* The manifest region's bytes as read and digest-checked at open (valid until close). */
+int32_t glmaxx_rank_file_manifest(const glmaxx_rank_file* file, const uint8_t** bytes,
+                                  uint64_t* length);
 /* Streams the payload region; placements may be NULL when count is 0.
  * stream is a cudaStream_t (NULL: the legacy default stream).  Returns after
  * every copy has completed. */

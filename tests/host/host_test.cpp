@@ -234,6 +234,7 @@ int run_rankfile(const std::string& dir) {
     const NativeRankFile& f = files[r];
     EXPECT(f.info().rank == uint32_t(r) && f.tensor_count() == 3);
     EXPECT(f.tensor_name(1) == "model.test.nvfp4.weight");
+    EXPECT(f.manifest() == "{\"rank\":" + std::to_string(r) + ",\"schema\":\"reader-test\"}");
     EXPECT(f.find(0x0501, 3, 0).size() == 1 && f.find(0x0501, 78, 0, 1).size() == 1);
     EXPECT(f.codec_metadata(1).size() == 128 && f.codec_metadata(2).size() == 96);
     const glmaxx_rank_payload_proof v = f.verify();

@@ -679,7 +679,7 @@ def test_rank_file_abi_exports_and_layouts():
     text = (R.abi.LIB_PATH.parent.parent / "include" / "glmaxx_rank_file.h").read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     names = sorted(set(re.findall(r"\b(glmaxx_[a-z0-9_]+)\s*\(", text)))
-    assert len(names) == 14
+    assert len(names) == 15
     lib = R._load()
     for n in names:
         fn = getattr(lib, n)
