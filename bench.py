@@ -84,6 +84,8 @@ def parse():
     # (one kernel per layer over NVLink) or an NCCL all-reduce plus the finish
     p.add_argument("--reduce", choices=["peer", "nccl"], default="peer")
     p.add_argument("--peer-mode", choices=["auto", "one", "two"], default="auto")
+    # --workload load: rank files loaded at once (1, or a TP4 node's 4 on threads)
+    p.add_argument("--rank-files", type=int, choices=[1, 4], default=1)
     a = p.parse_args()
     if a.tokens is None:
         a.tokens = WORKLOADS[a.workload]["tokens"]
@@ -843,10 +845,15 @@ LOAD_SAMPLE_EXPERTS = 16  # the CPU arms verify a 16-expert layer file (~90 MB)
 
 
 def write_layer_file(path: Path, experts: int, rank: int, seed: int) -> int:
-    """One TP4 rank file of one MoE layer: router (bf16 [E, 6144]) and fp32 bias,
-    per expert NVFP4 gate/up [1024, 6144] and down [6144, 512] (seeded random
-    codes, E4M3 scales 0x30..0x3f, global scale = amax / 2688), bf16 shared
-    expert shard.  Written by the product RankFileBuilder; returns the file size."""
+    """One TP4 rank file of one MoE layer (layer_file_builder); returns its size."""
+    return layer_file_builder(experts, rank, seed).write(path, bytes(range(16)))
+
+
+def layer_file_builder(experts: int, rank: int, seed: int):
+    """RankFileBuilder of one TP4 rank file of one MoE layer: router (bf16
+    [E, 6144]) and fp32 bias, per expert NVFP4 gate/up [1024, 6144] and down
+    [6144, 512] (seeded random codes, E4M3 scales 0x30..0x3f, global scale =
+    amax / 2688), bf16 shared expert shard."""
     import numpy as np
 
     from glmaxx_b200 import rank_file as R
@@ -885,7 +892,7 @@ def write_layer_file(path: Path, experts: int, rank: int, seed: int) -> int:
                                           (R.ROLE_SHARED_DOWN, H, Isr, "down_proj", 1, 0b10100)):
         add(f"{pre}.shared_experts.{name}.weight", role, -1, axis, flags, plain(n, k))
     manifest = ('{"rank":%d,"schema":"bench-layer"}' % rank).encode()
-    return R.RankFileBuilder(rank, manifest, tensors=recs).write(path, bytes(range(16)))
+    return R.RankFileBuilder(rank, manifest, tensors=recs)
 
 
 def oracle_load_rate(path: Path) -> tuple[float, float]:
@@ -925,6 +932,9 @@ def run_load(args):
         t0 = time.perf_counter()
         size = write_layer_file(path, EXPERTS, cfg.rank, args.seed + rank)
         write_s = time.perf_counter() - t0
+        node = None
+        if args.rank_files == 4:
+            node = load_node_rate(tmp, dev, args.seed + rank)
         # serial floor: one thread's SHA-256 over the payload; the PCIe copy for context
         buf = torch.empty(512 << 20, dtype=torch.uint8).numpy()
         buf[:] = 7
@@ -987,6 +997,7 @@ def run_load(args):
                 "config": {"workload": wl["name"], "file_bytes": size, "payload_bytes": payload,
                            "tensors": 2 * EXPERTS + 5, "write_s": round(write_s, 2),
                            "page_cache": "resident (file just written)",
+                           "rank_set": node,
                            "timing": "wall clock around synchronised calls (host-driven path)"},
                 "roofline": {"bound": wl["bound"], "achieved": value, "peak": sha_gbs,
                              "unit": "GB/s", "frac": value / sha_gbs, "traffic": None,
@@ -1001,6 +1012,35 @@ def run_load(args):
                 "gpu_launches": 0, "clocks": clock_info}), flush=True)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+
+
+def load_node_rate(tmp: Path, dev, seed: int) -> dict:
+    """Four TP4 rank files of one layer (ranks 0-3, as one node holds them)
+    validated as a set and loaded concurrently (load_rank_set, one thread per
+    file) into this GPU: aggregate payload GB/s over 3 timed loads."""
+    import torch
+
+    from glmaxx_b200 import rank_file as R
+    from glmaxx_b200.moe import MoEConfig
+    builders = [layer_file_builder(EXPERTS, r, seed + 17 * r) for r in range(4)]
+    conv = R.RankFileBuilder.derive_conversion_uuid(builders)  # covers all four files
+    paths = [tmp / f"node-rank{r}.g5n" for r in range(4)]
+    for b, p in zip(builders, paths):
+        b.write(p, conv)
+    del builders
+    cfgs = [MoEConfig(tp=4, rank=r) for r in range(4)]
+    rates, payload = [], 0
+    for _ in range(4):
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        out, proofs = R.load_rank_set(paths, cfgs, [LOAD_LAYER], [dev] * 4)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t
+        payload = sum(p.payload_bytes for p in proofs)
+        rates.append(payload / dt / 1e9)
+        del out
+    return {"files": 4, "payload_bytes": payload, "aggregate_gbs": statistics.median(rates[1:]),
+            "note": "4 rank files verified and placed concurrently (one thread each)"}
 
 
 def run_load_reference(args):

@@ -744,6 +744,17 @@ def load_moe_layers(reader: NativeRankReader, cfg, layers, device=None, stream=N
 
     device = torch.device(device or "cuda")
     host = device.type == "cpu"
+    if not host:  # allocations, zero fills and the load on that device, from any thread
+        with torch.cuda.device(device):
+            return _load_moe_layers(reader, cfg, layers, device, stream, False)
+    return _load_moe_layers(reader, cfg, layers, device, stream, True)
+
+
+def _load_moe_layers(reader, cfg, layers, device, stream, host):
+    import torch
+
+    from .moe import Exl3Experts, PackedNvfp4, RankWeights
+
     E, H, Ir, Isr = cfg.experts, cfg.hidden, cfg.local_intermediate, cfg.local_shared
     out, placements, need_exl3 = {}, [], False
 
@@ -903,3 +914,21 @@ def moe_layer_records(weights, cfg, layer: int, first_id: int = 0) -> list:
 def _torch_uint8():
     import torch
     return torch.uint8
+
+
+def load_rank_set(paths, cfgs, layers, devices):
+    """A node's four TP rank files: open them, validate_rank_set, then load each
+    rank's layers on its own device concurrently (one thread per file; the
+    native reader runs without the GIL).  Returns ([{layer: RankWeights}] in
+    rank order, [PayloadProof]).  cfgs[r] and devices[r] belong to rank r."""
+    from concurrent.futures import ThreadPoolExecutor
+    readers = [NativeRankReader.open(p) for p in paths]
+    try:
+        NativeRankReader.validate_rank_set(readers)
+        with ThreadPoolExecutor(len(readers)) as pool:
+            results = list(pool.map(lambda r: load_moe_layers(readers[r], cfgs[r], layers,
+                                                              devices[r]), range(len(readers))))
+    finally:
+        for rd in readers:
+            rd.close()
+    return [w for w, _ in results], [p for _, p in results]

@@ -100,3 +100,29 @@ def test_layer_selection_errors(tmp_path):
                            tp=4, rank=0, groups=1, topk_groups=1)
         with pytest.raises(ValueError):  # shapes must match the configuration
             R.load_moe_layers(rd, bigger, [LAYER], device="cpu")
+
+
+def test_rank_set_loads_concurrently(tmp_path):
+    """Four TP rank files, validated as a set and loaded on four threads, place
+    every rank's tensors as a sequential load does."""
+    cfgs = [MoEConfig(hidden=256, experts=4, intermediate=512, shared_intermediate=512, tp=4,
+                      rank=r, groups=1, topk_groups=1) for r in range(4)]
+    ws = [small_weights(c, seed=r) for r, c in enumerate(cfgs)]
+    builders = [R.RankFileBuilder(r, b'{"rank":%d}' % r,
+                                  tensors=R.moe_layer_records(ws[r], cfgs[r], LAYER))
+                for r in range(4)]
+    conv = R.RankFileBuilder.derive_conversion_uuid(builders)
+    for b in builders:
+        b.write(tmp_path / f"r{b.rank}.g5n", conv)
+    paths = [tmp_path / f"r{r}.g5n" for r in range(4)]
+    out, proofs = R.load_rank_set(paths, cfgs, [LAYER], ["cpu"] * 4)
+    assert [p.rank for p in proofs] == [0, 1, 2, 3]
+    for r in range(4):
+        lw, w = out[r][LAYER], ws[r]
+        for a, b in ((lw.router_weight, w.router_weight), (lw.shared2, w.shared2),
+                     (lw.w13.values, w.w13.values), (lw.w2.scales, w.w2.scales),
+                     (lw.w13.global_scale, w.w13.global_scale)):
+            assert same(a, b)
+    with pytest.raises(R.RankFileError) as e:  # ranks out of order
+        R.load_rank_set([paths[1], paths[0], paths[2], paths[3]], cfgs, [LAYER], ["cpu"] * 4)
+    assert e.value.kind == "RankSet"
