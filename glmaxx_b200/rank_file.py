@@ -916,6 +916,56 @@ def _torch_uint8():
     return torch.uint8
 
 
+def _set_identity(reader: NativeRankReader) -> dict:
+    """What validate_rank_set compares of one file (native_reader.rs:543-588):
+    rank, conversion UUID, the five input identities, header flags, the three
+    region digests, and per tensor the descriptor semantics, name and codec
+    semantics (NVFP4 geometry and plane sizes; EXL3 projection, shape, words)."""
+    tensors = []
+    for i, d in enumerate(reader.descriptors):
+        codec = ()
+        m = reader.tensor_codec_metadata(i)
+        if d.codec_id in (CODEC_NVFP4_1D, CODEC_NVFP4_2D):
+            codec = (m[6],) + struct.unpack_from("<IIII", m, 8) + struct.unpack_from("<II", m, 44)
+        elif d.codec_id == CODEC_EXL3_SOURCE:
+            codec = (m[12], m[13]) + struct.unpack_from("<HHII", m, 16) + \
+                struct.unpack_from("<QQ", m, 32)
+        tensors.append((d.tensor_id, d.role_id, d.layer_id, d.expert_id, d.codec_id,
+                        d.logical_dtype, d.stored_dtype, d.tp_shard_axis, d.ndim, d.flags,
+                        d.logical_shape, d.padded_shape, d.payload_bytes, d.aux_bytes,
+                        d.codec_metadata_bytes, d.payload_alignment, d.quant_group_elements,
+                        d.name, codec))
+    return {"rank": reader.rank, "conversion_uuid": reader.conversion_uuid,
+            "identities": b"".join(getattr(reader, n) for n in (
+                "model_config_sha256", "tokenizer_bundle_sha256", "chat_template_sha256",
+                "weight_policy_sha256", "kernel_abi_sha256")),
+            "header_flags": reader.header_flags,
+            "digests": reader.manifest_sha256 + reader.descriptor_sha256 + reader.payload_sha256,
+            "tensors": tensors}
+
+
+def validate_rank_set_distributed(reader: NativeRankReader, group=None) -> None:
+    """validate_rank_set when every rank process holds only its own file: the
+    four files' set identities are all-gathered over ``group`` (torch.distributed,
+    world size 4) and every rank applies the same checks to the same data, so
+    all ranks pass or all raise RankFileError("RankSet") together."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    gathered = [None] * world
+    dist.all_gather_object(gathered, _set_identity(reader), group=group)
+    if world != 4 or any(g["rank"] != r for r, g in enumerate(gathered)):
+        raise RankFileError(-1024)
+    first = gathered[0]
+    h = hashlib.sha256(b"g5n-conversion-v0\0")
+    for g in gathered:
+        for key in ("conversion_uuid", "identities", "header_flags", "tensors"):
+            if g[key] != first[key]:
+                raise RankFileError(-1024)
+        h.update(g["digests"])
+    if h.digest()[:16] != first["conversion_uuid"]:
+        raise RankFileError(-1024)
+
+
 def load_rank_set(paths, cfgs, layers, devices):
     """A node's four TP rank files: open them, validate_rank_set, then load each
     rank's layers on its own device concurrently (one thread per file; the
