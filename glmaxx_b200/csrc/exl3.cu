@@ -104,9 +104,9 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
     for (uint32_t kc = 0; kc < a.K; kc += kExl3KChunk) {
       const uint32_t kn = min(kExl3KChunk, a.K - kc);  // a multiple of 16
       __syncwarp();
-      for (uint32_t i = lane; i < RB * kExl3KChunk; i += 32) {
+      for (uint32_t i = lane; i < nr * kExl3KChunk; i += 32) {  // only this item's rows
         const uint32_t r = i / kExl3KChunk, k = i % kExl3KChunk;
-        xs[r][k] = (r < nr && k < kn) ? h2f(a.x[uint64_t(r0 + r) * a.K + kc + k]) : 0.f;
+        xs[r][k] = k < kn ? h2f(a.x[uint64_t(r0 + r) * a.K + kc + k]) : 0.f;
       }
       __syncwarp();
       uint32_t span[2][3];
@@ -154,7 +154,8 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
           }
         } else {
 #pragma unroll
-          for (int r = 0; r < RB; ++r)
+          for (int r = 0; r < RB; ++r) {
+            if (r >= static_cast<int>(nr)) break;  // nr is the same for the whole warp
 #pragma unroll
             for (int k4 = 0; k4 < 4; ++k4) {
               const float4 xv = *reinterpret_cast<const float4*>(&xs[r][k16 + 4 * k4]);
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
               acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.z, wf[4 * k4 + 2]));
               acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.w, wf[4 * k4 + 3]));
             }
+          }
         }
         __syncwarp();
       }
@@ -365,7 +367,10 @@ __global__ void exl3_rows_swiglu(Exl3RowMap m, const uint16_t* __restrict__ g,
   h[idx] = f2h(__fmul_rn(sv, h2f(u[idx])));
 }
 
-constexpr int kExl3GroupRowBlock = 2;
+// Rows per grouped work item: every item decodes its expert's whole projection,
+// so an expert with 3-4 rows decodes once instead of twice (rows >= 8 take the
+// tensor-core path); the multiply-add work follows the item's real row count.
+constexpr int kExl3GroupRowBlock = 4;
 
 }  // namespace
 
