@@ -11,7 +11,8 @@
 // the same error kind.
 //
 // verify_and_stream reads the payload region once in 8 MiB chunks into a ring
-// of staging slots (pinned when anything goes to the device).  One thread
+// of staging slots (pinned once anything goes to the device, and kept with the
+// file handle between loads).  One thread
 // hashes the whole payload in order; P plane workers each own the tensors
 // t = w (mod P) and, for their tensors, check padding, hash the planes, run
 // the codec validators and issue the device copies; the calling thread reads.
