@@ -922,6 +922,8 @@ def run_load(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if rank != 0:
+        return  # one process measures; a node's ranks load together with --rank-files 4
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     wl = WORKLOADS["load"]
@@ -990,7 +992,8 @@ def run_load(args):
                              f"layer file ({small.stat().st_size / 1e6:.0f} MB, {secs:.1f} s)"}
         if rank == 0:
             print(json.dumps({
-                "metric": wl["metric"], "value": value, "unit": "GB/s", "n_gpus": world,
+                "metric": wl["metric"], "value": value, "unit": "GB/s", "n_gpus": 1,
+                "launched_ranks": world,
                 "steps": steps, "warmup": warm, "ms_per_step": statistics.median(native) * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
                 "data": "synthetic (seeded NVFP4 codes and scales, written by RankFileBuilder)",
