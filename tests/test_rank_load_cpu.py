@@ -126,3 +126,33 @@ def test_rank_set_loads_concurrently(tmp_path):
     with pytest.raises(R.RankFileError) as e:  # ranks out of order
         R.load_rank_set([paths[1], paths[0], paths[2], paths[3]], cfgs, [LAYER], ["cpu"] * 4)
     assert e.value.kind == "RankSet"
+
+
+def test_bench_load_inputs_and_reference_arm(tmp_path):
+    """The load workload's input file (bench.layer_file_builder: router, bias,
+    NVFP4 experts, shared expert of one TP4 layer) verifies natively and in the
+    oracle, and the reference arm of `bench.py --workload load` (the oracle
+    reader) runs on the CPU and prints its JSON line."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import bench
+    path = tmp_path / "layer.g5n"
+    size = bench.write_layer_file(path, 4, 2, seed=5)
+    assert size == path.stat().st_size
+    with R.NativeRankReader.open(path) as rd:
+        assert rd.tensor_count() == 2 * 4 + 5 and rd.rank == 2
+        rd.verify()
+        cfg = MoEConfig(experts=4, tp=4, rank=2, groups=1, topk_groups=1)
+        loaded, _ = R.load_moe_layers(rd, cfg, [bench.LOAD_LAYER], device="cpu")
+        assert loaded[bench.LOAD_LAYER].w13.values.shape == (4, 1024, 3072)
+    OR.Reader(path.read_bytes()).verify()
+    root = Path(bench.__file__).resolve().parent
+    r = subprocess.run([sys.executable, str(root / "bench.py"), "--workload", "load", "--impl",
+                        "reference", "--steps", "1"], capture_output=True, text=True, timeout=600,
+                       cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
