@@ -730,3 +730,27 @@ def test_fuzzed_files_same_verdict(tmp_path, resign):
         assert got == want, (trial, pos, got, want)
         seen[want] = seen.get(want, 0) + 1
     assert len(seen) >= (4 if resign else 3), seen
+
+
+@pytest.mark.parametrize("order", ["scale-encoding-first", "zero-scale-first"])
+def test_earliest_tensor_error_wins_across_workers(tmp_path, order):
+    """Two resigned defects in different tensors of a multi-chunk file (handled
+    by different plane workers): the reader reports the earlier tensor's error,
+    as the reference's in-order stream does, whichever worker finds its own
+    defect first."""
+    specs = _big_family()
+    conv = OR.conversion_uuid([(r, manifest(r, "big"), specs) for r in range(4)])
+    b = bytearray(OR.build(0, manifest(0, "big"), specs, conv))
+    d0 = _descriptor_start(b)
+    early, late = (3, 11)
+    kinds = {"nan": "Nvfp4(ScaleEncoding)", "zero": "Nvfp4(ZeroScaleValue)"}
+    first, second = ("nan", "zero") if order == "scale-encoding-first" else ("zero", "nan")
+    for t, kind in ((early, first), (late, second)):
+        d = d0 + 256 * t
+        ao = struct.unpack_from("<Q", b, d + 88)[0]
+        b[ao + 4096] = 0x7F if kind == "nan" else 0
+        _rehash_plane(b, d, "aux")
+    OR.resign_header(b)
+    want = kinds[first]
+    assert oracle_verdict(bytes(b)) == want
+    assert native_verdict(tmp_path, bytes(b), "two.g5n") == want
