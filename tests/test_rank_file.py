@@ -754,3 +754,32 @@ def test_earliest_tensor_error_wins_across_workers(tmp_path, order):
     want = kinds[first]
     assert oracle_verdict(bytes(b)) == want
     assert native_verdict(tmp_path, bytes(b), "two.g5n") == want
+
+
+def test_changed_file_and_concurrent_verifies(tmp_path):
+    """ensure_unchanged (native_reader.rs:590-604): a file whose timestamps
+    change after open is refused ("Changed"); two threads verifying through one
+    handle take turns on its staging and both succeed."""
+    import threading
+    _, files = oracle_files(family("reader"))
+    path = tmp_path / "r.g5n"
+    path.write_bytes(files[0])
+    with R.NativeRankReader.open(path) as rd:
+        results = []
+
+        def run():
+            try:
+                results.append(bytes(rd.verify().payload_sha256))
+            except R.RankFileError as e:  # pragma: no cover - reported below
+                results.append(e.kind)
+        threads = [threading.Thread(target=run) for _ in range(2)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        assert results == [rd.payload_sha256] * 2
+        st = os.stat(path)
+        os.utime(path, ns=(st.st_atime_ns, st.st_mtime_ns + 1_000_000_000))
+        with pytest.raises(R.RankFileError) as e:
+            rd.verify()
+        assert e.value.kind == "Changed"
