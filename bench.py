@@ -60,11 +60,16 @@ HYBRID_NVFP4_EXPERTS = 64
 # the NVFP4 roofline is the measured cuBLAS bf16 rate scaled by this ratio.
 NVFP4_PER_BF16 = 4.0
 NVFP4_NOMINAL_TFLOPS = 9000.0
-# Zipf skew of the reference arm's own seeded router (bisection value of
-# glmaxx_b200.synth.fit_zipf_beta at the default seed); the arm times a token sample,
-# whose per-token cost does not depend on the skew.
-REF_ZIPF_BETA = 0.04
-REF_TIME_BUDGET_S = 90.0
+# The CPU timing plan (BASELINE CPU baseline): configs[1] and configs[3] are timed
+# on all their tokens; configs[2] on a seeded 512-token subset (per-token rate).
+# Expert weights are dequantised (NVFP4) or decoded (EXL3) once per expert into
+# fp32 planes outside the timed region; the timed part is the router and the
+# layer arithmetic, OpenMP over assignments with SIMD across output columns.
+CPU_PREFILL_SAMPLE_TOKENS = 512
+# prepared experts are held for the whole run when they fit in this fraction of
+# the host's available memory, else rebuilt (untimed) every step
+CPU_HOLD_FRACTION = 0.6
+REF_TIME_BUDGET_S = 120.0
 # measured peer copy over NVLink 5 on this pool, per direction per GPU
 NVLINK_PEER_GBS = 770.0
 
@@ -78,7 +83,6 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--seed", type=int, default=1234)
-    p.add_argument("--cpu-sample-tokens", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     # N > 1: how the ranks' partials are reduced -- the fused peer-memory finish
     # (one kernel per layer over NVLink) or an NCCL all-reduce plus the finish
@@ -181,40 +185,6 @@ def graph_kernel_nodes(graph) -> int | None:
         return None
 
 
-def cpu_baseline_from_device(layer, x, cfg, n_tokens: int):
-    """Oracle port (plain C restatement of crates/glm-reference, sequential fp32,
-    weights dequantised inside the call as the reference oracle does) timed on the
-    host cores for a bounded token sample of the same workload."""
-    import numpy as np
-
-    import oracle as O
-
-    T = x.shape[0]
-    sel = list(range(min(n_tokens, T)))
-    re, rw = layer.routes(T)
-    re = re.cpu().numpy().view(np.uint16)[sel]
-    rw = rw.cpu().numpy()[sel]
-    used = np.unique(re)
-    remap = {int(e): i for i, e in enumerate(used)}
-    re_m = np.vectorize(lambda e: remap[int(e)])(re).astype(np.uint16)
-    w = layer.w
-    idx = torch_index(used)
-    xb = x[sel].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
-    args = (xb, re_m, rw, w.w13.values[idx].cpu().numpy(), w.w13.scales[idx].cpu().numpy(),
-            w.w13.global_scale[idx].cpu().numpy(), w.w2.values[idx].cpu().numpy(),
-            w.w2.scales[idx].cpu().numpy(), w.w2.global_scale[idx].cpu().numpy(),
-            cfg.local_intermediate,
-            None if w.shared13 is None else w.shared13.view(torch_int16()).cpu().numpy().view(np.uint16),
-            None if w.shared2 is None else w.shared2.view(torch_int16()).cpu().numpy().view(np.uint16))
-    O.moe_layer(*args)  # warm (page-in)
-    t0 = time.perf_counter()
-    O.moe_layer(*args)
-    dt = time.perf_counter() - t0
-    return {"value": len(sel) / dt, "unit": UNIT, "cores": O.threads(), "kind": "port",
-            "sample": f"{len(sel)} of {T} tokens ({len(used)} experts), full layer incl. per-call "
-                      f"NVFP4 dequant, {dt:.2f} s"}
-
-
 # FC1 DRAM bytes per launch from ncu (dram__bytes_read.sum + dram__bytes_write.sum)
 # of the decode FC1 at 64 experts, T=64, TP1, divided by the touched experts of that
 # capture; FC1 traffic grows with the touched experts (weights dominate), so a
@@ -228,72 +198,178 @@ def fc1_traffic_estimate(touched: int, world: int):
     return FC1_DECODE_DRAM_BYTES_PER_EXPERT_TP1 * touched / world
 
 
-def exl3_layer_cpu(x16, route_experts, route_weights, tr, sc, H, I):
-    """CPU EXL3 experts for a token sample with the oracle's restated
-    Exl3Trellis::matmul_reference_f16 (crates/glm-format/src/exl3.rs:404-453):
-    gate and up on the fp16 token rows, h = fp16(silu(g) * u), down on h, routing-
-    weighted and summed in ascending expert order.  tr/sc: per-expert uint16 arrays."""
+def host_mem_available() -> int:
+    try:
+        for line in Path("/proc/meminfo").read_text().splitlines():
+            if line.startswith("MemAvailable:"):
+                return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+class PreparedExperts:
+    """The routed experts of a CPU run, each dequantised (NVFP4) or decoded (EXL3)
+    once into fp32 planes outside the timed region.  Held for the whole run when
+    they fit in host memory, else rebuilt every step (still untimed)."""
+
+    def __init__(self, make, n_experts: int, bytes_per_expert: int):
+        self.make = make
+        self.hold = n_experts * bytes_per_expert < CPU_HOLD_FRACTION * host_mem_available()
+        self.cache = {}
+        self.prep_s = 0.0
+
+    def __call__(self, e: int):
+        e = int(e)
+        if e in self.cache:
+            return self.cache[e]
+        t0 = time.perf_counter()
+        v = self.make(e)
+        self.prep_s += time.perf_counter() - t0
+        if self.hold:
+            self.cache[e] = v
+        return v
+
+
+def host_u16(t) -> "np.ndarray":
+    import numpy as np
+    import torch
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def nvfp4_prepare_fn(w, hidden: int, inter: int):
+    """prepare(e): expert e's packed NVFP4 shard copied to the host and dequantised
+    once (nvfp4.rs:279-301) into k-major fp32 planes."""
+    import oracle as O
+
+    def make(e):
+        return O.expert_prepare(w.w13.values[e].cpu().numpy(), w.w13.scales[e].cpu().numpy(),
+                                float(w.w13.global_scale[e]), w.w2.values[e].cpu().numpy(),
+                                w.w2.scales[e].cpu().numpy(), float(w.w2.global_scale[e]),
+                                hidden, inter)
+    return make
+
+
+def exl3_prepare_fn(x3, hidden: int, inter: int):
+    """prepare(e): expert e's gate/up/down trellises decoded once (exl3.rs:490-513)
+    to fp32, with its fp16 rotation signs."""
+    import oracle as O
+
+    def make(e):
+        return {"gate": O.exl3_prepare(host_u16(x3.gate_trellis[e]), hidden, inter),
+                "up": O.exl3_prepare(host_u16(x3.up_trellis[e]), hidden, inter),
+                "down": O.exl3_prepare(host_u16(x3.down_trellis[e]), inter, hidden),
+                **{n: host_u16(getattr(x3, n)[e]) for n in
+                   ("gate_suh", "gate_svh", "up_suh", "up_svh", "down_suh", "down_svh")}}
+    return make
+
+
+def exl3_layer_cpu(xb, route_experts, route_weights, prep):
+    """EXL3 experts of the sample on the CPU: per routed expert (ascending), gate and up
+    = matmul_reference_f16 (crates/glm-format/src/exl3.rs:404-453) on the fp16 token
+    rows, h = fp16(silu(g) * u), down on h; routing-weighted and summed over the slots
+    in ascending expert order.  Returns (routed [S, H], seconds excluding prepare)."""
     import numpy as np
 
     import oracle as O
     S, K = route_experts.shape
-    contrib = np.zeros((S, K, H), np.float32)
+    x16 = (xb.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
+    busy = 0.0
+    contrib = None
     for e in np.unique(route_experts):
-        rows = [(t, k) for t in range(S) for k in range(K) if route_experts[t, k] == e]
-        xin = np.stack([x16[t] for t, _ in rows])
-        g = O.exl3_matmul_reference(tr["gate"][e], H, I, sc["gate_suh"][e], sc["gate_svh"][e], xin)
-        u = O.exl3_matmul_reference(tr["up"][e], H, I, sc["up_suh"][e], sc["up_svh"][e], xin)
+        p = prep(int(e))
+        t0 = time.perf_counter()
+        rows = np.argwhere(route_experts == e)
+        xin = x16[rows[:, 0]]
+        g = O.exl3_project(p["gate"], p["gate_suh"], p["gate_svh"], xin)
+        u = O.exl3_project(p["up"], p["up_suh"], p["up_svh"], xin)
         gf = g.view(np.float16).astype(np.float32)
         uf = u.view(np.float16).astype(np.float32)
         h = (gf / (np.float32(1.0) + np.exp(-gf)) * uf).astype(np.float16).view(np.uint16)
-        d = O.exl3_matmul_reference(tr["down"][e], I, H, sc["down_suh"][e], sc["down_svh"][e], h)
-        df = d.view(np.float16).astype(np.float32)
-        for j, (t, k) in enumerate(rows):
-            contrib[t, k] = np.float32(route_weights[t, k]) * df[j]
-    out = np.zeros((S, H), np.float32)
-    for t in range(S):
-        order = np.argsort(route_experts[t], kind="stable")
-        acc = contrib[t, order[0]].copy()
-        for k in order[1:]:
-            acc = acc + contrib[t, k]
-        out[t] = acc
-    return out
-
-
-def cpu_baseline_exl3(layer, x, cfg, n_tokens: int):
-    """The EXL3 oracle composition timed on the host cores for a token sample
-    (per-call trellis decode, as the reference's CPU matmul does)."""
-    import numpy as np
-    T = x.shape[0]
-    S = min(n_tokens, T)
-    re, rw = layer.routes(T)
-    re = re.cpu().numpy().astype(np.int64)[:S]
-    rw = rw.cpu().numpy()[:S]
-    w = layer.w.exl3
-    used = np.unique(re)
-    tr = {n: {int(e): getattr(w, n + "_trellis")[int(e)].cpu().numpy().view(np.uint16)
-              for e in used} for n in ("gate", "up", "down")}
-    sc = {n: {int(e): getattr(w, n)[int(e)].cpu().numpy().view(np.uint16) for e in used}
-          for n in ("gate_suh", "gate_svh", "up_suh", "up_svh", "down_suh", "down_svh")}
-    xb = x[:S].contiguous().view(torch_int16()).cpu().numpy().view(np.uint16)
-    x16 = (xb.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
-    import oracle as O
+        d = O.exl3_project(p["down"], p["down_suh"], p["down_svh"], h)
+        if contrib is None:
+            contrib = np.zeros((S, K, d.shape[1]), np.float32)
+        contrib[rows[:, 0], rows[:, 1]] = (route_weights[rows[:, 0], rows[:, 1]][:, None] *
+                                           d.view(np.float16).astype(np.float32))
+        busy += time.perf_counter() - t0
     t0 = time.perf_counter()
-    exl3_layer_cpu(x16, re, rw, tr, sc, cfg.hidden, cfg.local_intermediate)
-    dt = time.perf_counter() - t0
-    return {"value": S / dt, "unit": UNIT, "cores": O.threads(), "kind": "port",
-            "sample": f"{S} of {T} tokens ({len(used)} experts), EXL3 gate/up/down per routed "
-                      f"expert with per-call trellis decode, {dt:.2f} s"}
+    order = np.argsort(route_experts, axis=1, kind="stable")
+    out = np.take_along_axis(contrib, order[:, :1, None], 1)[:, 0].copy()
+    for j in range(1, K):
+        out = out + np.take_along_axis(contrib, order[:, j:j + 1, None], 1)[:, 0]
+    busy += time.perf_counter() - t0
+    return out, busy
 
 
-def torch_index(used):
-    import torch
-    return torch.as_tensor(used.astype("int64"))
+def cpu_sample(T: int, workload: str, seed: int):
+    """Token indices the CPU timing covers: every token, except configs[2]'s seeded
+    512-token subset."""
+    import numpy as np
+    if workload == "prefill" and T > CPU_PREFILL_SAMPLE_TOKENS:
+        return np.sort(np.random.default_rng(seed).choice(T, CPU_PREFILL_SAMPLE_TOKENS,
+                                                          replace=False))
+    return np.arange(T)
 
 
-def torch_int16():
-    import torch
-    return torch.int16
+class CpuLayer:
+    """The reference's CPU path of one full layer (oracle/, the C restatement of
+    crates/glm-reference: the router restatement, then the NVFP4 or EXL3 experts and
+    the bf16 shared expert) on a token sample, on all host cores."""
+
+    def __init__(self, w, cfg, codec, xb):
+        import oracle as O
+        self.w, self.cfg, self.codec, self.xb = w, cfg, codec, xb
+        self.wr = host_u16(w.router_weight)
+        self.bias = w.router_bias.cpu().numpy()
+        H, Ir = cfg.hidden, cfg.local_intermediate
+        per = 3 * H * Ir * 4  # fp32 planes of gate, up and down
+        make = exl3_prepare_fn(w.exl3, H, Ir) if codec == "exl3" else nvfp4_prepare_fn(w, H, Ir)
+        self.prep = PreparedExperts(make, cfg.experts, per)
+        t0 = time.perf_counter()
+        self.shared = None if w.shared13 is None else O.shared_prepare(host_u16(w.shared13),
+                                                                       host_u16(w.shared2))
+        self.prep.prep_s += time.perf_counter() - t0
+
+    def step(self):
+        """One timed pass: (seconds excluding expert preparation, touched experts,
+        the layer output [S, H] = routed + shared)."""
+        import numpy as np
+
+        import oracle as O
+        c = self.cfg
+        t0 = time.perf_counter()
+        ex, wt = O.router(self.xb, self.wr, self.bias, c.groups, c.topk_groups, c.top_k,
+                          c.route_scale)
+        busy = time.perf_counter() - t0
+        shared = None
+        if self.codec == "exl3":
+            routed, b = exl3_layer_cpu(self.xb, ex.astype(np.int64), wt, self.prep)
+            busy += b
+            if self.shared is not None:
+                t0 = time.perf_counter()
+                shared = O.shared_rows(self.xb, np.arange(self.xb.shape[0]), *self.shared)
+                busy += time.perf_counter() - t0
+        else:
+            routed, shared, b = O.moe_layer_prepared(self.xb, ex, wt, self.prep,
+                                                     c.local_intermediate, shared=self.shared)
+            busy += b
+        out = routed if shared is None else routed + shared
+        return busy, int(np.unique(ex).size), out
+
+
+def cpu_baseline(w, cfg, codec, x, workload: str, seed: int):
+    """cpu_baseline of our arm: the CPU path timed once on this box's host cores."""
+    import oracle as O
+    T = x.shape[0]
+    sel = cpu_sample(T, workload, seed)
+    xb = host_u16(x)[sel]
+    cl = CpuLayer(w, cfg, codec, xb)
+    busy, touched, _ = cl.step()
+    return {"value": len(sel) / busy, "unit": UNIT, "cores": int(O.lib().orc_threads()),
+            "kind": "port",
+            "sample": f"{len(sel)} of {T} tokens ({touched} experts): router + full layer, "
+                      f"{busy:.2f} s; experts dequantised once outside the timing "
+                      f"({cl.prep.prep_s:.1f} s)"}
 
 
 def run_ours(args):
@@ -666,13 +742,11 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            if codec == "exl3":
-                cpu = cpu_baseline_exl3(layer, x, cfg, args.cpu_sample_tokens)
-            elif codec == "hybrid":
+            if codec == "hybrid":
                 cpu = {"value": None, "unit": UNIT,
                        "note": "see the decode and exl3 workloads' baselines (per codec)"}
             else:
-                cpu = cpu_baseline_from_device(layer, x, cfg, args.cpu_sample_tokens)
+                cpu = cpu_baseline(layer.w, cfg, codec, x, args.workload, args.seed)
         except Exception as exc:  # noqa: BLE001
             cpu = {"value": None, "unit": UNIT, "error": repr(exc)[:200]}
 
@@ -719,123 +793,80 @@ def run_ours(args):
 
 
 def run_reference(args):
-    """Reference arm: the reference's CPU implementation of the path (no Rust
-    toolchain exists here, so its C restatement oracle/, which reproduces the
-    reference's golden vectors) on this box's host cores, same config/metric."""
+    """Reference arm: the reference's CPU implementation of the path on this box's host
+    cores.  No Rust toolchain exists here, so it is the C restatement in oracle/
+    (which reproduces the reference's golden vectors) -- the router, the routed
+    experts and the shared expert of one full layer, on the same seeded weights and
+    inputs as our arm (generated by the same code, on cuda:0 when there is one), per
+    the BASELINE CPU plan: configs[1] and [3] on all tokens, configs[2] on a seeded
+    512-token subset, each expert dequantised once outside the timed region, OpenMP
+    over assignments.  The reference's CPU path has no tensor parallelism, so at any
+    N it computes the whole layer (the TP1 weights)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
+    import torch
 
     import oracle as O
+    from glmaxx_b200 import synth
+    from glmaxx_b200.moe import MoEConfig
 
     wl = WORKLOADS[args.workload]
-    if wl.get("codec") == "hybrid":
+    codec = wl.get("codec")
+    if codec == "hybrid":
         print(json.dumps({"impl": "reference", "metric": wl["metric"], "unavailable":
                           "the CPU arm times the per-codec workloads (decode, prefill, exl3); the "
                           "hybrid stack has no separate CPU arm"}), flush=True)
         return
-    rng = np.random.default_rng(args.seed)
-    T = args.tokens
-    S = min(T, max(1, args.cpu_sample_tokens))
-    Ir = INTER // world
-    # every token costs the same on this path (router + 8 expert rows), so only the
-    # sampled tokens are generated and each step runs router + layer on them
-    x = O.f32_to_bf16_bits(rng.standard_normal((S, HIDDEN)).astype(np.float32))
-    wr = O.f32_to_bf16_bits((rng.standard_normal((EXPERTS, HIDDEN)) * 0.02).astype(np.float32))
-    bias = (rng.standard_normal(EXPERTS) * 0.01).astype(np.float32)
-    if wl["zipf"]:
-        perm = rng.permutation(EXPERTS).astype(np.float32)
-        bias = (bias + REF_ZIPF_BETA * (-1.1 * np.log1p(perm))).astype(np.float32)
-    experts, weights = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
-    used = np.unique(experts)
-    remap = {int(e): i for i, e in enumerate(used)}
-    if wl.get("codec") == "exl3":
-        H, Ir = HIDDEN, INTER // world
-        words = O.exl3_trellis_words(H, Ir, 3)
-        tr = {n: {int(e): O.exl3_xorshift_trellis(args.seed * 1000 + 3 * int(e) + j, words)
-                  for e in used} for j, n in enumerate(("gate", "up", "down"))}
-
-        def signs(n, mag, salt):
-            r = np.random.default_rng(args.seed + salt)
-            return {int(e): np.where(r.random(n) < 0.5, -mag, mag).astype(np.float16)
-                    .view(np.uint16) for e in used}
-        mag = 0.02 / 1.2441
-        sc = {"gate_suh": signs(H, 1.0, 1), "gate_svh": signs(Ir, mag, 2),
-              "up_suh": signs(H, 1.0, 3), "up_svh": signs(Ir, mag, 4),
-              "down_suh": signs(Ir, 1.0, 5), "down_svh": signs(H, mag, 6)}
-        x16 = (x.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
-
-        def step():
-            t0 = time.perf_counter()
-            ex, wt = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
-            exl3_layer_cpu(x16, ex.astype(np.int64), wt, tr, sc, H, Ir)
-            return time.perf_counter() - t0
-        for _ in range(min(args.warmup, 1)):
-            step()
-        times = []
-        t_start = time.perf_counter()
-        while len(times) < args.steps and (not times or
-                                           time.perf_counter() - t_start < REF_TIME_BUDGET_S):
-            times.append(step())
-        per_step = statistics.mean(times)
-        value = S / per_step
-        print(json.dumps({
-            "impl": "reference", "metric": wl["metric"], "value": value, "unit": UNIT,
-            "n_gpus": world, "steps": len(times), "steps_requested": args.steps,
-            "warmup": min(args.warmup, 1), "ms_per_step": per_step * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded trellis words, signs, N(0,1) activations)",
-            "config": {"workload": wl["name"], "tokens": T,
-                       "parallelism": f"tp{world} shard on one host process"},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
-                             "sample": f"{S} tokens of {T} per step ({len(used)} experts), router"
-                                       " + EXL3 gate/up/down with per-call trellis decode"},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}), flush=True)
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "reference", "metric": wl["metric"], "unavailable":
+                          "needs cuda:0 to generate the same seeded weights as our arm (the "
+                          "timed part runs on the host cores)"}), flush=True)
         return
-    v13, s13, g13, v2, s2, g2 = [], [], [], [], [], []
-    for e in used:
-        er = np.random.default_rng(args.seed * 1000 + int(e))
-        p13 = O.pack((er.standard_normal((2 * Ir, HIDDEN)) * 0.02).astype(np.float32))
-        p2 = O.pack((er.standard_normal((HIDDEN, Ir)) * 0.02).astype(np.float32))
-        v13.append(p13.values), s13.append(p13.scales), g13.append(p13.global_scale)
-        v2.append(p2.values), s2.append(p2.scales), g2.append(p2.global_scale)
-    sh13 = O.f32_to_bf16_bits((rng.standard_normal((2 * Ir, HIDDEN)) * 0.02).astype(np.float32))
-    sh2 = O.f32_to_bf16_bits((rng.standard_normal((HIDDEN, Ir)) * 0.02).astype(np.float32))
-    packed = (np.stack(v13), np.stack(s13), np.array(g13, np.float32), np.stack(v2),
-              np.stack(s2), np.array(g2, np.float32), Ir, sh13, sh2)
-
-    def step():
-        t0 = time.perf_counter()
-        ex, wt = O.router(x, wr, bias, 8, 4, TOPK, 2.5)
-        re_m = np.vectorize(lambda e: remap[int(e)])(ex).astype(np.uint16)
-        O.moe_layer(x, re_m, wt, *packed)
-        return time.perf_counter() - t0
+    dev = torch.device("cuda", 0)
+    T = args.tokens
+    cfg = MoEConfig()
+    beta = synth.fit_zipf_beta(cfg, T, args.seed, dev)[0] if wl["zipf"] else None
+    if codec == "exl3":
+        w = synth.make_exl3_rank_weights(cfg, seed=args.seed, device=dev, zipf_beta=beta)
+    else:
+        w = synth.make_rank_weights(cfg, seed=args.seed, device=dev, zipf_beta=beta)
+    x = synth.make_input(T, HIDDEN, seed=args.seed, device=dev)
+    sel = cpu_sample(T, args.workload, args.seed)
+    cl = CpuLayer(w, cfg, codec, host_u16(x)[sel])
 
     # warm-up and timed steps stop early once REF_TIME_BUDGET_S is spent, so that the
     # arm ends within a few minutes whatever K and W are; "steps" reports the count run
-    for _ in range(min(args.warmup, 2)):
-        step()
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        cl.step()
     times = []
     t_start = time.perf_counter()
+    touched = 0
     while len(times) < args.steps and (not times or
                                        time.perf_counter() - t_start < REF_TIME_BUDGET_S):
-        times.append(step())
+        busy, touched, _ = cl.step()
+        times.append(busy)
     per_step = statistics.mean(times)
-    value = S / per_step
+    value = len(sel) / per_step
+    cores = int(O.lib().orc_threads())
+    what = ("router + EXL3 gate/up/down (trellises decoded once per expert) + bf16 shared "
+            "expert" if codec == "exl3" else
+            "router + NVFP4 FC1/SwiGLU/FC2 (experts dequantised once) + bf16 shared expert")
     print(json.dumps({
         "impl": "reference", "metric": wl["metric"], "value": value, "unit": UNIT,
         "n_gpus": world, "steps": len(times), "steps_requested": args.steps,
-        "warmup": min(args.warmup, 2), "ms_per_step": per_step * 1e3,
+        "warmup": warm, "ms_per_step": per_step * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic (seeded, same shapes and distributions)",
+        "data": "synthetic, the same seeded weights and inputs as our arm",
         "config": {"workload": wl["name"], "tokens": T,
-                   "parallelism": f"tp{world} shard on one host process"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": O.threads(), "kind": "port",
-                         "sample": f"{S} tokens of {T} per step ({len(used)} experts), router "
-                                   "+ full layer incl. per-call NVFP4 dequant"},
+                   "parallelism": "whole layer on one host process (the reference CPU path "
+                                  "has no tensor parallelism)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{len(sel)} of {T} tokens per step ({touched} experts): "
+                                   f"{what}; preparation {cl.prep.prep_s:.1f} s untimed, "
+                                   f"experts {'held' if cl.prep.hold else 'rebuilt per step'}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

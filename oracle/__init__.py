@@ -100,11 +100,19 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_router_select": (i32, [vp, u64, u64, vp, u32, u32, u32, f32, vp, vp]),
         "orc_moe_layer": (i32, [u32, u32, u32, u32, u32, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                 vp, vp, u32, vp, u32, vp, vp, i32]),
+        "orc_expert_prepare": (i32, [vp, vp, f32, vp, vp, f32, u32, u32, vp, vp]),
+        "orc_shared_prepare": (i32, [vp, vp, u32, u32, vp, vp]),
+        "orc_moe_expert_h": (i32, [u32, u32, vp, vp, u32, vp, vp, i32]),
+        "orc_moe_expert_rows": (i32, [u32, u32, vp, vp, vp, vp, u32, vp, vp, vp, i32]),
+        "orc_shared_rows": (i32, [u32, u32, vp, vp, u32, vp, vp, vp, i32]),
+        "orc_threads": (i32, []),
         "orc_f32_to_f16_bits": (u16, [f32]),
         "orc_f16_bits_to_f32": (f32, [u16]),
         "orc_exl3_xorshift_trellis": (None, [u64, u64, vp]),
         "orc_exl3_decode_native_at": (u16, [vp, u64, u32, u64, u64]),
         "orc_exl3_reconstruct_native": (None, [vp, u64, u64, u32, vp]),
+        "orc_exl3_prepare": (i32, [vp, u64, u64, u32, vp]),
+        "orc_exl3_project": (i32, [vp, u64, u64, vp, vp, vp, u64, vp, i32]),
         "orc_exl3_matmul_reference": (i32, [vp, u64, u64, u32, vp, vp, vp, u64, vp, i32]),
     }
     for name, (res, args) in sig.items():
@@ -376,6 +384,113 @@ def moe_layer(x_bf16, route_experts, route_weights, w13_values, w13_scales, w13_
     return routed.reshape(nsel, h), shared.reshape(nsel, h)
 
 
+def expert_prepare(w13_values, w13_scales, w13_global, w2_values, w2_scales, w2_global,
+                   hidden, local_inter):
+    """One expert dequantised once (nvfp4.rs:279-301) into k-major fp32 planes:
+    (w13t [H, 2I], w2t [I, H])."""
+    w13t = np.empty((hidden, 2 * local_inter), np.float32)
+    w2t = np.empty((local_inter, hidden), np.float32)
+    a = [np.ascontiguousarray(v) for v in (w13_values, w13_scales, w2_values, w2_scales)]
+    _check(lib().orc_expert_prepare(_p(a[0]), _p(a[1]), float(w13_global), _p(a[2]), _p(a[3]),
+                                    float(w2_global), hidden, local_inter, _p(w13t), _p(w2t)),
+           "expert_prepare")
+    return w13t, w2t
+
+
+def shared_prepare(shared13_bf16, shared2_bf16):
+    """The bf16 shared expert as k-major fp32 planes (s13t [H, 2Is], s2t [Is, H])."""
+    s13 = np.ascontiguousarray(shared13_bf16, np.uint16)
+    s2 = np.ascontiguousarray(shared2_bf16, np.uint16)
+    hidden, inter = s2.shape
+    s13t = np.empty((hidden, 2 * inter), np.float32)
+    s2t = np.empty((inter, hidden), np.float32)
+    _check(lib().orc_shared_prepare(_p(s13), _p(s2), hidden, inter, _p(s13t), _p(s2t)),
+           "shared_prepare")
+    return s13t, s2t
+
+
+def moe_expert_rows(x_bf16, tokens, weights, out_rows, w13t, w2t, out):
+    """Adds one expert's weighted FC1 -> SwiGLU -> FC2 rows into out[out_rows]."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    wt = np.ascontiguousarray(weights, np.float32)
+    rows = np.ascontiguousarray(out_rows, np.uint32)
+    hidden, inter = x.shape[1], w2t.shape[0]
+    assert out.dtype == np.float32 and out.flags.c_contiguous
+    _check(lib().orc_moe_expert_rows(hidden, inter, _p(x), _p(tok), _p(wt), _p(rows), tok.size,
+                                     _p(w13t), _p(w2t), _p(out), threads()), "moe_expert_rows")
+
+
+def moe_expert_h(x_bf16, tokens, w13t):
+    """FC1 + SwiGLU (routed_fc1.rs:84-103) of one expert's rows: h [rows, I],
+    bf16-valued fp32."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    inter = w13t.shape[1] // 2
+    h = np.zeros((tok.size, inter), np.float32)
+    _check(lib().orc_moe_expert_h(x.shape[1], inter, _p(x), _p(tok), tok.size, _p(w13t), _p(h),
+                                  threads()), "moe_expert_h")
+    return h
+
+
+def shared_rows(x_bf16, tokens, s13t, s2t):
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    tok = np.ascontiguousarray(tokens, np.uint32)
+    out = np.zeros((tok.size, x.shape[1]), np.float32)
+    _check(lib().orc_shared_rows(x.shape[1], s2t.shape[0], _p(x), _p(tok), tok.size, _p(s13t),
+                                 _p(s2t), _p(out), threads()), "shared_rows")
+    return out
+
+
+def expert_rows_plan(route_experts, token_subset=None):
+    """Compacted order (routed_fc1.rs:20-58) of the routes of the selected tokens:
+    {expert: (tokens ascending, slots, output rows)} in ascending expert order."""
+    re = np.asarray(route_experts).astype(np.int64)
+    t_all = np.arange(re.shape[0]) if token_subset is None else np.asarray(token_subset, np.int64)
+    out_row = np.arange(t_all.size)
+    tok = np.repeat(t_all, re.shape[1])
+    slot = np.tile(np.arange(re.shape[1]), t_all.size)
+    row = np.repeat(out_row, re.shape[1])
+    exp = re[tok, slot]
+    order = np.lexsort((slot, tok, exp))
+    plan = {}
+    exp, tok, slot, row = exp[order], tok[order], slot[order], row[order]
+    bounds = np.flatnonzero(np.diff(exp)) + 1
+    for a, b in zip(np.r_[0, bounds], np.r_[bounds, exp.size]):
+        if b > a:
+            plan[int(exp[a])] = (tok[a:b], slot[a:b], row[a:b])
+    return plan
+
+
+def moe_layer_prepared(x_bf16, route_experts, route_weights, prepare, local_inter,
+                       shared=None, token_subset=None):
+    """orc_moe_layer, bit for bit, on experts dequantised once: prepare(e) returns
+    expert e's (w13t, w2t) (expert_prepare) and is called once per routed expert in
+    ascending order, outside the timed part; shared is (s13t, s2t) or None.
+    Returns (routed, shared_out, compute seconds excluding prepare)."""
+    import time
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    rw = np.asarray(route_weights, np.float32)
+    hidden = x.shape[1]
+    plan = expert_rows_plan(route_experts, token_subset)
+    nsel = x.shape[0] if token_subset is None else len(token_subset)
+    routed = np.zeros((nsel, hidden), np.float32)
+    busy = 0.0
+    for e in sorted(plan):
+        tok, slot, row = plan[e]
+        w13t, w2t = prepare(e)
+        t0 = time.perf_counter()
+        moe_expert_rows(x, tok, rw[tok, slot], row, w13t, w2t, routed)
+        busy += time.perf_counter() - t0
+    shared_out = np.zeros((nsel, hidden), np.float32)
+    if shared is not None:
+        toks = np.arange(x.shape[0]) if token_subset is None else np.asarray(token_subset)
+        t0 = time.perf_counter()
+        shared_out = shared_rows(x, toks, *shared)
+        busy += time.perf_counter() - t0
+    return routed, shared_out, busy
+
+
 # -------------------------------------------------------------------------- exl3
 def f32_to_f16_bits(x: float) -> int:
     return int(lib().orc_f32_to_f16_bits(x))
@@ -412,3 +527,23 @@ def exl3_matmul_reference(trellis, k, n, suh, svh, activations_f16, bits=3) -> n
     _check(lib().orc_exl3_matmul_reference(_p(tr), k, n, bits, _p(su), _p(sv), _p(a), rows,
                                            _p(out), threads()), "exl3 matmul")
     return out.reshape(rows, n)
+
+
+def exl3_prepare(trellis, k: int, n: int, bits: int = 3) -> np.ndarray:
+    """One trellis decoded once (exl3.rs:490-513) to fp32 [k, n]."""
+    tr = np.ascontiguousarray(trellis, np.uint16)
+    out = np.empty((k, n), np.float32)
+    _check(lib().orc_exl3_prepare(_p(tr), k, n, bits, _p(out)), "exl3_prepare")
+    return out
+
+
+def exl3_project(weights_f32, suh, svh, activations_f16) -> np.ndarray:
+    """matmul_reference_f16 (exl3.rs:404-453) on weights from exl3_prepare: same bits."""
+    k, n = weights_f32.shape
+    x = np.ascontiguousarray(activations_f16, np.uint16).reshape(-1, k)
+    out = np.zeros((x.shape[0], n), np.uint16)
+    _check(lib().orc_exl3_project(_p(weights_f32), k, n, _p(np.ascontiguousarray(suh, np.uint16)),
+                                  _p(np.ascontiguousarray(svh, np.uint16)), _p(x), x.shape[0],
+                                  _p(out), threads()), "exl3_project")
+    return out
+

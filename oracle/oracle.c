@@ -1035,11 +1035,26 @@ void orc_exl3_xorshift_trellis(uint64_t seed, uint64_t words, uint16_t* trellis)
 }
 
 /* exl3.rs:471-477 */
-static uint16_t decode_3inst_f16(uint16_t window) {
+static uint16_t decode_3inst_f16_direct(uint16_t window) {
   const uint32_t value = (uint32_t)window * 0xCBAC1FEDu;
   const uint32_t packed = (value & 0x8FFF8FFFu) ^ 0x3B603B60u;
   return orc_f32_to_f16_bits(orc_f16_bits_to_f32((uint16_t)packed) +
                              orc_f16_bits_to_f32((uint16_t)(packed >> 16)));
+}
+
+/* The decode is a pure function of the 16-bit window: tabulated once. */
+static uint16_t g_3inst_table[65536];
+static int g_3inst_ready = 0;
+
+static uint16_t decode_3inst_f16(uint16_t window) {
+  if (!__atomic_load_n(&g_3inst_ready, __ATOMIC_ACQUIRE)) {
+#pragma omp critical(orc_3inst_table)
+    if (!g_3inst_ready) {
+      for (uint32_t w = 0; w < 65536; ++w) g_3inst_table[w] = decode_3inst_f16_direct((uint16_t)w);
+      __atomic_store_n(&g_3inst_ready, 1, __ATOMIC_RELEASE);
+    }
+  }
+  return g_3inst_table[window];
 }
 
 /* exl3.rs:479-513 */
@@ -1089,48 +1104,356 @@ static void hadamard_128(const float* input, float* output) {
 
 static float f16_round(float v) { return orc_f16_bits_to_f32(orc_f32_to_f16_bits(v)); }
 
-/* exl3.rs:404-453 (Exl3Trellis::matmul_reference_f16). */
-int orc_exl3_matmul_reference(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
-                              const uint16_t* suh, const uint16_t* svh,
-                              const uint16_t* activations, uint64_t rows, uint16_t* output,
-                              int threads) {
+/* Columns per SIMD block of the fast oracle paths below. */
+enum { kPrepCols = 32 };
+
+/* sums of kPrepCols columns [c0, c0 + kPrepCols) over ascending k (defined below). */
+static void dot_block(const float* act, uint64_t k_len, const float* wt, uint64_t ld,
+                      uint64_t c0, float* out);
+
+/* The decoded weights of one trellis (exl3.rs:490-513), converted once to fp32,
+ * [k][n] row-major: the prepared form of an EXL3 projection. */
+int orc_exl3_prepare(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
+                     float* nativef) {
+  if (k % 128 != 0 || n % 128 != 0) return ORC_ERR_SHAPE;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < (int64_t)k; ++r)
+    for (uint64_t c = 0; c < n; ++c)
+      nativef[(uint64_t)r * n + c] =
+          orc_f16_bits_to_f32(orc_exl3_decode_native_at(trellis, n, bits, (uint64_t)r, c));
+  return ORC_OK;
+}
+
+/* exl3.rs:404-453 (Exl3Trellis::matmul_reference_f16) on prepared weights.
+ * Arithmetic per output column is the reference's: an fp32 sum over ascending k
+ * of source[k] * w[k][c] (each product and add rounded once), rounded to fp16.
+ * For speed all rows' rotated sources are built first and 32 adjacent columns
+ * advance together in SIMD lanes. */
+int orc_exl3_project(const float* nativef, uint64_t k, uint64_t n, const uint16_t* suh,
+                     const uint16_t* svh, const uint16_t* activations, uint64_t rows,
+                     uint16_t* output, int threads) {
 #ifdef _OPENMP
   if (threads > 0) omp_set_num_threads(threads);
 #else
   (void)threads;
 #endif
   if (k % 128 != 0 || n % 128 != 0) return ORC_ERR_SHAPE;
-  uint16_t* native = malloc(sizeof(uint16_t) * k * n);
-  float* nativef = malloc(sizeof(float) * k * n);
-  if (!native || !nativef) {
-    free(native), free(nativef);
+  if (rows == 0) return ORC_OK;
+  float* source = malloc(sizeof(float) * k * rows);
+  float* projected = malloc(sizeof(float) * n * rows);
+  if (!source || !projected) {
+    free(source), free(projected);
     return ORC_ERR_ALLOC;
   }
-  orc_exl3_reconstruct_native(trellis, k, n, bits, native);
-  for (uint64_t i = 0; i < k * n; ++i) nativef[i] = orc_f16_bits_to_f32(native[i]);
-  float* source = malloc(sizeof(float) * k);
-  float* projected = malloc(sizeof(float) * n);
-  float tmp[128];
-  for (uint64_t r = 0; r < rows; ++r) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < (int64_t)rows; ++r) {
+    float tmp[128];
+    float* src = source + (uint64_t)r * k;
     for (uint64_t i = 0; i < k; ++i)
-      source[i] = f16_round(orc_f16_bits_to_f32(activations[r * k + i]) * orc_f16_bits_to_f32(suh[i]));
+      src[i] = f16_round(orc_f16_bits_to_f32(activations[(uint64_t)r * k + i]) *
+                         orc_f16_bits_to_f32(suh[i]));
     for (uint64_t b = 0; b < k; b += 128) {
-      hadamard_128(source + b, tmp);
-      for (int i = 0; i < 128; ++i) source[b + i] = f16_round(tmp[i]);
+      hadamard_128(src + b, tmp);
+      for (int i = 0; i < 128; ++i) src[b + i] = f16_round(tmp[i]);
+    }
+  }
+  const int64_t tiles = (int64_t)(n / kPrepCols);
+#pragma omp parallel for schedule(static) collapse(2)
+  for (int64_t r = 0; r < (int64_t)rows; ++r)
+    for (int64_t j = 0; j < tiles; ++j) {
+      float acc[kPrepCols];
+      const uint64_t c0 = (uint64_t)j * kPrepCols;
+      dot_block(source + (uint64_t)r * k, k, nativef, n, c0, acc);
+      for (int c = 0; c < kPrepCols; ++c) projected[(uint64_t)r * n + c0 + c] = f16_round(acc[c]);
     }
 #pragma omp parallel for schedule(static)
-    for (int64_t c = 0; c < (int64_t)n; ++c) {
-      float acc = 0.0f;
-      for (uint64_t i = 0; i < k; ++i) acc += source[i] * nativef[i * n + (uint64_t)c];
-      projected[c] = f16_round(acc);
-    }
+  for (int64_t r = 0; r < (int64_t)rows; ++r) {
+    float tmp[128];
+    float* pr = projected + (uint64_t)r * n;
     for (uint64_t b = 0; b < n; b += 128) {
-      hadamard_128(projected + b, tmp);
-      for (int i = 0; i < 128; ++i)
-        projected[b + i] = f16_round(tmp[i] * orc_f16_bits_to_f32(svh[b + i]));
+      hadamard_128(pr + b, tmp);
+      for (int i = 0; i < 128; ++i) pr[b + i] = f16_round(tmp[i] * orc_f16_bits_to_f32(svh[b + i]));
     }
-    for (uint64_t c = 0; c < n; ++c) output[r * n + c] = orc_f32_to_f16_bits(projected[c]);
+    for (uint64_t c = 0; c < n; ++c) output[(uint64_t)r * n + c] = orc_f32_to_f16_bits(pr[c]);
   }
-  free(native), free(nativef), free(source), free(projected);
+  free(source), free(projected);
   return ORC_OK;
 }
+
+/* exl3.rs:404-453 (Exl3Trellis::matmul_reference_f16): decode, then project. */
+int orc_exl3_matmul_reference(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
+                              const uint16_t* suh, const uint16_t* svh,
+                              const uint16_t* activations, uint64_t rows, uint16_t* output,
+                              int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#endif
+  if (k % 128 != 0 || n % 128 != 0) return ORC_ERR_SHAPE;
+  float* nativef = malloc(sizeof(float) * k * n);
+  if (!nativef) return ORC_ERR_ALLOC;
+  int status = orc_exl3_prepare(trellis, k, n, bits, nativef);
+  if (status == ORC_OK)
+    status = orc_exl3_project(nativef, k, n, suh, svh, activations, rows, output, threads);
+  free(nativef);
+  return status;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Prepared-expert form of orc_moe_layer: the same arithmetic bit for bit,     */
+/* arranged for speed as the CPU-baseline plan asks (each expert dequantised    */
+/* once, OpenMP over assignments, SIMD across output columns).  Each expert's   */
+/* weights are dequantised (nvfp4.rs:279-301) into k-major fp32 planes, so a    */
+/* block of output columns keeps one running sum per column in SIMD lanes while */
+/* k ascends: every column is still the sequential sum of routed_fc1.rs:84-103  */
+/* and routed_fc2.rs:60-86, each product and each add rounded once.            */
+/* ------------------------------------------------------------------------- */
+
+
+static int omp_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* Transpose src [n][k] into dst [k][ld] (blocked). */
+static void transpose_into(const float* src, uint64_t n, uint64_t k, float* dst, uint64_t ld) {
+#pragma omp parallel for schedule(static) collapse(2)
+  for (int64_t nb = 0; nb < (int64_t)((n + 31) / 32); ++nb)
+    for (int64_t kb = 0; kb < (int64_t)((k + 31) / 32); ++kb)
+      for (uint64_t r = (uint64_t)nb * 32; r < n && r < (uint64_t)nb * 32 + 32; ++r)
+        for (uint64_t c = (uint64_t)kb * 32; c < k && c < (uint64_t)kb * 32 + 32; ++c)
+          dst[c * ld + r] = src[r * k + c];
+}
+
+/* PackedNvfp4::dequantize (nvfp4.rs:279-301, (e2m1 * e4m3) * global, that
+ * product order) of an [n][k] tensor written k-major into dst [k][n]: the 16
+ * values of a scale block come from a 16-entry table built with the same two
+ * products, so every weight is the same float as orc_nvfp4_dequantize's. */
+static void dequantize_transposed(const uint8_t* values, const uint8_t* scales,
+                                  float global_scale, uint64_t n, uint64_t k, float* dst) {
+  const uint64_t padded_n = align_up(n, 128), padded_k = align_up(k, 64);
+#pragma omp parallel for schedule(static) collapse(2)
+  for (int64_t nb = 0; nb < (int64_t)(n / 64); ++nb)
+    for (int64_t kb = 0; kb < (int64_t)(k / 64); ++kb) {
+      float tile[64][65];
+      for (uint64_t r = 0; r < 64; ++r) {
+        const uint64_t row = (uint64_t)nb * 64 + r;
+        for (uint64_t g = 0; g < 4; ++g) {
+          const uint64_t col0 = (uint64_t)kb * 64 + g * 16;
+          const float dec = orc_decode_e4m3(
+              scales[orc_scale_offset(row, col0 / 16, padded_n, padded_k)]);
+          float lut[16];
+          for (int c = 0; c < 16; ++c) lut[c] = orc_decode_e2m1((uint8_t)c) * dec * global_scale;
+          const uint8_t* v = values + (row * padded_k + col0) / 2;
+          for (int j = 0; j < 8; ++j) {
+            tile[r][g * 16 + 2 * j] = lut[v[j] & 0x0f];
+            tile[r][g * 16 + 2 * j + 1] = lut[v[j] >> 4];
+          }
+        }
+      }
+      for (uint64_t c = 0; c < 64; ++c)
+        for (uint64_t r = 0; r < 64; ++r)
+          dst[((uint64_t)kb * 64 + c) * n + (uint64_t)nb * 64 + r] = tile[r][c];
+    }
+}
+
+int orc_expert_prepare(const uint8_t* w13_values, const uint8_t* w13_scales, float w13_global,
+                       const uint8_t* w2_values, const uint8_t* w2_scales, float w2_global,
+                       uint32_t hidden, uint32_t local_inter, float* w13t, float* w2t) {
+  const uint64_t H = hidden, I = local_inter, N13 = 2ull * I;
+  if (I % 64 != 0 || H % 64 != 0) return ORC_ERR_SHAPE;
+  dequantize_transposed(w13_values, w13_scales, w13_global, N13, H, w13t);
+  dequantize_transposed(w2_values, w2_scales, w2_global, H, I, w2t);
+  return ORC_OK;
+}
+
+int orc_shared_prepare(const uint16_t* shared13_bf16, const uint16_t* shared2_bf16,
+                       uint32_t hidden, uint32_t shared_inter, float* s13t, float* s2t) {
+  const uint64_t H = hidden, IS = shared_inter, N13 = 2ull * IS;
+  if (IS % kPrepCols != 0 || H % kPrepCols != 0) return ORC_ERR_SHAPE;
+  float* tmp = malloc(sizeof(float) * N13 * H);
+  if (!tmp) return ORC_ERR_ALLOC;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)(N13 * H); ++i) tmp[i] = bf16_bits_to_f32(shared13_bf16[i]);
+  transpose_into(tmp, N13, H, s13t, N13);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)(H * IS); ++i) tmp[i] = bf16_bits_to_f32(shared2_bf16[i]);
+  transpose_into(tmp, H, IS, s2t, H);
+  free(tmp);
+  return ORC_OK;
+}
+
+/* gate/up sums of kPrepCols columns [c0, c0 + kPrepCols) over ascending k. */
+__attribute__((target_clones("avx512f", "avx2", "default")))
+static void dual_dot_block(const float* act, uint64_t k_len, const float* wt, uint64_t ld,
+                           uint64_t c0, uint64_t up_off, float* gate, float* up) {
+  float g[kPrepCols], u[kPrepCols];
+  for (int c = 0; c < kPrepCols; ++c) g[c] = 0.0f, u[c] = 0.0f;
+  for (uint64_t k = 0; k < k_len; ++k) {
+    const float a = act[k];
+    const float* wk = wt + k * ld + c0;
+    for (int c = 0; c < kPrepCols; ++c) g[c] = g[c] + a * wk[c];
+    for (int c = 0; c < kPrepCols; ++c) u[c] = u[c] + a * wk[up_off + c];
+  }
+  for (int c = 0; c < kPrepCols; ++c) gate[c] = g[c], up[c] = u[c];
+}
+
+/* sums of kPrepCols columns [c0, c0 + kPrepCols) over ascending k. */
+__attribute__((target_clones("avx512f", "avx2", "default")))
+static void dot_block(const float* act, uint64_t k_len, const float* wt, uint64_t ld,
+                      uint64_t c0, float* out) {
+  float s[kPrepCols];
+  for (int c = 0; c < kPrepCols; ++c) s[c] = 0.0f;
+  for (uint64_t k = 0; k < k_len; ++k) {
+    const float a = act[k];
+    const float* wk = wt + k * ld + c0;
+    for (int c = 0; c < kPrepCols; ++c) s[c] = s[c] + a * wk[c];
+  }
+  for (int c = 0; c < kPrepCols; ++c) out[c] = s[c];
+}
+
+/* FC1 + SwiGLU of one expert's assignments (routed_fc1.rs:84-103): row i is
+ * token tokens[i]; h [rows][I] receives bf16_round(silu(gate) * up). */
+int orc_moe_expert_h(uint32_t hidden, uint32_t local_inter, const uint16_t* x_bf16,
+                     const uint32_t* tokens, uint32_t rows, const float* w13t, float* h,
+                     int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#else
+  (void)threads;
+#endif
+  const uint64_t H = hidden, I = local_inter, N13 = 2ull * I;
+  if (rows == 0) return ORC_OK;
+  if (I % kPrepCols != 0 || H % kPrepCols != 0) return ORC_ERR_SHAPE;
+  float* act = malloc(sizeof(float) * rows * H);
+  if (!act) return ORC_ERR_ALLOC;
+  int status = ORC_OK;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)rows; ++i) {
+    float* ar = act + (uint64_t)i * H;
+    float* row = malloc(sizeof(float) * H);
+    int st = row ? ORC_OK : ORC_ERR_ALLOC;
+    if (st == ORC_OK) {
+      for (uint64_t k = 0; k < H; ++k)
+        row[k] = orc_bf16_round(bf16_bits_to_f32(x_bf16[(uint64_t)tokens[i] * H + k]));
+      st = nvfp4_row_roundtrip(row, H, ar);
+    }
+    free(row);
+    if (st != ORC_OK) {
+#pragma omp critical
+      status = st;
+    }
+  }
+  if (status == ORC_OK) {
+    const int64_t tiles = (int64_t)(I / kPrepCols);
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+    for (int64_t i = 0; i < (int64_t)rows; ++i)
+      for (int64_t j = 0; j < tiles; ++j) {
+        float gate[kPrepCols], up[kPrepCols];
+        const uint64_t c0 = (uint64_t)j * kPrepCols;
+        dual_dot_block(act + (uint64_t)i * H, H, w13t, N13, c0, I, gate, up);
+        for (int c = 0; c < kPrepCols; ++c)
+          h[(uint64_t)i * I + c0 + c] = orc_bf16_round(silu(gate[c]) * up[c]);
+      }
+  }
+  free(act);
+  return status;
+}
+
+/* One expert's assignments (routed_fc1.rs:84-103 then routed_fc2.rs:60-86):
+ * row i is token tokens[i] with routing weight weights[i]; its weighted FC2
+ * output is added to out + out_rows[i] * hidden.  Tokens are distinct within an
+ * expert, so rows write disjoint outputs; calling this per expert in ascending
+ * order keeps the reference's compacted accumulation order. */
+int orc_moe_expert_rows(uint32_t hidden, uint32_t local_inter, const uint16_t* x_bf16,
+                        const uint32_t* tokens, const float* weights, const uint32_t* out_rows,
+                        uint32_t rows, const float* w13t, const float* w2t, float* out,
+                        int threads) {
+  const uint64_t H = hidden, I = local_inter;
+  if (rows == 0) return ORC_OK;
+  float* h = malloc(sizeof(float) * rows * I);
+  float* src = malloc(sizeof(float) * rows * I);
+  if (!h || !src) {
+    free(h), free(src);
+    return ORC_ERR_ALLOC;
+  }
+  int status = orc_moe_expert_h(hidden, local_inter, x_bf16, tokens, rows, w13t, h, threads);
+  if (status != ORC_OK) goto done;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)rows; ++i) {
+    const int st = nvfp4_row_roundtrip(h + (uint64_t)i * I, I, src + (uint64_t)i * I);
+    if (st != ORC_OK) {
+#pragma omp critical
+      status = st;
+    }
+  }
+  if (status != ORC_OK) goto done;
+  {
+    const int64_t tiles = (int64_t)(H / kPrepCols);
+#pragma omp parallel for schedule(dynamic, 4) collapse(2)
+    for (int64_t i = 0; i < (int64_t)rows; ++i)
+      for (int64_t j = 0; j < tiles; ++j) {
+        float acc[kPrepCols];
+        const uint64_t c0 = (uint64_t)j * kPrepCols;
+        dot_block(src + (uint64_t)i * I, I, w2t, H, c0, acc);
+        float* o = out + (uint64_t)out_rows[i] * H + c0;
+        const float weight = weights[i];
+        for (int c = 0; c < kPrepCols; ++c) o[c] += weight * acc[c];
+      }
+  }
+done:
+  free(h), free(src);
+  return status;
+}
+
+/* The bf16 shared expert of orc_moe_layer on prepared planes: shared_out row i
+ * (token tokens[i]) = down(bf16_round(silu(gate) * up)), sequential-k sums. */
+int orc_shared_rows(uint32_t hidden, uint32_t shared_inter, const uint16_t* x_bf16,
+                    const uint32_t* tokens, uint32_t rows, const float* s13t, const float* s2t,
+                    float* shared_out, int threads) {
+#ifdef _OPENMP
+  if (threads > 0) omp_set_num_threads(threads);
+#else
+  (void)threads;
+#endif
+  const uint64_t H = hidden, IS = shared_inter, N13 = 2ull * IS;
+  if (rows == 0) return ORC_OK;
+  if (IS % kPrepCols != 0 || H % kPrepCols != 0) return ORC_ERR_SHAPE;
+  float* xs = malloc(sizeof(float) * rows * H);
+  float* h = malloc(sizeof(float) * rows * IS);
+  if (!xs || !h) {
+    free(xs), free(h);
+    return ORC_ERR_ALLOC;
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < (int64_t)rows; ++i)
+    for (uint64_t k = 0; k < H; ++k)
+      xs[(uint64_t)i * H + k] = bf16_bits_to_f32(x_bf16[(uint64_t)tokens[i] * H + k]);
+  {
+    const int64_t tiles = (int64_t)(IS / kPrepCols);
+#pragma omp parallel for schedule(dynamic, 1) collapse(2)
+    for (int64_t i = 0; i < (int64_t)rows; ++i)
+      for (int64_t j = 0; j < tiles; ++j) {
+        float gate[kPrepCols], up[kPrepCols];
+        const uint64_t c0 = (uint64_t)j * kPrepCols;
+        dual_dot_block(xs + (uint64_t)i * H, H, s13t, N13, c0, IS, gate, up);
+        for (int c = 0; c < kPrepCols; ++c)
+          h[(uint64_t)i * IS + c0 + c] = orc_bf16_round(silu(gate[c]) * up[c]);
+      }
+  }
+  {
+    const int64_t tiles = (int64_t)(H / kPrepCols);
+#pragma omp parallel for schedule(dynamic, 4) collapse(2)
+    for (int64_t i = 0; i < (int64_t)rows; ++i)
+      for (int64_t j = 0; j < tiles; ++j) {
+        const uint64_t c0 = (uint64_t)j * kPrepCols;
+        dot_block(h + (uint64_t)i * IS, IS, s2t, H, c0, shared_out + (uint64_t)i * H + c0);
+      }
+  }
+  free(xs), free(h);
+  return ORC_OK;
+}
+
+int orc_threads(void) { return omp_threads(); }

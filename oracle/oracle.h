@@ -105,6 +105,28 @@ int orc_moe_layer(uint32_t tokens, uint32_t hidden, uint32_t experts, uint32_t l
                   uint32_t shared_inter, const uint32_t* token_subset, uint32_t subset_count,
                   float* routed_out, float* shared_out, int threads);
 
+/* Prepared-expert form of orc_moe_layer (same bits): an expert's weights
+ * dequantised once into k-major fp32 planes (w13t [H][2I], w2t [I][H]; shared
+ * s13t [H][2Is], s2t [Is][H]), then its assignments in parallel with SIMD
+ * across output columns.  Calling orc_moe_expert_rows per expert in ascending
+ * order reproduces the compacted accumulation order of orc_moe_layer. */
+int orc_expert_prepare(const uint8_t* w13_values, const uint8_t* w13_scales, float w13_global,
+                       const uint8_t* w2_values, const uint8_t* w2_scales, float w2_global,
+                       uint32_t hidden, uint32_t local_inter, float* w13t, float* w2t);
+int orc_shared_prepare(const uint16_t* shared13_bf16, const uint16_t* shared2_bf16,
+                       uint32_t hidden, uint32_t shared_inter, float* s13t, float* s2t);
+int orc_moe_expert_h(uint32_t hidden, uint32_t local_inter, const uint16_t* x_bf16,
+                     const uint32_t* tokens, uint32_t rows, const float* w13t, float* h,
+                     int threads);
+int orc_moe_expert_rows(uint32_t hidden, uint32_t local_inter, const uint16_t* x_bf16,
+                        const uint32_t* tokens, const float* weights, const uint32_t* out_rows,
+                        uint32_t rows, const float* w13t, const float* w2t, float* out,
+                        int threads);
+int orc_shared_rows(uint32_t hidden, uint32_t shared_inter, const uint16_t* x_bf16,
+                    const uint32_t* tokens, uint32_t rows, const float* s13t, const float* s2t,
+                    float* shared_out, int threads);
+int orc_threads(void);
+
 /* crates/glm-format/src/exl3.rs */
 uint16_t orc_f32_to_f16_bits(float value);
 float orc_f16_bits_to_f32(uint16_t bits);
@@ -113,6 +135,11 @@ uint16_t orc_exl3_decode_native_at(const uint16_t* trellis, uint64_t logical_n, 
                                    uint64_t row, uint64_t column);
 void orc_exl3_reconstruct_native(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
                                  uint16_t* output);
+int orc_exl3_prepare(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
+                     float* nativef);
+int orc_exl3_project(const float* nativef, uint64_t k, uint64_t n, const uint16_t* suh,
+                     const uint16_t* svh, const uint16_t* activations, uint64_t rows,
+                     uint16_t* output, int threads);
 int orc_exl3_matmul_reference(const uint16_t* trellis, uint64_t k, uint64_t n, uint32_t bits,
                               const uint16_t* suh, const uint16_t* svh,
                               const uint16_t* activations, uint64_t rows, uint16_t* output,
