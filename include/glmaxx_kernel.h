@@ -608,6 +608,20 @@ int32_t glmaxx_nvfp4_pack_launch(uint64_t src, int32_t src_is_bf16, uint32_t bat
                                  uint64_t scratch, uint64_t validation_error_u32,
                                  void* cuda_stream);
 
+/* Measurement entry point (no reference counterpart: the reference publishes no
+ * NVFP4 tensor peak).  `ctas` CTAs (one per SM) each issue `iters` x 4 (x2 when
+ * dual) back-to-back tcgen05 block-scaled NVFP4 MMAs, M = 128, N = n (128 or
+ * 256; dual needs 128), K = 64, on operands resident in shared memory and scales
+ * resident in TMEM, with copies_per_kblock tcgen05.cp scale copies before each
+ * K-block's MMAs (copy_kind 1: 32x128b.warpx4, 512 bytes; 2: 128x256b, 4 KB;
+ * 0: none).  FLOPs per launch = ctas * iters * 4 * (dual ? 2 : 1) * 2*128*n*64.
+ * iters <= 200000.  cycles_u64 (optional, [ctas]) receives each CTA's %clock64
+ * span of its MMA loop; status_u32 receives GLMAXX_STATUS bits. */
+int32_t glmaxx_nvfp4_mma_peak_launch(uint32_t n, uint32_t dual, uint32_t copy_kind,
+                                     uint32_t copies_per_kblock, uint32_t iters, uint32_t ctas,
+                                     uint32_t* status_u32, unsigned long long* cycles_u64,
+                                     void* cuda_stream);
+
 #if defined(__cplusplus)
 }
 
