@@ -4,7 +4,7 @@
 // Some callers cannot hand the library scratch memory: an engine whose HBM is
 // carved up front into a fixed arena with no room left for per-call workspace,
 // or code that runs while the device must not allocate (cudaMalloc/cudaFree may
-// synchronise the device and are not allowed during stream capture).  For them
+// synchronise the device).  For them
 // the router's scratch (partial logits, token-in-expert bitmap, word prefixes,
 // counts) lives in one file-scope device array of kRouterStaticScratchBytes,
 // which every GPU that loads this library holds until the process exits.
@@ -15,10 +15,13 @@
 //    caller's, as usual.
 //  - Shapes whose scratch would exceed the array are rejected with
 //    GLMAXX_ERR_DESCRIPTOR (the limit is GLMAXX_ROUTER_STATIC_SCRATCH_BYTES;
-//    glmaxx_router_workspace_bytes() gives a shape's need).
+//    glmaxx_router_workspace_bytes() gives a shape's need: 256 experts at top-8
+//    fit up to T = 507, 4,190,208 bytes; T = 508 needs 4,198,400).
 //  - The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress with that device current).  Make that first call
-//    outside any stream capture.
+//    (cudaGetSymbolAddress with that device current) and caches it for the
+//    life of the process; cudaDeviceReset, which would reload the module at a
+//    possibly different address, is not supported.  Make that first call before
+//    any stream capture.
 //  - All calls on a device share the one array and leave their scratch in it.
 //    Everything that must start at zero is cleared by the call itself (the
 //    bitmap by the logits kernel, the status word by a memset).  Two calls whose

@@ -533,15 +533,17 @@ int32_t glmaxx_router_compact_launch(const struct glmaxx_router_descriptor* desc
 /* Allocation-free variant of glmaxx_router_compact_launch (no counterpart in the
  * reference library).  For callers that cannot provide or allocate scratch
  * memory -- an engine whose HBM is planned up front with no per-call
- * workspace, or code running under stream capture where cudaMalloc is not
- * allowed -- the router's scratch lives in a device array of
+ * workspace, or code that must not call cudaMalloc (it can synchronise the
+ * device) -- the router's scratch lives in a device array of
  * GLMAXX_ROUTER_STATIC_SCRATCH_BYTES inside this library, held by every GPU
  * that loads it until exit.  The descriptor's workspace fields are ignored;
  * inputs and outputs are the caller's.  Shapes needing more scratch than the
- * array (glmaxx_router_workspace_bytes) return GLMAXX_ERR_DESCRIPTOR.  The
- * first call on a device looks up the array's address and should be made
- * outside stream capture.  All calls share the array: calls whose GPU work
- * overlaps race and must be serialised by the caller. */
+ * array (glmaxx_router_workspace_bytes > 4 MiB; with 256 experts and top-8
+ * that is T > 507) return GLMAXX_ERR_DESCRIPTOR.  The first call on a device
+ * looks up the array's address (cached for the process; cudaDeviceReset is not
+ * supported) and should be made before any stream capture.  All calls share
+ * the array: calls whose GPU work overlaps race and must be serialised by the
+ * caller. */
 #define GLMAXX_ROUTER_STATIC_SCRATCH_BYTES (4ull << 20)
 int32_t glmaxx_router_compact_launch_static(const struct glmaxx_router_descriptor* descriptor,
                                             void* cuda_stream, int32_t* asynchronous_error);

@@ -1,8 +1,8 @@
 """The allocation-free router entry point (glmaxx_router_compact_launch_static).
 
 Callers that cannot allocate -- an engine with a fixed up-front HBM plan, or code
-under stream capture where cudaMalloc is not allowed -- use this variant, whose
-scratch is a device array inside the library.  This file sorts last so that a
+that must not call cudaMalloc (it can synchronise the device) -- use this
+variant, whose scratch is a device array inside the library.  This file sorts last so that a
 run stopping at its first failure has already run every other test; it also
 passes alone in a fresh process.
 """
@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from glmaxx_b200 import abi
 
 pytestmark = pytest.mark.gpu
@@ -59,11 +60,19 @@ def _launch(fn, T, x, w, b, o, ws=None):
     return status
 
 
+def _bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
 def test_static_router_matches_workspace_router_twice():
+    """Calls in a row on different shapes: T=64 and T=200 take the small-T logits
+    kernel, T=507 (the largest shape whose scratch fits) the tiled one.  Every
+    output equals the workspace router's, and the routes equal the oracle
+    router's bits."""
     assert torch.cuda.is_available()
     dev = torch.device("cuda:0")
     L = abi.load()
-    for T, seed in [(64, 1), (200, 2)]:  # two calls in a row, different shapes
+    for T, seed in [(64, 1), (200, 2), (507, 4)]:
         x, w, b = _bufs(T, seed)
         ref = _outputs(T, dev)
         ws = torch.empty(int(L.glmaxx_router_workspace_bytes(T, H, E, K)), dtype=torch.uint8,
@@ -75,13 +84,19 @@ def test_static_router_matches_workspace_router_twice():
         assert int(got["st"].item()) == 0
         for k in ref:
             assert torch.equal(got[k], ref[k]), k
+        ref_e, ref_w = O.router(_bits(x), _bits(w), b.cpu().numpy(), 8, 4, K, 2.5)
+        assert np.array_equal(_bits(got["re"]), ref_e)
+        assert np.array_equal(got["rw"].cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
 
 
 def test_static_router_rejects_shapes_beyond_its_scratch():
     L = abi.load()
     dev = torch.device("cuda:0")
-    T = 4096  # 8 * T * E * 4 bytes of partial logits alone exceed the array
+    T = 508  # the first token count whose scratch exceeds the array (T = 507 fits)
     assert int(L.glmaxx_router_workspace_bytes(T, H, E, K)) > abi.ROUTER_STATIC_SCRATCH_BYTES
-    x, w, b = _bufs(8, 3)
-    o = _outputs(8, dev)
+    assert int(L.glmaxx_router_workspace_bytes(T - 1, H, E, K)) <= abi.ROUTER_STATIC_SCRATCH_BYTES
+    x, w, b = _bufs(T, 3)
+    o = _outputs(T, dev)
     assert _launch(L.glmaxx_router_compact_launch_static, T, x, w, b, o) == -2  # GLMAXX_ERR_DESCRIPTOR
+    torch.cuda.synchronize()
+    assert int(o["st"].item()) == -1  # nothing ran: the status word is untouched
