@@ -807,6 +807,23 @@ int32_t glmaxx_ipc_close(uint64_t pointer) {
   if (pointer == 0) return GLMAXX_ERR_NULL;
   return int32_t(cudaIpcCloseMemHandle(reinterpret_cast<void*>(pointer)));
 }
+int32_t glmaxx_peer_enable(int32_t peer_device) {
+  int dev = -1, count = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st == cudaSuccess) st = cudaGetDeviceCount(&count);
+  if (st != cudaSuccess) return int32_t(st);
+  if (peer_device < 0 || peer_device >= count || peer_device == dev) return GLMAXX_ERR_DESCRIPTOR;
+  int can = 0;
+  st = cudaDeviceCanAccessPeer(&can, dev, peer_device);
+  if (st != cudaSuccess) return int32_t(st);
+  if (!can) return int32_t(cudaErrorPeerAccessUnsupported);
+  st = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (st == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();  // clear the error state the repeated enable left behind
+    st = cudaSuccess;
+  }
+  return int32_t(st);
+}
 int32_t glmaxx_pinned_alloc(uint64_t bytes, uint64_t* pointer) {
   if (bytes == 0 || pointer == nullptr) return GLMAXX_ERR_NULL;
   void* p = nullptr;

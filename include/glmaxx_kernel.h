@@ -564,6 +564,11 @@ int32_t glmaxx_moe_finish_peer_launch(const struct glmaxx_moe_finish_descriptor*
 int32_t glmaxx_ipc_handle(uint64_t pointer, uint8_t handle[64]);
 int32_t glmaxx_ipc_open(const uint8_t handle[64], uint64_t* pointer);
 int32_t glmaxx_ipc_close(uint64_t pointer);
+/* One process driving several GPUs (a thread per rank): lets the current device
+ * read and write peer_device's memory directly (cudaDeviceEnablePeerAccess; a
+ * repeat call succeeds).  Returns GLMAXX_ERR_DESCRIPTOR for the current device or
+ * an index out of range, cudaErrorPeerAccessUnsupported without a peer path. */
+int32_t glmaxx_peer_enable(int32_t peer_device);
 
 /* Profiling (the CUDA-event timing of the reference, crates/glm-cuda/src/
  * ffi.rs:3057-3079, per stage): while set, layer launches on the calling
