@@ -92,7 +92,7 @@ def parse():
     p.add_argument("--rank-files", type=int, choices=[1, 4], default=1)
     a = p.parse_args()
     if a.tokens is None:
-        a.tokens = WORKLOADS[a.workload]["tokens"]
+        a.tokens = WORKLOADS.get(a.workload, {"tokens": 0})["tokens"]
     return a
 
 
@@ -116,8 +116,11 @@ def measured_peaks():
 # rates give the measured NVFP4 peak; the others price the scale-factor copies
 # of the grouped GEMMs (dual 128 + 6 atom copies per 4 K-blocks is the decode
 # pattern, dual 128 + 1.5 lane-major copies per K-block the prefill pattern).
+# copy kind | 4 issues a stage's 4 K-blocks' copies together before its first MMA.
 NVFP4_PEAK_CASES = [(256, 0, 0, 0), (128, 0, 0, 0), (128, 1, 0, 0), (128, 1, 1, 3),
-                    (128, 1, 2, 1), (128, 1, 2, 2), (256, 0, 1, 3), (256, 0, 2, 1)]
+                    (128, 1, 2, 1), (128, 1, 2, 2), (256, 0, 1, 3), (256, 0, 2, 1),
+                    (256, 0, 2, 2), (128, 0, 2, 1), (128, 0, 1, 2), (128, 1, 6, 1),
+                    (256, 0, 6, 1), (256, 0, 6, 2), (256, 0, 5, 3)]
 
 
 def nvfp4_mma_peak(dev, iters: int = 20000, reps: int = 5):

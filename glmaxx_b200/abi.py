@@ -239,6 +239,7 @@ SIGNATURES = {
     "glmaxx_moe_layer_set_stage_events": (ctypes.c_int32, [_U64P, u32]),
     "glmaxx_moe_layer_plane": (ctypes.c_int32, [_P, u32, _U64P, _U64P]),
     "glmaxx_peer_enable": (ctypes.c_int32, [ctypes.c_int32]),
+    "glmaxx_nvfp4_codec_selfcheck_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_nvfp4_mma_peak_launch": (ctypes.c_int32, [u32, u32, u32, u32, u32, u32, _P, _P, _P]),
     "glmaxx_nvfp4_pack_launch": (ctypes.c_int32, [u64, ctypes.c_int32, u32, u32, u32, u64, u64,
                                                   u64, u64, u64, u64, _P]),

@@ -360,29 +360,58 @@ __device__ __forceinline__ float e4m3_decode(uint32_t code) {
   return (code & 0x80) ? -mag : mag;
 }
 
+// Hardware conversions with the reference codec's rounding (round to nearest,
+// ties to the even code, saturating): cvt.rn.satfinite.e2m1x2.f32 packs two
+// E2M1 codes (first operand in the high nibble); cvt.rn.satfinite.e4m3x2.f32
+// two E4M3 codes.  For finite inputs they give the codes of e2m1_encode /
+// e4m3_encode_pos (the restatement of float.rs:15-73) -- checked over every fp32
+// bit pattern by glmaxx_nvfp4_codec_selfcheck_launch (tests/test_gpu_codec.py).
+__device__ __forceinline__ uint32_t e2m1x8_cvt(const float (&q)[8]) {
+  uint32_t out;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(out)
+      : "f"(q[0]), "f"(q[1]), "f"(q[2]), "f"(q[3]), "f"(q[4]), "f"(q[5]), "f"(q[6]), "f"(q[7]));
+  return out;
+}
+__device__ __forceinline__ uint32_t e2m1_cvt(float q) {
+  uint16_t out;
+  asm("{\n\t.reg .b8 b0;\n\tcvt.rn.satfinite.e2m1x2.f32 b0, %1, %1;\n\t"
+      "mov.b16 %0, {b0, b0};\n\t}"
+      : "=h"(out)
+      : "f"(q));
+  return out & 0xfu;
+}
+__device__ __forceinline__ uint32_t e4m3_cvt_pos(float v) {
+  uint16_t out;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(out) : "f"(v));
+  return out & 0xffu;
+}
+
 // Quantise one 16-element block (nvfp4.rs:567-608): scale code from the block
 // amax, then each value divided by decode(scale) * global.  Returns the scale
-// code; writes the 16 codes as 8 bytes (even element in the low nibble).
+// code; writes the 16 codes as 8 bytes (even element in the low nibble).  A zero
+// value or a zero scale gives code 0 (not the E2M1 code of -0), as the reference.
 __device__ __forceinline__ uint32_t nvfp4_block(const float* v, float global_scale,
                                                 uint2* packed) {
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   uint32_t sc = 0;
-  if (amax != 0.0f) sc = e4m3_encode_pos(__fdiv_rn(__fdiv_rn(amax, 6.0f), global_scale));
+  if (amax != 0.0f) sc = e4m3_cvt_pos(__fdiv_rn(__fdiv_rn(amax, 6.0f), global_scale));
   const float dec = __fmul_rn(e4m3_decode(sc), global_scale);
-  uint32_t w0 = 0, w1 = 0;
+  float q0[8], q1[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    uint32_t code = 0;
-    if (!(v[i] == 0.0f || sc == 0)) code = e2m1_encode(__fdiv_rn(v[i], dec));
-    if (i < 8)
-      w0 |= code << (4 * i);
-    else
-      w1 |= code << (4 * (i - 8));
+  for (int i = 0; i < 8; ++i) {
+    q0[i] = (v[i] == 0.0f || sc == 0) ? 0.0f : __fdiv_rn(v[i], dec);
+    q1[i] = (v[i + 8] == 0.0f || sc == 0) ? 0.0f : __fdiv_rn(v[i + 8], dec);
   }
-  packed->x = w0;
-  packed->y = w1;
+  packed->x = e2m1x8_cvt(q0);
+  packed->y = e2m1x8_cvt(q1);
   return sc;
 }
 

@@ -66,6 +66,9 @@ struct LayerPlan {
   // run); plane_mode: routed results go through the per-slot plane and the
   // deterministic expert-order combine (decode, and any layer with EXL3 experts)
   bool exl3, nvfp4, plane_mode;
+  // external: the routed plane is the caller's (expert parallelism); only the
+  // shared expert and the combine run
+  bool external;
   uint64_t exl3_ws;
   uint64_t tiles, tile_count, route_row, row_token, row_slot, row_weight, gx, gh, row_prow;
   uint64_t xq, xsf, hbuf, hq, hsf, plane, hs, sbuf, sparts1, sparts2, total;
@@ -81,28 +84,30 @@ struct LayerPlan {
     exl3 = (d.flags & GLMAXX_MOE_EXL3_EXPERTS) != 0;
     const glmaxx_moe_exl3_experts* xe =
         exl3 ? reinterpret_cast<const glmaxx_moe_exl3_experts*>(d.exl3_experts) : nullptr;
-    nvfp4 = !exl3 || (xe != nullptr && xe->codec_u8 != 0);
-    plane_mode = decode || exl3;
+    external = (d.flags & GLMAXX_MOE_EXTERNAL_ROUTED) != 0;
+    nvfp4 = !external && (!exl3 || (xe != nullptr && xe->codec_u8 != 0));
+    plane_mode = decode || exl3 || external;
     nt = decode ? 32 : 128;
     const uint32_t A = r.A;
     const uint32_t active = A < r.E ? A : r.E;
     max_tiles = (A + nt - 1) / nt + active;
     sf_rows = max_tiles * 128;  // each n tile owns a 128-row scale atom
-    tiles = c.take(uint64_t(max_tiles) * sizeof(NTile));
+    const uint64_t rA = external ? 0 : A;  // the routed stages' planes (none when external)
+    tiles = c.take(external ? 0 : uint64_t(max_tiles) * sizeof(NTile));
     tile_count = c.take(16);
-    route_row = c.take(uint64_t(A) * 4);
-    row_token = c.take(uint64_t(A) * 4);
-    row_slot = c.take(uint64_t(A) * 4);
-    row_weight = c.take(uint64_t(A) * 4);
-    gx = c.take(uint64_t(A) * 4);
-    gh = c.take(uint64_t(A) * 4);
-    row_prow = c.take(uint64_t(A) * 4);
-    xq = c.take(uint64_t(A) * H / 2);
-    xsf = c.take(uint64_t(sf_rows) * H / 16);
-    hbuf = c.take(uint64_t(A) * I * 2);
-    hq = c.take(uint64_t(A) * I / 2);
-    hsf = c.take(uint64_t(sf_rows) * I / 16);
-    plane = plane_mode ? c.take(uint64_t(A) * H * 4) : c.take(0);
+    route_row = c.take(rA * 4);
+    row_token = c.take(rA * 4);
+    row_slot = c.take(rA * 4);
+    row_weight = c.take(rA * 4);
+    gx = c.take(rA * 4);
+    gh = c.take(rA * 4);
+    row_prow = c.take(rA * 4);
+    xq = c.take(rA * H / 2);
+    xsf = c.take(external ? 0 : uint64_t(sf_rows) * H / 16);
+    hbuf = c.take(rA * I * 2);
+    hq = c.take(rA * I / 2);
+    hsf = c.take(external ? 0 : uint64_t(sf_rows) * I / 16);
+    plane = (plane_mode && !external) ? c.take(uint64_t(A) * H * 4) : c.take(0);
     hs = shared ? c.take(uint64_t(r.T) * Is * 2) : c.take(0);
     sbuf = (shared && plane_mode) ? c.take(uint64_t(r.T) * H * 4) : c.take(0);
     exl3_ws = exl3 ? c.take(exl3_experts_workspace_bytes(A, H, I, r.E)) : c.take(0);
@@ -131,8 +136,15 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
   for (uint64_t v : d.reserved)
     if (v) return false;
   if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT |
-                          GLMAXX_MOE_EXL3_EXPERTS))
+                          GLMAXX_MOE_EXL3_EXPERTS | GLMAXX_MOE_EXTERNAL_ROUTED))
     return false;
+  if (d.flags & GLMAXX_MOE_EXTERNAL_ROUTED) {
+    if (!(d.flags & GLMAXX_MOE_ROUTES_GIVEN) || (d.flags & GLMAXX_MOE_EXL3_EXPERTS) ||
+        !aligned(d.routed_plane_f32, 16))
+      return false;
+  } else if (d.routed_plane_f32) {
+    return false;
+  }
   bool nvfp4_weights = true;
   if (d.flags & GLMAXX_MOE_EXL3_EXPERTS) {
     if (d.exl3_experts == 0) return false;
@@ -174,6 +186,7 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
       return false;
     if (!aligned(d.shared13_bf16, 256) || !aligned(d.shared2_bf16, 256)) return false;
   }
+  if (d.flags & GLMAXX_MOE_EXTERNAL_ROUTED) nvfp4_weights = false;  // no routed GEMMs run
   if (nvfp4_weights &&
       !(aligned(d.w13_values, 256) && aligned(d.w13_scales, 16) && aligned(d.w13_global_f32, 4) &&
         aligned(d.w2_values, 256) && aligned(d.w2_scales, 16) && aligned(d.w2_global_f32, 4)))
@@ -393,6 +406,23 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
       CHECK(launch_gemm(kShared2Bf16N128, g2, info.sms, sstream));
     }
     if (side) CHECK(cudaEventRecord(side->join, sstream));
+  }
+
+  if (p.external) {
+    // Expert parallelism: the routed slot plane was written by the experts'
+    // owner ranks; what is left is the deterministic combine with the shared
+    // expert, the same kernel (and so the same bits) as the local plane path.
+    for (uint32_t stage = kStageCompact; stage <= kStageFc2; ++stage) CHECK(mark(stage, stream));
+    CHECK(mark(kStageCombine, stream));
+    if (side) CHECK(cudaStreamWaitEvent(stream, side->join, 0));
+    const float* shared_in = !p.shared ? nullptr
+                             : (p.decode ? at<float>(ws, p.sparts2) : at<float>(ws, p.sbuf));
+    CHECK(launch_combine(reinterpret_cast<const float*>(d.routed_plane_f32), experts, shared_in,
+                         p.decode ? p.s2_splits : 1,
+                         (p.shared && p.decode) ? at<float>(ws, p.sbuf) : nullptr, out, r.T, p.H,
+                         r.K, stream));
+    CHECK(mark(kLayerStages, stream));
+    return 0;
   }
 
   // 1. router (or caller routes) -> dense routes + token-in-expert bitmap

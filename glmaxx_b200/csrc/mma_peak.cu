@@ -9,7 +9,9 @@
 //   shapes: N = 128 or 256 tokens per MMA; dual = two MMAs per K-block that
 //   share the B tile (the FC1 gate/up pattern, N = 128 only).
 //   copies: kind 1 = tcgen05.cp.32x128b.warpx4 (one 512-byte scale atom, to all
-//   four lane quarters), kind 2 = tcgen05.cp.128x256b (4 KB lane-major block).
+//   four lane quarters), kind 2 = tcgen05.cp.128x256b (4 KB lane-major block);
+//   kind | 4: the copies of a 4-K-block stage are issued together before its
+//   first MMA (the grouped GEMMs' pattern) instead of before each K-block.
 //
 // Operand bytes are a fixed pseudo-random pattern (finite E2M1 codes, E4M3
 // scales near 1), so the tensor pipe does representative switching work.
@@ -51,7 +53,7 @@ __device__ __forceinline__ uint32_t mix32(uint32_t i) {
   return i;
 }
 
-template <int N, bool DUAL, int CP_KIND>
+template <int N, bool DUAL, int CP_KIND, bool BATCH>
 __global__ void __launch_bounds__(kPeakThreads, 1)
     nvfp4_mma_peak_kernel(uint32_t iters, uint32_t copies, uint32_t* status,
                           unsigned long long* cycles) {
@@ -106,8 +108,8 @@ __global__ void __launch_bounds__(kPeakThreads, 1)
     for (uint32_t it = 0; it < iters; ++it) {
 #pragma unroll
       for (int kb = 0; kb < 4; ++kb) {
-        if (CP_KIND != 0) {
-          for (uint32_t c = 0; c < copies; ++c) {
+        if (CP_KIND != 0 && (!BATCH || kb == 0)) {
+          for (uint32_t c = 0; c < (BATCH ? 4 * copies : copies); ++c) {
             const uint32_t dst = tmem + kCpBase + (slot % kCpSlots) * 8;
             if (CP_KIND == 1)
               tc_cp_sf(dst, smem_desc_sf(ssf + (slot % 16) * 512));
@@ -138,11 +140,11 @@ __global__ void __launch_bounds__(kPeakThreads, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-template <int N, bool DUAL, int CP_KIND>
+template <int N, bool DUAL, int CP_KIND, bool BATCH = false>
 cudaError_t launch_peak(uint32_t iters, uint32_t copies, uint32_t ctas, uint32_t* status,
                         unsigned long long* cycles, cudaStream_t stream) {
   using S = PeakShape<N, DUAL>;
-  auto kern = nvfp4_mma_peak_kernel<N, DUAL, CP_KIND>;
+  auto kern = nvfp4_mma_peak_kernel<N, DUAL, CP_KIND, BATCH>;
   cudaError_t st = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
   if (st != cudaSuccess) return st;
   kern<<<ctas, kPeakThreads, S::kSmem, stream>>>(iters, copies, status, cycles);
@@ -159,30 +161,31 @@ extern "C" int32_t glmaxx_nvfp4_mma_peak_launch(uint32_t n, uint32_t dual, uint3
                                                 void* cuda_stream) {
   using namespace glmaxx;
   if (status_u32 == nullptr) return GLMAXX_ERR_NULL;
-  if (!(n == 128 || n == 256) || (dual && n != 128) || copy_kind > 2 ||
-      (copy_kind == 0) != (copies_per_kblock == 0) || copies_per_kblock > 16 || iters == 0 || iters > 200000 ||
-      ctas == 0 || ctas > 4096)
+  const uint32_t form = copy_kind & 3u;
+  const bool batch = (copy_kind & 4u) != 0;
+  if (!(n == 128 || n == 256) || (dual && n != 128) || copy_kind > 6 || form == 3 ||
+      (form == 0) != (copies_per_kblock == 0) || (batch && form == 0) || copies_per_kblock > 16 ||
+      iters == 0 || iters > 200000 || ctas == 0 || ctas > 4096)
     return GLMAXX_ERR_DESCRIPTOR;
   DeviceInfo info;
   const int32_t arch = current_device_info(&info);
   if (arch != 0) return arch;
   cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
   cudaError_t st = cudaErrorInvalidValue;
-#define GLMAXX_PEAK(N_, D_, K_) \
-  st = launch_peak<N_, D_, K_>(iters, copies_per_kblock, ctas, status_u32, cycles_u64, s)
-  if (n == 128 && dual) {
-    if (copy_kind == 0) GLMAXX_PEAK(128, true, 0);
-    else if (copy_kind == 1) GLMAXX_PEAK(128, true, 1);
-    else GLMAXX_PEAK(128, true, 2);
-  } else if (n == 128) {
-    if (copy_kind == 0) GLMAXX_PEAK(128, false, 0);
-    else if (copy_kind == 1) GLMAXX_PEAK(128, false, 1);
-    else GLMAXX_PEAK(128, false, 2);
-  } else {
-    if (copy_kind == 0) GLMAXX_PEAK(256, false, 0);
-    else if (copy_kind == 1) GLMAXX_PEAK(256, false, 1);
-    else GLMAXX_PEAK(256, false, 2);
-  }
+#define GLMAXX_PEAK(N_, D_, K_, B_) \
+  st = launch_peak<N_, D_, K_, B_>(iters, copies_per_kblock, ctas, status_u32, cycles_u64, s)
+#define GLMAXX_PEAK_FORMS(N_, D_)                    \
+  do {                                               \
+    if (form == 0) GLMAXX_PEAK(N_, D_, 0, false);    \
+    else if (form == 1 && !batch) GLMAXX_PEAK(N_, D_, 1, false); \
+    else if (form == 1) GLMAXX_PEAK(N_, D_, 1, true);            \
+    else if (!batch) GLMAXX_PEAK(N_, D_, 2, false);              \
+    else GLMAXX_PEAK(N_, D_, 2, true);                           \
+  } while (0)
+  if (n == 128 && dual) GLMAXX_PEAK_FORMS(128, true);
+  else if (n == 128) GLMAXX_PEAK_FORMS(128, false);
+  else GLMAXX_PEAK_FORMS(256, false);
+#undef GLMAXX_PEAK_FORMS
 #undef GLMAXX_PEAK
   return st == cudaSuccess ? 0 : int32_t(st);
 }

@@ -32,97 +32,94 @@ namespace glmaxx {
 // Router logits.  Canonical order (shared with the CPU restatement):
 //   logit[t][e] = ((s_0 + s_1) + ...) + s_7,  s_c = fma-chain over the c-th
 //   eighth of H in ascending k from 0.
-// Both logits kernels write the eight chunk sums partial[c][t][e]; the selection
-// kernel adds them in that order.  The first kernel of a step also clears the
+// grid (E/32, ceil(T/32), 8), 256 threads: warp w -> experts e0+4w..e0+4w+3,
+// lane -> token t0+lane.  The first kernel of a step also clears the
 // token-in-expert bitmap.
 // ---------------------------------------------------------------------------
-// Small T (decode): lane = expert, 32 experts per warp, two warps per CTA; each
-// thread runs the 8 fma chains of its expert against the CTA's 8 tokens, as four
-// fma.rn.f32x2 over token pairs (two independent correctly rounded fmas each, so
-// every chain is still one ascending fma chain).  The 8 token rows of the chunk
-// are staged once in shared memory as fp32 [k][8] and read as broadcasts; each
-// lane streams its expert's weight row with 16-byte loads, 8 loads in flight.
-// grid (ceil(E/64), ceil(T/8), 8).  The old design (32 tokens x 32 experts per
-// CTA, both operands from shared memory) was bound by shared-memory bandwidth.
-constexpr uint32_t kRsTokens = 8;
-constexpr uint32_t kRsThreads = 64;
-constexpr uint32_t kRsRing = 8;  // weight loads in flight per lane (8 x 16 bytes)
+// K is staged through shared memory in fp32 sub-tiles of 256 (pitch 260 keeps
+// the 128-bit loads of one warp phase on distinct banks); each thread keeps four
+// independent fma-chains (4 experts of one token) in ascending k.
+constexpr uint32_t kRouterSub = 256;
+constexpr uint32_t kRouterPitch = kRouterSub + 4;
 
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
-__global__ void __launch_bounds__(kRsThreads) router_logits_rows_kernel(
+__global__ void __launch_bounds__(256) router_logits_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
     uint32_t T, uint32_t H, uint32_t E, uint32_t* __restrict__ bitmap, uint32_t bitmap_words) {
-  extern __shared__ __align__(16) float rxs[];  // [chunk][8 tokens] fp32
+  extern __shared__ float rsm[];
+  float* xs = rsm;                        // [32 tokens][kRouterPitch]
+  float* ws = rsm + 32 * kRouterPitch;    // [32 experts][kRouterPitch]
   const uint32_t chunk = H / 8;
-  const uint32_t c = blockIdx.z, t0 = blockIdx.y * kRsTokens;
+  const uint32_t e0 = blockIdx.x * 32, t0 = blockIdx.y * 32, c = blockIdx.z;
   const uint32_t tid = threadIdx.x;
   {
     const uint64_t lin = (uint64_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     const uint64_t nthreads = uint64_t(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
     for (uint64_t i = lin * blockDim.x + tid; i < bitmap_words; i += nthreads) bitmap[i] = 0;
   }
-  // stage the 8 token rows of this chunk: piece i = (row i % 8, 8 columns from 8 * (i / 8))
-  const uint32_t pieces = kRsTokens * (chunk / 8);
-  for (uint32_t i = tid; i < pieces; i += kRsThreads) {
-    const uint32_t r = i % kRsTokens, kk = (i / kRsTokens) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t0 + r < T)
-      v = *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + uint64_t(c) * chunk + kk);
-    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  // Sub-tile fills are software-pipelined: the global loads of sub-tile s+1 are
+  // in flight while sub-tile s is computed.  Thread tid owns pieces tid + 256i
+  // (i < 4) of 16 bytes: row p / 32, columns (p % 32) * 8 .. +8.
+  uint4 rx[4], rw[4];
+  auto gload = [&](uint32_t k0) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      rxs[(kk + 2 * q) * kRsTokens + r] = __uint_as_float(wv[q] << 16);
-      rxs[(kk + 2 * q + 1) * kRsTokens + r] = __uint_as_float(wv[q] & 0xffff0000u);
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
+      const uint64_t col = uint64_t(c) * chunk + k0 + kk;
+      const bool in_k = k0 + kk < chunk;
+      rx[i] = (in_k && t0 + r < T) ? *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + col)
+                                   : make_uint4(0, 0, 0, 0);
+      rw[i] = (in_k && e0 + r < E) ? *reinterpret_cast<const uint4*>(w + uint64_t(e0 + r) * H + col)
+                                   : make_uint4(0, 0, 0, 0);
     }
-  }
-  __syncthreads();
-  const uint32_t e = blockIdx.x * kRsThreads + tid;
-  if (e >= E) return;
-  const uint16_t* wr = w + uint64_t(e) * H + uint64_t(c) * chunk;
-  const uint32_t nsteps = chunk / 8;
-  uint64_t acc[4] = {0, 0, 0, 0};  // token pairs (0,1), (2,3), (4,5), (6,7)
-  uint4 ring[kRsRing];
+  };
+  auto sstore = [&]() {
 #pragma unroll
-  for (uint32_t j = 0; j < kRsRing; ++j)
-    ring[j] = j < nsteps ? __ldg(reinterpret_cast<const uint4*>(wr) + j) : make_uint4(0, 0, 0, 0);
-  for (uint32_t s0 = 0; s0 < nsteps; s0 += kRsRing) {
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
+      const uint32_t xw[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
+      const uint32_t wwv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
+      float4* xd = reinterpret_cast<float4*>(xs + r * kRouterPitch + kk);
+      float4* wd = reinterpret_cast<float4*>(ws + r * kRouterPitch + kk);
+      xd[0] = make_float4(__uint_as_float(xw[0] << 16), __uint_as_float(xw[0] & 0xffff0000u),
+                          __uint_as_float(xw[1] << 16), __uint_as_float(xw[1] & 0xffff0000u));
+      xd[1] = make_float4(__uint_as_float(xw[2] << 16), __uint_as_float(xw[2] & 0xffff0000u),
+                          __uint_as_float(xw[3] << 16), __uint_as_float(xw[3] & 0xffff0000u));
+      wd[0] = make_float4(__uint_as_float(wwv[0] << 16), __uint_as_float(wwv[0] & 0xffff0000u),
+                          __uint_as_float(wwv[1] << 16), __uint_as_float(wwv[1] & 0xffff0000u));
+      wd[1] = make_float4(__uint_as_float(wwv[2] << 16), __uint_as_float(wwv[2] & 0xffff0000u),
+                          __uint_as_float(wwv[3] << 16), __uint_as_float(wwv[3] & 0xffff0000u));
+    }
+  };
+  gload(0);
+  for (uint32_t k0 = 0; k0 < chunk; k0 += kRouterSub) {
+    const uint32_t kn = min(kRouterSub, chunk - k0);  // multiple of 8 (H % 256 == 0)
+    __syncthreads();
+    sstore();
+    __syncthreads();
+    if (k0 + kRouterSub < chunk) gload(k0 + kRouterSub);
+    const float* xr = xs + lane * kRouterPitch;
+    const float* wr = ws + (warp * 4) * kRouterPitch;
+#pragma unroll 2
+    for (uint32_t k = 0; k < kn; k += 4) {
+      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
 #pragma unroll
-    for (uint32_t j = 0; j < kRsRing; ++j) {
-      const uint32_t s = s0 + j;
-      if (s < nsteps) {
-        const uint4 cur = ring[j];
-        if (s + kRsRing < nsteps) ring[j] = __ldg(reinterpret_cast<const uint4*>(wr) + s + kRsRing);
-        const uint32_t words[4] = {cur.x, cur.y, cur.z, cur.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const uint32_t k = 8 * s + 2 * q + half;
-            const uint32_t wb = half ? (words[q] & 0xffff0000u) : (words[q] << 16);
-            const uint64_t wdup = (uint64_t(wb) << 32) | wb;
-            const ulonglong2 xa = *reinterpret_cast<const ulonglong2*>(rxs + k * kRsTokens);
-            const ulonglong2 xb = *reinterpret_cast<const ulonglong2*>(rxs + k * kRsTokens + 4);
-            acc[0] = ffma2(xa.x, wdup, acc[0]);
-            acc[1] = ffma2(xa.y, wdup, acc[1]);
-            acc[2] = ffma2(xb.x, wdup, acc[2]);
-            acc[3] = ffma2(xb.y, wdup, acc[3]);
-          }
-        }
+      for (int j = 0; j < 4; ++j) {
+        const float4 wv = *reinterpret_cast<const float4*>(wr + j * kRouterPitch + k);
+        acc[j] = fmaf(xv.x, wv.x, acc[j]);
+        acc[j] = fmaf(xv.y, wv.y, acc[j]);
+        acc[j] = fmaf(xv.z, wv.z, acc[j]);
+        acc[j] = fmaf(xv.w, wv.w, acc[j]);
       }
     }
   }
+  const uint32_t t = t0 + lane;
+  if (t < T) {
 #pragma unroll
-  for (int p = 0; p < 4; ++p) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t t = t0 + 2 * p + h;
-      if (t < T)
-        partial[(uint64_t(c) * T + t) * E + e] = __uint_as_float(uint32_t(acc[p] >> (32 * h)));
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t e = e0 + warp * 4 + j;
+      if (e < E) partial[(uint64_t(c) * T + t) * E + e] = acc[j];
     }
   }
 }
@@ -140,6 +137,12 @@ constexpr uint32_t kRtXPitch = 128 * 2 + 8;  // floats per k row of token pairs
 constexpr uint32_t kRtWPitch = 128 + 4;      // floats per k row of experts
 constexpr uint32_t kRtBufFloats = kRtSlab * (kRtXPitch + kRtWPitch);
 constexpr uint32_t kRouterTiledMinTokens = 256;
+
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 
 __global__ void __launch_bounds__(256, 2) router_logits_tiled_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
@@ -502,16 +505,62 @@ __global__ void zero_words_kernel(uint32_t* p, uint64_t n) {
 // Compaction (single CTA, 1024 threads): per-expert counts and word prefixes
 // from the bitmap, exclusive offsets (plain and 128-padded), n-tile list.
 // ---------------------------------------------------------------------------
+// Large T: the per-expert word prefixes and counts, one CTA per expert (the
+// experts' scans are independent; a single CTA walking 256 experts x W words
+// was a latency chain of ~200 us at T = 8192).  Thread j scans a run of
+// consecutive words; the run totals are scanned across the CTA.
+constexpr uint32_t kPrefixThreads = 256;
+__global__ void __launch_bounds__(kPrefixThreads) compact_prefix_kernel(
+    const uint32_t* __restrict__ bitmap, uint32_t W, uint32_t* __restrict__ wprefix,
+    uint32_t* __restrict__ counts) {
+  __shared__ uint32_t warp_tot[kPrefixThreads / 32];
+  const uint32_t e = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t per = (W + kPrefixThreads - 1) / kPrefixThreads;  // words per thread (<= 8)
+  const uint32_t w0 = tid * per;
+  const uint32_t* row = bitmap + uint64_t(e) * W;
+  uint32_t pc[8];
+  uint32_t tot = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    pc[i] = (i < per && w0 + i < W) ? __popc(row[w0 + i]) : 0u;
+    tot += pc[i];
+  }
+  uint32_t incl = tot;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= uint32_t(off)) incl += o;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  uint32_t base = 0;
+  for (uint32_t w = 0; w < warp; ++w) base += warp_tot[w];
+  uint32_t run = base + incl - tot;  // exclusive prefix of this thread's first word
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    if (i < per && w0 + i < W) wprefix[uint64_t(e) * W + w0 + i] = run;
+    run += pc[i];
+  }
+  if (tid == kPrefixThreads - 1) {
+    uint32_t total = 0;
+    for (uint32_t w = 0; w < kPrefixThreads / 32; ++w) total += warp_tot[w];
+    counts[e] = total;
+  }
+}
+
 __global__ void __launch_bounds__(1024) compact_kernel(
     const uint32_t* __restrict__ bitmap, uint32_t W, uint32_t E, uint32_t nt, uint32_t sf_row_cap,
     uint32_t max_tiles, uint32_t* __restrict__ wprefix, uint32_t* __restrict__ counts,
     uint32_t* __restrict__ offsets, uint32_t* __restrict__ poffs, NTile* __restrict__ tiles,
     uint32_t* __restrict__ tile_count, uint32_t* __restrict__ status,
-    const uint8_t* __restrict__ no_tiles) {
-  // no_tiles[e] != 0 (optional): expert e gets rows but no GEMM tiles (an EXL3 expert)
+    const uint8_t* __restrict__ no_tiles, bool counts_ready) {
+  // no_tiles[e] != 0 (optional): expert e gets rows but no GEMM tiles (an EXL3 expert).
+  // counts_ready: compact_prefix_kernel already wrote wprefix and counts.
   __shared__ uint32_t cnt_s[256], toff_s[257], poff_s[257], off_s[257];
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (W <= 32 && E <= 256) {
+  if (counts_ready) {
+    for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt_s[e] = counts[e];
+  } else if (W <= 32 && E <= 256) {
     // T <= 1024: one bitmap word per lane; the warp's 8 experts (warp + 32q) load
     // together and their scans interleave
     uint32_t pc[8], incl[8];
@@ -537,7 +586,7 @@ __global__ void __launch_bounds__(1024) compact_kernel(
       }
     }
   }
-  for (uint32_t e = warp; (W > 32 || E > 256) && e < E; e += 32) {
+  for (uint32_t e = warp; !counts_ready && (W > 32 || E > 256) && e < E; e += 32) {
     uint32_t running = 0;
     for (uint32_t w0 = 0; w0 < W; w0 += 32) {
       const uint32_t w = w0 + lane;
@@ -1126,8 +1175,17 @@ __global__ void pack_encode_kernel(const void* __restrict__ src, int src_bf16, u
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
                                  uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,
                                  cudaStream_t stream) {
+  const size_t smem = 2ull * 32 * kRouterPitch * 4;
+  static bool configured[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t st = cudaFuncSetAttribute(router_logits_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    if (st != cudaSuccess) return st;
+    configured[dev] = true;
+  }
   if (T >= kRouterTiledMinTokens && E % 128 == 0) {
     const size_t tsmem = 2ull * kRtBufFloats * 4;
     static bool tconfigured[64] = {};
@@ -1143,18 +1201,8 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* pa
                                                              bitmap_words);
     return cudaPeekAtLastError();
   }
-  // H <= 16384: at most 64 KB of staged token rows
-  const size_t smem = size_t(H / 8) * kRsTokens * 4;
-  static bool configured[64] = {};
-  if (!configured[dev]) {
-    cudaError_t st = cudaFuncSetAttribute(router_logits_rows_kernel,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 64 << 10);
-    if (st != cudaSuccess) return st;
-    configured[dev] = true;
-  }
-  dim3 grid((E + kRsThreads - 1) / kRsThreads, (T + kRsTokens - 1) / kRsTokens, 8);
-  router_logits_rows_kernel<<<grid, kRsThreads, smem, stream>>>(x, w, partial, T, H, E, bitmap,
-                                                                bitmap_words);
+  dim3 grid((E + 31) / 32, (T + 31) / 32, 8);
+  router_logits_kernel<<<grid, 256, smem, stream>>>(x, w, partial, T, H, E, bitmap, bitmap_words);
   return cudaPeekAtLastError();
 }
 
@@ -1193,9 +1241,16 @@ cudaError_t launch_compact(const uint32_t* bitmap, uint32_t T, uint32_t E, uint3
                            uint32_t* counts, uint32_t* offsets, uint32_t* poffs, NTile* tiles,
                            uint32_t* tile_count, uint32_t* status, cudaStream_t stream,
                            const uint8_t* no_tiles) {
-  compact_kernel<<<1, 1024, 0, stream>>>(bitmap, (T + 31) / 32, E, nt, sf_row_cap, max_tiles,
-                                         wprefix, counts, offsets, poffs, tiles, tile_count, status,
-                                         no_tiles);
+  const uint32_t W = (T + 31) / 32;
+  // more than one bitmap word per lane (T > 1024): per-expert prefixes on E CTAs first
+  const bool wide = W > 32 && W <= 8 * kPrefixThreads && E <= 256;
+  if (wide) {
+    compact_prefix_kernel<<<E, kPrefixThreads, 0, stream>>>(bitmap, W, wprefix, counts);
+    const cudaError_t st = cudaPeekAtLastError();
+    if (st != cudaSuccess) return st;
+  }
+  compact_kernel<<<1, 1024, 0, stream>>>(bitmap, W, E, nt, sf_row_cap, max_tiles, wprefix, counts,
+                                         offsets, poffs, tiles, tile_count, status, no_tiles, wide);
   return cudaPeekAtLastError();
 }
 

@@ -48,6 +48,7 @@ enum {
   GLMAXX_MOE_EXL3_ABI_VERSION = 1,
   GLMAXX_MOE_FINISH_ABI_VERSION = 1,
   GLMAXX_MOE_PEER_ABI_VERSION = 1,
+  GLMAXX_MOE_EP_ABI_VERSION = 1,
   GLMAXX_FC1_DECODE_PERSISTENT = 1,
   GLMAXX_FC1_PREFILL_GROUPED = 2,
   GLMAXX_EXL3_GATE = 1,
@@ -82,6 +83,11 @@ enum {
   GLMAXX_MOE_ROUTES_GIVEN = 1u << 0,   /* route_experts/route_weights are inputs */
   GLMAXX_MOE_SHARED_EXPERT = 1u << 1,  /* add the bf16 shared expert            */
   GLMAXX_MOE_EXL3_EXPERTS = 1u << 2,   /* exl3_experts describes EXL3 experts   */
+  /* the routed contributions are already in routed_plane_f32 [tokens][top_k][hidden]
+   * (expert parallelism: written there by the experts' owner ranks); the step runs
+   * the shared expert and the deterministic expert-order combine only.  Needs
+   * GLMAXX_MOE_ROUTES_GIVEN (route_experts_u16 orders the combine). */
+  GLMAXX_MOE_EXTERNAL_ROUTED = 1u << 3,
 };
 
 /* glmaxx_kernel.h:22-57 (unchanged layout). */
@@ -317,7 +323,9 @@ struct glmaxx_moe_layer_descriptor {
   uint64_t sequence;
   /* host address of a glmaxx_moe_exl3_experts (flag GLMAXX_MOE_EXL3_EXPERTS), else 0 */
   uint64_t exl3_experts;
-  uint64_t reserved[3];
+  /* flag GLMAXX_MOE_EXTERNAL_ROUTED: [tokens][top_k][hidden] fp32 slot plane, else 0 */
+  uint64_t routed_plane_f32;
+  uint64_t reserved[2];
 };
 
 /*
@@ -400,6 +408,59 @@ struct glmaxx_moe_peer_descriptor {
   uint64_t norms_bf16;
   uint64_t status_u32;
   uint64_t reserved[3];
+};
+
+/*
+ * Expert-parallel exchange (new; the all-to-all alternative to the reference's
+ * tensor-parallel layout, crates/glm-engine/src/manifest.rs:143-165 -- not a
+ * reference layout).  Experts are split in contiguous blocks over `ranks`
+ * owners (owner of e = e / (experts / ranks)); tokens are split over ranks as
+ * data.  Per step, on every rank: glmaxx_router_compact_launch on its tokens;
+ * glmaxx_moe_ep_dispatch_launch sends each compacted row to its expert's owner
+ * (bf16 token row, owner-local expert, routing weight, source); the owner runs
+ * glmaxx_moe_layer_launch over its received rows (GLMAXX_MOE_ROUTES_GIVEN,
+ * top_k 1, its experts' weights); glmaxx_moe_ep_return_launch copies each output
+ * row into the source rank's slot plane [tokens][top_k][hidden]; the source runs
+ * glmaxx_moe_layer_launch with GLMAXX_MOE_EXTERNAL_ROUTED (shared expert +
+ * expert-order combine).  The arrays of 8 hold every rank's buffers as mapped on
+ * this GPU, in rank order (entries >= ranks are 0).  dest_row_offset[d] is the
+ * first row of this rank's block in owner d's buffers: the sum of the row counts
+ * ranks before this one send to d (their expert_offsets, exchanged by the host).
+ * Rows move with plain 16-byte loads and stores, peer memory included.  A row
+ * past an owner's capacity sets GLMAXX_STATUS_CAPACITY_EXCEEDED and is dropped.
+ */
+#if defined(__cplusplus)
+struct alignas(16) glmaxx_moe_ep_descriptor {
+#else
+struct glmaxx_moe_ep_descriptor {
+#endif
+  uint32_t abi_version; /* GLMAXX_MOE_EP_ABI_VERSION */
+  uint32_t struct_bytes;
+  uint32_t ranks;       /* 1..8 */
+  uint32_t rank;
+  uint32_t tokens;      /* dispatch: this rank's tokens */
+  uint32_t hidden;
+  uint32_t experts;     /* all experts (a multiple of ranks) */
+  uint32_t top_k;
+  uint32_t rows;        /* return: rows this rank received */
+  uint32_t reserved0[3];
+  uint64_t input_bf16;            /* dispatch: [tokens][hidden]                   */
+  uint64_t compacted_tokens_u32;  /* dispatch: glmaxx_router_compact_launch outputs */
+  uint64_t compacted_experts_u16;
+  uint64_t compacted_slots_u8;
+  uint64_t compacted_weights_f32;
+  uint64_t expert_offsets_u32;
+  uint64_t recv_x_bf16[8];        /* every rank's receive buffers                 */
+  uint64_t recv_expert_u16[8];
+  uint64_t recv_weight_f32[8];
+  uint64_t recv_source_u32[8];
+  uint32_t recv_capacity[8];      /* rows each rank's receive buffers hold        */
+  uint32_t dest_row_offset[8];
+  uint64_t rows_out_f32;          /* return: [rows][hidden], this rank's owner output */
+  uint64_t planes_f32[8];         /* every rank's slot plane [tokens_r][top_k][hidden] */
+  uint32_t plane_tokens[8];
+  uint64_t validation_error_u32;
+  uint64_t reserved[4];
 };
 
 /* ---- reference entry points (glmaxx_kernel.h:123-250) ---- */
@@ -621,13 +682,27 @@ int32_t glmaxx_nvfp4_pack_launch(uint64_t src, int32_t src_is_bf16, uint32_t bat
  * 256; dual needs 128), K = 64, on operands resident in shared memory and scales
  * resident in TMEM, with copies_per_kblock tcgen05.cp scale copies before each
  * K-block's MMAs (copy_kind 1: 32x128b.warpx4, 512 bytes; 2: 128x256b, 4 KB;
- * 0: none).  FLOPs per launch = ctas * iters * 4 * (dual ? 2 : 1) * 2*128*n*64.
+ * 0: none; copy_kind | 4: a 4-K-block stage's copies all issued before its first
+ * MMA).  FLOPs per launch = ctas * iters * 4 * (dual ? 2 : 1) * 2*128*n*64.
  * iters <= 200000.  cycles_u64 (optional, [ctas]) receives each CTA's %clock64
  * span of its MMA loop; status_u32 receives GLMAXX_STATUS bits. */
 int32_t glmaxx_nvfp4_mma_peak_launch(uint32_t n, uint32_t dual, uint32_t copy_kind,
                                      uint32_t copies_per_kblock, uint32_t iters, uint32_t ctas,
                                      uint32_t* status_u32, unsigned long long* cycles_u64,
                                      void* cuda_stream);
+
+int32_t glmaxx_moe_ep_dispatch_launch(const struct glmaxx_moe_ep_descriptor* descriptor,
+                                      void* cuda_stream);
+int32_t glmaxx_moe_ep_return_launch(const struct glmaxx_moe_ep_descriptor* descriptor,
+                                    void* cuda_stream);
+
+/* Self-check (no reference counterpart): runs every fp32 bit pattern through the
+ * hardware E2M1 / E4M3 conversions the quantisation kernels use and through this
+ * library's restatement of the reference codec (float.rs:15-73), on the GPU.
+ * result_u64x4 (device): [0] E2M1 mismatches over all finite values, [1] E4M3
+ * mismatches over all positive finite values, [2]/[3] bits + 1 of one
+ * mismatching input (0 = none). */
+int32_t glmaxx_nvfp4_codec_selfcheck_launch(unsigned long long* result_u64x4, void* cuda_stream);
 
 #if defined(__cplusplus)
 }
@@ -643,6 +718,7 @@ static_assert(sizeof(glmaxx_moe_layer_descriptor) == 240, "layer descriptor size
 static_assert(sizeof(glmaxx_moe_exl3_experts) == 128, "EXL3 experts descriptor size");
 static_assert(sizeof(glmaxx_moe_finish_descriptor) == 112, "finish descriptor size");
 static_assert(sizeof(glmaxx_moe_peer_descriptor) == 80, "peer descriptor size");
+static_assert(sizeof(glmaxx_moe_ep_descriptor) == 560, "expert-parallel descriptor size");
 #endif
 
 #endif /* GLMAXX_KERNEL_H_ */

@@ -214,6 +214,7 @@ unsafe extern "C" {
         validation_error_u32: u64,
         stream: *mut c_void,
     ) -> i32;
+    pub fn glmaxx_nvfp4_codec_selfcheck_launch(result_u64x4: *mut u64, stream: *mut c_void) -> i32;
     pub fn glmaxx_nvfp4_mma_peak_launch(
         n: u32,
         dual: u32,
