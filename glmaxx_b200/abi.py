@@ -20,11 +20,13 @@ EXL3_ABI_VERSION = 1
 MOE_EXL3_ABI_VERSION = 1
 MOE_FINISH_ABI_VERSION = 1
 MOE_PEER_ABI_VERSION = 1
+MOE_EP_ABI_VERSION = 1
 PEER_ONE_SHOT, PEER_TWO_SHOT = 1, 2
 ROUTER_ABI_VERSION = 3
 MOE_LAYER_ABI_VERSION = 3
 DECODE_PERSISTENT = 1
 PREFILL_GROUPED = 2
+ERR_NULL, ERR_DESCRIPTOR, ERR_WRONG_ARCH = -1, -2, -120
 EXL3_GATE, EXL3_UP, EXL3_DOWN = 1, 2, 3
 PLANES = {"fc1_output_bf16": 0, "row_token_u32": 1, "row_slot_u32": 2, "row_weight_f32": 3,
           "expert_offsets_u32": 4, "shared_f32": 5, "routed_f32": 6}
@@ -33,6 +35,7 @@ ROUTER_STATIC_SCRATCH_BYTES = 4 << 20
 MOE_ROUTES_GIVEN = 1 << 0
 MOE_SHARED_EXPERT = 1 << 1
 MOE_EXL3_EXPERTS = 1 << 2
+MOE_EXTERNAL_ROUTED = 1 << 3
 
 STATUS_BITS = {
     1 << 0: "route-token-out-of-range",
@@ -130,7 +133,8 @@ class MoeLayerDescriptor(_Desc):
                             "w2_global_f32", "shared13_bf16", "shared2_bf16",
                             "route_experts_u16", "route_weights_f32", "output_f32",
                             "validation_error_u32", "workspace", "workspace_bytes",
-                            "sequence", "exl3_experts")] + [("reserved", u64 * 3)]
+                            "sequence", "exl3_experts", "routed_plane_f32")] + \
+        [("reserved", u64 * 2)]
 
 
 class MoeFinishDescriptor(_Desc):
@@ -156,9 +160,24 @@ class MoeExl3Experts(_Desc):
                             "down_suh_f16", "down_svh_f16")] + [("reserved", u64 * 4)]
 
 
+class MoeEpDescriptor(_Desc):
+    """glmaxx_moe_ep_descriptor (new, expert parallelism), 560 bytes."""
+    _fields_ = [(n, u32) for n in ("abi_version", "struct_bytes", "ranks", "rank", "tokens",
+                                   "hidden", "experts", "top_k", "rows")] + \
+        [("reserved0", u32 * 3)] + \
+        [(n, u64) for n in ("input_bf16", "compacted_tokens_u32", "compacted_experts_u16",
+                            "compacted_slots_u8", "compacted_weights_f32",
+                            "expert_offsets_u32")] + \
+        [(n, u64 * 8) for n in ("recv_x_bf16", "recv_expert_u16", "recv_weight_f32",
+                                "recv_source_u32")] + \
+        [("recv_capacity", u32 * 8), ("dest_row_offset", u32 * 8), ("rows_out_f32", u64),
+         ("planes_f32", u64 * 8), ("plane_tokens", u32 * 8), ("validation_error_u32", u64),
+         ("reserved", u64 * 4)]
+
+
 EXPECTED_SIZES = {Fc1Descriptor: 224, Fc2Descriptor: 224, Exl3Descriptor: 144,
                   RouterDescriptor: 192, MoeLayerDescriptor: 240, MoeExl3Experts: 128,
-                  MoeFinishDescriptor: 112, MoePeerDescriptor: 80}
+                  MoeFinishDescriptor: 112, MoePeerDescriptor: 80, MoeEpDescriptor: 560}
 
 _P = ctypes.c_void_p
 _I32P = ctypes.POINTER(ctypes.c_int32)
@@ -239,6 +258,8 @@ SIGNATURES = {
     "glmaxx_moe_layer_set_stage_events": (ctypes.c_int32, [_U64P, u32]),
     "glmaxx_moe_layer_plane": (ctypes.c_int32, [_P, u32, _U64P, _U64P]),
     "glmaxx_peer_enable": (ctypes.c_int32, [ctypes.c_int32]),
+    "glmaxx_moe_ep_dispatch_launch": (ctypes.c_int32, [_P, _P]),
+    "glmaxx_moe_ep_return_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_nvfp4_codec_selfcheck_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_nvfp4_mma_peak_launch": (ctypes.c_int32, [u32, u32, u32, u32, u32, u32, _P, _P, _P]),
     "glmaxx_nvfp4_pack_launch": (ctypes.c_int32, [u64, ctypes.c_int32, u32, u32, u32, u64, u64,

@@ -136,9 +136,12 @@ class RoutedMoE:
                                          device=self.device)
 
     def _descriptor(self, tokens: int, x: torch.Tensor, out: torch.Tensor,
-                    routes_given: bool, path: int) -> abi.MoeLayerDescriptor:
+                    routes_given: bool, path: int,
+                    external_plane: torch.Tensor | None = None) -> abi.MoeLayerDescriptor:
         c, w = self.cfg, self.w
         flags = (abi.MOE_ROUTES_GIVEN if routes_given else 0)
+        if external_plane is not None:
+            flags |= abi.MOE_EXTERNAL_ROUTED
         if c.shared_intermediate and w.shared13 is not None:
             flags |= abi.MOE_SHARED_EXPERT
         xd = None
@@ -170,7 +173,8 @@ class RoutedMoE:
             shared2_bf16=_ptr(w.shared2), route_experts_u16=self.route_experts.data_ptr(),
             route_weights_f32=self.route_weights.data_ptr(), output_f32=out.data_ptr(),
             validation_error_u32=self.status.data_ptr(), sequence=1,
-            exl3_experts=ctypes.addressof(xd) if xd is not None else 0)
+            exl3_experts=ctypes.addressof(xd) if xd is not None else 0,
+            routed_plane_f32=_ptr(external_plane))
         d._exl3 = xd  # the library reads it through exl3_experts at launch
         need = int(self.lib.glmaxx_moe_layer_workspace_bytes(ctypes.byref(d)))
         key = (tokens, flags, path)
@@ -185,9 +189,14 @@ class RoutedMoE:
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None,
                 routes: tuple[torch.Tensor, torch.Tensor] | None = None,
-                path: int = 0) -> torch.Tensor:
+                path: int = 0, external_plane: torch.Tensor | None = None) -> torch.Tensor:
         """x: [T, H] bf16 -> fp32 rank partial [T, H] (routed + shared).
-        routes: optional (experts [T, K] int16, weights [T, K] f32) to bypass the router."""
+        routes: optional (experts [T, K] int16, weights [T, K] f32) to bypass the router.
+        external_plane: [T, K, H] fp32 routed contributions computed elsewhere (expert
+        parallelism): only the shared expert and the expert-order combine run."""
+        if external_plane is not None:
+            assert routes is not None, "the external plane needs the routes (combine order)"
+            assert external_plane.dtype == torch.float32 and external_plane.is_contiguous()
         assert x.dtype == torch.bfloat16 and x.is_contiguous() and x.shape[1] == self.cfg.hidden
         t = x.shape[0]
         assert t <= self.max_tokens
@@ -196,7 +205,7 @@ class RoutedMoE:
         if routes is not None:
             self.route_experts[:t].copy_(routes[0])
             self.route_weights[:t].copy_(routes[1])
-        d = self._descriptor(t, x, out, routes is not None, path)
+        d = self._descriptor(t, x, out, routes is not None, path, external_plane)
         err = ctypes.c_int32(0)
         abi.check(self.lib.glmaxx_moe_layer_launch(ctypes.byref(d), ctypes.c_void_p(_stream()),
                                                    ctypes.byref(err)), "moe_layer_launch")

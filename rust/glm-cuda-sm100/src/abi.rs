@@ -12,6 +12,7 @@ pub const MOE_LAYER_ABI_VERSION: u32 = 3;
 pub const MOE_EXL3_ABI_VERSION: u32 = 1;
 pub const MOE_FINISH_ABI_VERSION: u32 = 1;
 pub const MOE_PEER_ABI_VERSION: u32 = 1;
+pub const MOE_EP_ABI_VERSION: u32 = 1;
 
 /// `path` of [`MoeLayerDescriptor`]: 0 picks by token count.
 pub const PATH_AUTO: u32 = 0;
@@ -22,6 +23,7 @@ pub const PATH_PREFILL_GROUPED: u32 = 2;
 pub const MOE_ROUTES_GIVEN: u32 = 1 << 0;
 pub const MOE_SHARED_EXPERT: u32 = 1 << 1;
 pub const MOE_EXL3_EXPERTS: u32 = 1 << 2;
+pub const MOE_EXTERNAL_ROUTED: u32 = 1 << 3;
 
 /// `flags` of [`MoePeerDescriptor`].
 pub const MOE_PEER_ONE_SHOT: u32 = 1;
@@ -143,7 +145,10 @@ pub struct MoeLayerDescriptor {
     pub workspace_bytes: u64,
     pub sequence: u64,
     pub exl3_experts: u64,
-    pub reserved: [u64; 3],
+    /// Flag [`MOE_EXTERNAL_ROUTED`]: the `[tokens][top_k][hidden]` fp32 slot plane
+    /// the experts' owner ranks wrote (expert parallelism), else 0.
+    pub routed_plane_f32: u64,
+    pub reserved: [u64; 2],
 }
 
 /// `glmaxx_moe_finish_descriptor` (112 bytes): residual + attention + every
@@ -188,12 +193,47 @@ pub struct MoePeerDescriptor {
     pub reserved: [u64; 3],
 }
 
+/// `glmaxx_moe_ep_descriptor` (560 bytes): the expert-parallel dispatch and
+/// return.  The arrays of 8 hold every rank's buffers in rank order.
+#[repr(C, align(16))]
+#[derive(Clone, Copy, Debug, Default)]
+pub struct MoeEpDescriptor {
+    pub abi_version: u32,
+    pub struct_bytes: u32,
+    pub ranks: u32,
+    pub rank: u32,
+    pub tokens: u32,
+    pub hidden: u32,
+    pub experts: u32,
+    pub top_k: u32,
+    pub rows: u32,
+    pub reserved0: [u32; 3],
+    pub input_bf16: u64,
+    pub compacted_tokens_u32: u64,
+    pub compacted_experts_u16: u64,
+    pub compacted_slots_u8: u64,
+    pub compacted_weights_f32: u64,
+    pub expert_offsets_u32: u64,
+    pub recv_x_bf16: [u64; 8],
+    pub recv_expert_u16: [u64; 8],
+    pub recv_weight_f32: [u64; 8],
+    pub recv_source_u32: [u64; 8],
+    pub recv_capacity: [u32; 8],
+    pub dest_row_offset: [u32; 8],
+    pub rows_out_f32: u64,
+    pub planes_f32: [u64; 8],
+    pub plane_tokens: [u32; 8],
+    pub validation_error_u32: u64,
+    pub reserved: [u64; 4],
+}
+
 // Frozen layouts (the C header static_asserts the same sizes).
 const _: () = assert!(core::mem::size_of::<RouterDescriptor>() == 192);
 const _: () = assert!(core::mem::size_of::<MoeExl3Experts>() == 128);
 const _: () = assert!(core::mem::size_of::<MoeLayerDescriptor>() == 240);
 const _: () = assert!(core::mem::size_of::<MoeFinishDescriptor>() == 112);
 const _: () = assert!(core::mem::size_of::<MoePeerDescriptor>() == 80);
+const _: () = assert!(core::mem::size_of::<MoeEpDescriptor>() == 560);
 const _: () = assert!(core::mem::align_of::<MoeLayerDescriptor>() == 16);
 
 impl RouterDescriptor {
@@ -237,6 +277,17 @@ impl MoeFinishDescriptor {
             abi_version: MOE_FINISH_ABI_VERSION,
             struct_bytes: core::mem::size_of::<Self>() as u32,
             eps: 1e-6,
+            ..Self::default()
+        }
+    }
+}
+
+impl MoeEpDescriptor {
+    #[must_use]
+    pub fn new() -> Self {
+        Self {
+            abi_version: MOE_EP_ABI_VERSION,
+            struct_bytes: core::mem::size_of::<Self>() as u32,
             ..Self::default()
         }
     }

@@ -9,7 +9,7 @@
 use core::ffi::{c_char, c_void};
 
 use crate::abi::{
-    MoeFinishDescriptor, MoeLayerDescriptor, MoePeerDescriptor, RouterDescriptor,
+    MoeEpDescriptor, MoeFinishDescriptor, MoeLayerDescriptor, MoePeerDescriptor, RouterDescriptor,
 };
 
 #[link(name = "glmaxx_sm100")]
@@ -214,6 +214,8 @@ unsafe extern "C" {
         validation_error_u32: u64,
         stream: *mut c_void,
     ) -> i32;
+    pub fn glmaxx_moe_ep_dispatch_launch(descriptor: *const MoeEpDescriptor, stream: *mut c_void) -> i32;
+    pub fn glmaxx_moe_ep_return_launch(descriptor: *const MoeEpDescriptor, stream: *mut c_void) -> i32;
     pub fn glmaxx_nvfp4_codec_selfcheck_launch(result_u64x4: *mut u64, stream: *mut c_void) -> i32;
     pub fn glmaxx_nvfp4_mma_peak_launch(
         n: u32,

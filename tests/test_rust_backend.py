@@ -22,7 +22,8 @@ STRUCTS = {"glmaxx_router_descriptor": "RouterDescriptor",
            "glmaxx_moe_exl3_experts": "MoeExl3Experts",
            "glmaxx_moe_layer_descriptor": "MoeLayerDescriptor",
            "glmaxx_moe_finish_descriptor": "MoeFinishDescriptor",
-           "glmaxx_moe_peer_descriptor": "MoePeerDescriptor"}
+           "glmaxx_moe_peer_descriptor": "MoePeerDescriptor",
+           "glmaxx_moe_ep_descriptor": "MoeEpDescriptor"}
 
 
 def _strip_c(s):
