@@ -96,11 +96,14 @@ struct GemmShape {
                                                       : 512;
   static constexpr int kABytes = 128 * 128;
   static constexpr int kBBytes = NT * 128;
-  // Lane-major scales (128-row N tiles): each operand's scales of a stage are
-  // staged as two 4 KB blocks, one per K-block pair, each [atom kb x4 | atom
-  // kb+1 x4], and reach TMEM with two 128x256b copies instead of four 32x128b
-  // broadcast copies.  A converter warp writes them; the TMA moves A and B only.
-  static constexpr bool kLaneSf = FP4 && NT == 128;
+  // Lane-major scales (128-row N tiles, dual MMAs): each operand's scales of a
+  // stage are staged as two 4 KB blocks, one per K-block pair, each [atom kb x4 |
+  // atom kb+1 x4], and reach TMEM with two 128x256b copies instead of four
+  // 32x128b broadcast copies.  A converter warp writes them; the TMA moves A and B
+  // only.  Measured at T = 8192: FC1 (dual) 1.69 ms lane-major vs 1.85 ms with
+  // broadcast copies of TMA-loaded atoms; the single-MMA FC2 the other way round,
+  // 1.21 vs 1.08 ms, so it takes the atoms.
+  static constexpr bool kLaneSf = FP4 && NT == 128 && DUAL;
   static constexpr int kSfaBytes = FP4 ? (kLaneSf ? 8192 : 2048) : 0;
   static constexpr int kSfbBytes = FP4 ? (kLaneSf ? 8192 : 2048 * kNJ) : 0;
   static constexpr int kStageBytes = kAcc * kABytes + kBBytes + kAcc * kSfaBytes + kSfbBytes;
@@ -115,7 +118,7 @@ struct GemmShape {
 // padded so that the 16-byte row reads of 8 lanes hit distinct banks.
 template <bool FP4, bool DUAL, int NT, int EPI>
 struct EpiTile {
-  static constexpr bool kOn = GemmShape<FP4, DUAL, NT>::kLaneSf && EPI != kEpiStorePartial;
+  static constexpr bool kOn = FP4 && NT == 128 && EPI != kEpiStorePartial;
   static constexpr bool kBf16 = EPI == kEpiSwiGLU;
   static constexpr int kPitch = kBf16 ? 80 : 144;
   static constexpr int kWarpBytes = kOn ? 16 * kPitch : 0;
