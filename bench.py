@@ -88,6 +88,14 @@ def parse():
     # (one kernel per layer over NVLink) or an NCCL all-reduce plus the finish
     p.add_argument("--reduce", choices=["peer", "nccl"], default="peer")
     p.add_argument("--peer-mode", choices=["auto", "one", "two"], default="auto")
+    # N > 1: token-split routing (each rank routes T/N tokens, the routes are
+    # all-gathered) where it pays (tp_route.split_pays), always, or never
+    p.add_argument("--split-route", choices=["auto", "on", "off"], default="auto")
+    # how a prefill-size step combines its routed rows: fp32 atomics into the output
+    # (faster: T=8192 layer 3.91 / 2.68 / 1.97 ms at TP1 / TP2 / TP8 shards against
+    # 4.56 / 3.23 / 2.33 ms), or the slot plane + expert-order combine
+    # (GLMAXX_MOE_DETERMINISTIC, the same bits run after run)
+    p.add_argument("--combine", choices=["atomic", "plane"], default="atomic")
     # --workload load: rank files loaded at once (1, or a TP4 node's 4 on threads)
     p.add_argument("--rank-files", type=int, choices=[1, 4], default=1)
     a = p.parse_args()
@@ -478,6 +486,7 @@ def run_ours(args):
         g = torch.Generator().manual_seed(args.seed * 13 + 1)
         nvfp4_mask = torch.zeros(EXPERTS, dtype=torch.bool)
         nvfp4_mask[torch.randperm(EXPERTS, generator=g)[:HYBRID_NVFP4_EXPERTS]] = True
+    deterministic = args.combine == "plane"
     layers = []
     for li in range(n_layers):
         seed = args.seed + 7919 * li
@@ -488,11 +497,18 @@ def run_ours(args):
                                              nvfp4_experts=nvfp4_mask)
         else:
             w = synth.make_rank_weights(cfg, seed=seed, device=dev, zipf_beta=beta)
-        layers.append(RoutedMoE(cfg, w, T))
+        layers.append(RoutedMoE(cfg, w, T, deterministic=deterministic))
     layer = layers[0]
     weights = layer.w
     x = synth.make_input(T, HIDDEN, seed=args.seed, device=dev)
     use_peer = world > 1 and args.reduce == "peer"
+    from glmaxx_b200 import tp_route
+    split = world > 1 and (args.split_route == "on" or
+                           (args.split_route == "auto" and tp_route.split_pays(T, world)))
+    # token-split routing: each layer's routes land in that layer's own route
+    # buffers, which its forward() then reads in place (routes given)
+    routers = ([tp_route.SplitRouter(cfg, lay.w, T, rank, world, dev, out=lay.routes(T))
+                for lay in layers] if split else None)
     group = None
     if use_peer:
         # every rank maps every rank's partial, output and stacked-layer buffers
@@ -534,7 +550,10 @@ def run_ours(args):
 
     def layer_and_finish(li):
         """layer li, and (stack) the finish that forms layer li+1's bf16 input."""
-        layers[li](xs[li], outs[li])
+        if routers is not None:
+            layers[li](xs[li], outs[li], routes=routers[li](xs[li]))
+        else:
+            layers[li](xs[li], outs[li])
         if use_peer:
             peer_finish(li)
 
@@ -553,6 +572,10 @@ def run_ours(args):
             status = lay.device_status()
             if status:
                 raise RuntimeError(f"device status after warm-up: {status}")
+        for r in routers or []:
+            status = r.device_status()
+            if status:
+                raise RuntimeError(f"token-slice router status after warm-up: {status}")
         if use_peer and int(peer_status.item()):
             raise RuntimeError(f"peer finish status after warm-up: {int(peer_status.item())}")
         # one graph per layer (its routed step; the finish joins it when no collective
@@ -680,7 +703,10 @@ def run_ours(args):
             # a short device spin first, so that every launch of the step is queued
             # before the GPU reaches it and the stage events time the GPU alone
             torch.cuda._sleep(2_000_000)
-            layer(x, out)
+            if routers is not None:
+                layer(x, out, routes=routers[0](x))
+            else:
+                layer(x, out)
             stream.synchronize()
             for i, s in enumerate(abi.LAYER_STAGES):
                 stage_ms[s].append(evs[i].elapsed_time(evs[i + 1]))
@@ -838,8 +864,13 @@ def run_ours(args):
                        "hidden": HIDDEN, "experts": EXPERTS, "top_k": TOPK, "groups": 8,
                        "topk_groups": 4, "intermediate": INTER, "shared_intermediate": INTER,
                        "parallelism": f"tp{world} (expert intermediate sharded, "
-                                      + ("fused peer-memory finish over NVLink)" if use_peer
-                                         else "NCCL all-reduce)"),
+                                      + ("fused peer-memory finish over NVLink" if use_peer
+                                         else "NCCL all-reduce")
+                                      + (", token-split routing + NCCL route all-gather)"
+                                         if split else ")"),
+                       "routed_combine": ("slot plane + expert-order combine"
+                                          if deterministic or T <= 256 or codec is not None
+                                          else "fp32 atomics into the output"),
                        "l2": "weights per step >> 126 MB L2 (no flush needed)",
                        "timing": ("CUDA-graph replay of the layer and its peer finish"
                                   if use_peer else "CUDA-graph replay of the layer"
@@ -859,8 +890,12 @@ def run_ours(args):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        del graph
+        # every CUDA graph that holds an NCCL call (the split router's all-gather)
+        # must be gone before destroy_process_group, or the exit waits for ever
+        del graph, gr
         graphs.clear()
+        import gc
+        gc.collect()
         torch.cuda.synchronize()
         if group is not None:
             outs, out, xs, rs = None, None, None, None

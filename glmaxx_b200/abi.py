@@ -36,6 +36,7 @@ MOE_ROUTES_GIVEN = 1 << 0
 MOE_SHARED_EXPERT = 1 << 1
 MOE_EXL3_EXPERTS = 1 << 2
 MOE_EXTERNAL_ROUTED = 1 << 3
+MOE_DETERMINISTIC = 1 << 4
 
 STATUS_BITS = {
     1 << 0: "route-token-out-of-range",

@@ -86,7 +86,7 @@ struct LayerPlan {
         exl3 ? reinterpret_cast<const glmaxx_moe_exl3_experts*>(d.exl3_experts) : nullptr;
     external = (d.flags & GLMAXX_MOE_EXTERNAL_ROUTED) != 0;
     nvfp4 = !external && (!exl3 || (xe != nullptr && xe->codec_u8 != 0));
-    plane_mode = decode || exl3 || external;
+    plane_mode = decode || exl3 || external || (d.flags & GLMAXX_MOE_DETERMINISTIC) != 0;
     nt = decode ? 32 : 128;
     const uint32_t A = r.A;
     const uint32_t active = A < r.E ? A : r.E;
@@ -136,7 +136,8 @@ bool valid_layer(const glmaxx_moe_layer_descriptor& d) {
   for (uint64_t v : d.reserved)
     if (v) return false;
   if (d.flags & ~uint32_t(GLMAXX_MOE_ROUTES_GIVEN | GLMAXX_MOE_SHARED_EXPERT |
-                          GLMAXX_MOE_EXL3_EXPERTS | GLMAXX_MOE_EXTERNAL_ROUTED))
+                          GLMAXX_MOE_EXL3_EXPERTS | GLMAXX_MOE_EXTERNAL_ROUTED |
+                          GLMAXX_MOE_DETERMINISTIC))
     return false;
   if (d.flags & GLMAXX_MOE_EXTERNAL_ROUTED) {
     if (!(d.flags & GLMAXX_MOE_ROUTES_GIVEN) || (d.flags & GLMAXX_MOE_EXL3_EXPERTS) ||

@@ -32,94 +32,123 @@ namespace glmaxx {
 // Router logits.  Canonical order (shared with the CPU restatement):
 //   logit[t][e] = ((s_0 + s_1) + ...) + s_7,  s_c = fma-chain over the c-th
 //   eighth of H in ascending k from 0.
-// grid (E/32, ceil(T/32), 8), 256 threads: warp w -> experts e0+4w..e0+4w+3,
-// lane -> token t0+lane.  The first kernel of a step also clears the
-// token-in-expert bitmap.
+// Both kernels split the grid's z over the 8 chunks, and the first kernel of a
+// step also clears the token-in-expert bitmap.
 // ---------------------------------------------------------------------------
-// K is staged through shared memory in fp32 sub-tiles of 256 (pitch 260 keeps
-// the 128-bit loads of one warp phase on distinct banks); each thread keeps four
-// independent fma-chains (4 experts of one token) in ascending k.
-constexpr uint32_t kRouterSub = 256;
-constexpr uint32_t kRouterPitch = kRouterSub + 4;
+// Small-T kernel: CTA tile 32 tokens x 32 experts x one K chunk, 8 warps of
+// 16 tokens x 8 experts; lane (tp = lane % 8, ep = lane / 8) of warp w owns
+// tokens tp and tp + 8 and experts ep and ep + 4 of its warp's tile: four
+// independent fma-chains, each in ascending k, two warps per scheduler.
+// K advances in phases of 128 elements.  The kernel is bound by the latency of
+// its global loads unless most of a CTA's 96 KB are in flight at once, so the
+// raw bf16 rows of up to kRbRing phases are requested by cp.async at the start
+// (a ring of phase buffers, refilled kRbRing - 1 phases ahead).  Each phase is
+// then widened to fp32 into one of two compute buffers ([row][k], 528-byte
+// pitch: 16 mod 128, so the 16-byte loads of 8 consecutive rows fall on
+// distinct banks).  Per 4 k a thread loads 4 x 16 bytes for 16 fmas, and a
+// warp's load touches 8 (tokens) or 4 (experts) rows: one wavefront each.
+constexpr uint32_t kRbTile = 32;              // tokens (and experts) per CTA
+constexpr uint32_t kRbThreads = 256;
+constexpr uint32_t kRbPhaseK = 128;           // k per phase
+constexpr uint32_t kRbRows = 2 * kRbTile;     // x rows then w rows
+constexpr uint32_t kRbRing = 6;               // bf16 phase buffers (H = 6144: the whole chunk)
+constexpr uint32_t kRbRawPitch = kRbPhaseK * 2 + 16;       // bytes per bf16 row
+constexpr uint32_t kRbRawBytes = kRbRows * kRbRawPitch;    // one bf16 phase buffer
+constexpr uint32_t kRbPitch = kRbPhaseK + 4;               // floats per fp32 row
+constexpr uint32_t kRbBufFloats = kRbRows * kRbPitch;      // one fp32 compute buffer
+constexpr uint32_t kRbSmem = kRbRing * kRbRawBytes + 2 * kRbBufFloats * 4;
+constexpr uint32_t kRbPieces = kRbRows * kRbPhaseK / 8 / kRbThreads;  // 16-byte pieces per thread
 
-__global__ void __launch_bounds__(256) router_logits_kernel(
+__global__ void __launch_bounds__(kRbThreads) router_logits_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, float* __restrict__ partial,
     uint32_t T, uint32_t H, uint32_t E, uint32_t* __restrict__ bitmap, uint32_t bitmap_words) {
-  extern __shared__ float rsm[];
-  float* xs = rsm;                        // [32 tokens][kRouterPitch]
-  float* ws = rsm + 32 * kRouterPitch;    // [32 experts][kRouterPitch]
-  const uint32_t chunk = H / 8;
-  const uint32_t e0 = blockIdx.x * 32, t0 = blockIdx.y * 32, c = blockIdx.z;
+  extern __shared__ __align__(16) uint8_t rb_smem[];
+  uint8_t* raw = rb_smem;                                              // [kRbRing][rows][pitch]
+  float* fbuf = reinterpret_cast<float*>(rb_smem + kRbRing * kRbRawBytes);  // [2][rows][pitch]
+  const uint32_t chunk = H / 8;  // multiple of 32 (H % 256 == 0)
+  const uint32_t e0 = blockIdx.x * kRbTile, t0 = blockIdx.y * kRbTile, c = blockIdx.z;
   const uint32_t tid = threadIdx.x;
   {
     const uint64_t lin = (uint64_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     const uint64_t nthreads = uint64_t(gridDim.x) * gridDim.y * gridDim.z * blockDim.x;
     for (uint64_t i = lin * blockDim.x + tid; i < bitmap_words; i += nthreads) bitmap[i] = 0;
   }
-  const uint32_t warp = tid >> 5, lane = tid & 31;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  // Sub-tile fills are software-pipelined: the global loads of sub-tile s+1 are
-  // in flight while sub-tile s is computed.  Thread tid owns pieces tid + 256i
-  // (i < 4) of 16 bytes: row p / 32, columns (p % 32) * 8 .. +8.
-  uint4 rx[4], rw[4];
-  auto gload = [&](uint32_t k0) {
+  const uint32_t phases = (chunk + kRbPhaseK - 1) / kRbPhaseK;
+  // piece i of a phase: row i / 16 (x rows 0..31, then w rows), k 8 * (i % 16);
+  // rows past T or E, and k past the chunk, are zero
+  auto fill = [&](uint32_t p) {
+    if (p < phases) {
+      uint8_t* buf = raw + (p % kRbRing) * kRbRawBytes;
+      const uint32_t k0 = p * kRbPhaseK;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
-      const uint64_t col = uint64_t(c) * chunk + k0 + kk;
-      const bool in_k = k0 + kk < chunk;
-      rx[i] = (in_k && t0 + r < T) ? *reinterpret_cast<const uint4*>(x + uint64_t(t0 + r) * H + col)
-                                   : make_uint4(0, 0, 0, 0);
-      rw[i] = (in_k && e0 + r < E) ? *reinterpret_cast<const uint4*>(w + uint64_t(e0 + r) * H + col)
-                                   : make_uint4(0, 0, 0, 0);
-    }
-  };
-  auto sstore = [&]() {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t p = tid + 256u * i, r = p >> 5, kk = (p & 31) * 8;
-      const uint32_t xw[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
-      const uint32_t wwv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
-      float4* xd = reinterpret_cast<float4*>(xs + r * kRouterPitch + kk);
-      float4* wd = reinterpret_cast<float4*>(ws + r * kRouterPitch + kk);
-      xd[0] = make_float4(__uint_as_float(xw[0] << 16), __uint_as_float(xw[0] & 0xffff0000u),
-                          __uint_as_float(xw[1] << 16), __uint_as_float(xw[1] & 0xffff0000u));
-      xd[1] = make_float4(__uint_as_float(xw[2] << 16), __uint_as_float(xw[2] & 0xffff0000u),
-                          __uint_as_float(xw[3] << 16), __uint_as_float(xw[3] & 0xffff0000u));
-      wd[0] = make_float4(__uint_as_float(wwv[0] << 16), __uint_as_float(wwv[0] & 0xffff0000u),
-                          __uint_as_float(wwv[1] << 16), __uint_as_float(wwv[1] & 0xffff0000u));
-      wd[1] = make_float4(__uint_as_float(wwv[2] << 16), __uint_as_float(wwv[2] & 0xffff0000u),
-                          __uint_as_float(wwv[3] << 16), __uint_as_float(wwv[3] & 0xffff0000u));
-    }
-  };
-  gload(0);
-  for (uint32_t k0 = 0; k0 < chunk; k0 += kRouterSub) {
-    const uint32_t kn = min(kRouterSub, chunk - k0);  // multiple of 8 (H % 256 == 0)
-    __syncthreads();
-    sstore();
-    __syncthreads();
-    if (k0 + kRouterSub < chunk) gload(k0 + kRouterSub);
-    const float* xr = xs + lane * kRouterPitch;
-    const float* wr = ws + (warp * 4) * kRouterPitch;
-#pragma unroll 2
-    for (uint32_t k = 0; k < kn; k += 4) {
-      const float4 xv = *reinterpret_cast<const float4*>(xr + k);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 wv = *reinterpret_cast<const float4*>(wr + j * kRouterPitch + k);
-        acc[j] = fmaf(xv.x, wv.x, acc[j]);
-        acc[j] = fmaf(xv.y, wv.y, acc[j]);
-        acc[j] = fmaf(xv.z, wv.z, acc[j]);
-        acc[j] = fmaf(xv.w, wv.w, acc[j]);
+      for (int j = 0; j < int(kRbPieces); ++j) {
+        const uint32_t i = tid + kRbThreads * j, r = i / 16, kk = (i % 16) * 8;
+        const bool is_x = r < kRbTile;
+        const uint32_t row = (is_x ? t0 : e0) + (r % kRbTile);
+        uint8_t* dst = buf + r * kRbRawPitch + kk * 2;
+        if (row < (is_x ? T : E) && k0 + kk < chunk)
+          cp_async_16(dst, (is_x ? x : w) + uint64_t(row) * H + uint64_t(c) * chunk + k0 + kk);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
       }
     }
-  }
-  const uint32_t t = t0 + lane;
-  if (t < T) {
+    cp_async_commit();  // one group per phase slot, empty past the last phase
+  };
+  auto widen = [&](uint32_t p) {
+    const uint8_t* src = raw + (p % kRbRing) * kRbRawBytes;
+    float* dst = fbuf + (p & 1) * kRbBufFloats;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t e = e0 + warp * 4 + j;
-      if (e < E) partial[(uint64_t(c) * T + t) * E + e] = acc[j];
+    for (int j = 0; j < int(kRbPieces); ++j) {
+      const uint32_t i = tid + kRbThreads * j, r = i / 16, kk = (i % 16) * 8;
+      const uint4 u = *reinterpret_cast<const uint4*>(src + r * kRbRawPitch + kk * 2);
+      const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+      float4* d = reinterpret_cast<float4*>(dst + r * kRbPitch + kk);
+      d[0] = make_float4(__uint_as_float(v[0] << 16), __uint_as_float(v[0] & 0xffff0000u),
+                         __uint_as_float(v[1] << 16), __uint_as_float(v[1] & 0xffff0000u));
+      d[1] = make_float4(__uint_as_float(v[2] << 16), __uint_as_float(v[2] & 0xffff0000u),
+                         __uint_as_float(v[3] << 16), __uint_as_float(v[3] & 0xffff0000u));
+    }
+  };
+  for (uint32_t p = 0; p + 1 < kRbRing; ++p) fill(p);
+  const uint32_t warp = tid >> 5, lane = tid & 31;
+  const uint32_t tp = lane & 7, ep = lane >> 3;
+  const uint32_t xrow = (warp & 1) * 16 + tp;             // and xrow + 8
+  const uint32_t wrow = kRbTile + (warp >> 1) * 8 + ep;   // and wrow + 4
+  float acc[2][2] = {};
+  for (uint32_t p = 0; p < phases; ++p) {
+    cp_async_wait<kRbRing - 2>();  // phase p has landed (this thread's copies)
+    __syncthreads();               // ... everyone's; phase p - 1's raw buffer is widened
+    fill(p + kRbRing - 1);         // into the raw buffer of phase p - 1
+    widen(p);
+    __syncthreads();
+    const float* buf = fbuf + (p & 1) * kRbBufFloats;
+    const float* xr = buf + xrow * kRbPitch;
+    const float* wr = buf + wrow * kRbPitch;
+    const uint32_t kn = min(kRbPhaseK, chunk - p * kRbPhaseK);
+#pragma unroll 4
+    for (uint32_t k = 0; k < kn; k += 4) {
+      const float4 xa = *reinterpret_cast<const float4*>(xr + k);
+      const float4 xb = *reinterpret_cast<const float4*>(xr + 8 * kRbPitch + k);
+      const float4 wa = *reinterpret_cast<const float4*>(wr + k);
+      const float4 wb = *reinterpret_cast<const float4*>(wr + 4 * kRbPitch + k);
+      const float xv[2][4] = {{xa.x, xa.y, xa.z, xa.w}, {xb.x, xb.y, xb.z, xb.w}};
+      const float wv[2][4] = {{wa.x, wa.y, wa.z, wa.w}, {wb.x, wb.y, wb.z, wb.w}};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) acc[i][j] = fmaf(xv[i][q], wv[j][q], acc[i][j]);
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t t = t0 + xrow + 8 * i;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t e = e0 + (wrow - kRbTile) + 4 * j;
+      if (t < T && e < E) partial[(uint64_t(c) * T + t) * E + e] = acc[i][j];
     }
   }
 }
@@ -1175,14 +1204,13 @@ __global__ void pack_encode_kernel(const void* __restrict__ src, int src_bf16, u
 cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* partial, uint32_t T,
                                  uint32_t H, uint32_t E, uint32_t* bitmap, uint32_t bitmap_words,
                                  cudaStream_t stream) {
-  const size_t smem = 2ull * 32 * kRouterPitch * 4;
   static bool configured[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
     cudaError_t st = cudaFuncSetAttribute(router_logits_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(smem));
+                                          static_cast<int>(kRbSmem));
     if (st != cudaSuccess) return st;
     configured[dev] = true;
   }
@@ -1201,8 +1229,9 @@ cudaError_t launch_router_logits(const uint16_t* x, const uint16_t* w, float* pa
                                                              bitmap_words);
     return cudaPeekAtLastError();
   }
-  dim3 grid((E + 31) / 32, (T + 31) / 32, 8);
-  router_logits_kernel<<<grid, 256, smem, stream>>>(x, w, partial, T, H, E, bitmap, bitmap_words);
+  dim3 grid((E + kRbTile - 1) / kRbTile, (T + kRbTile - 1) / kRbTile, 8);
+  router_logits_kernel<<<grid, kRbThreads, kRbSmem, stream>>>(x, w, partial, T, H, E, bitmap,
+                                                             bitmap_words);
   return cudaPeekAtLastError();
 }
 

@@ -122,8 +122,12 @@ class RoutedMoE:
     weighted combine, shared expert) for up to ``max_tokens`` tokens."""
 
     def __init__(self, cfg: MoEConfig, weights: RankWeights, max_tokens: int,
-                 device: torch.device | None = None):
+                 device: torch.device | None = None, deterministic: bool = False):
+        """deterministic: GLMAXX_MOE_DETERMINISTIC -- prefill-size steps combine the
+        routed rows through the slot plane in expert order (bit-reproducible)
+        instead of fp32 atomics."""
         self.cfg = cfg
+        self.deterministic = deterministic
         self.w = weights
         self.device = device or weights.router_weight.device
         self.lib = abi.load()
@@ -142,6 +146,8 @@ class RoutedMoE:
         flags = (abi.MOE_ROUTES_GIVEN if routes_given else 0)
         if external_plane is not None:
             flags |= abi.MOE_EXTERNAL_ROUTED
+        if self.deterministic:
+            flags |= abi.MOE_DETERMINISTIC
         if c.shared_intermediate and w.shared13 is not None:
             flags |= abi.MOE_SHARED_EXPERT
         xd = None
@@ -203,8 +209,11 @@ class RoutedMoE:
         if out is None:
             out = torch.empty((t, self.cfg.hidden), dtype=torch.float32, device=self.device)
         if routes is not None:
-            self.route_experts[:t].copy_(routes[0])
-            self.route_weights[:t].copy_(routes[1])
+            # routes already in this layer's own buffers (a SplitRouter's output) are read in place
+            if routes[0].data_ptr() != self.route_experts.data_ptr():
+                self.route_experts[:t].copy_(routes[0])
+            if routes[1].data_ptr() != self.route_weights.data_ptr():
+                self.route_weights[:t].copy_(routes[1])
         d = self._descriptor(t, x, out, routes is not None, path, external_plane)
         err = ctypes.c_int32(0)
         abi.check(self.lib.glmaxx_moe_layer_launch(ctypes.byref(d), ctypes.c_void_p(_stream()),

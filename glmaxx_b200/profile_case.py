@@ -32,6 +32,10 @@ def main():
     p.add_argument("--shared", type=int, default=2048)
     p.add_argument("--seed", type=int, default=7)
     p.add_argument("--codec", choices=["nvfp4", "exl3", "hybrid"], default="nvfp4")
+    # the layer flag GLMAXX_MOE_DETERMINISTIC (slot plane + expert-order combine)
+    p.add_argument("--deterministic", action="store_true")
+    # after the steps, time this many more (CUDA events on the launch stream)
+    p.add_argument("--time", type=int, default=0)
     a = p.parse_args()
     groups = 8 if a.experts % 8 == 0 and a.experts >= 64 else 1
     cfg = MoEConfig(experts=a.experts, groups=groups, topk_groups=min(4, groups),
@@ -47,17 +51,26 @@ def main():
             mask[torch.randperm(a.experts, generator=g)[:a.experts // 4]] = True
         w = synth.make_exl3_rank_weights(cfg, seed=a.seed, device=dev, nvfp4_experts=mask)
     x = synth.make_input(a.tokens, cfg.hidden, seed=a.seed, device=dev)
-    layer = RoutedMoE(cfg, w, a.tokens)
+    layer = RoutedMoE(cfg, w, a.tokens, deterministic=a.deterministic)
     out = torch.empty((a.tokens, cfg.hidden), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream()
+    ms = None
     with torch.cuda.stream(stream):
         for _ in range(a.steps):
             layer(x, out, path=a.path)
+        if a.time:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(a.time):
+                layer(x, out, path=a.path)
+            e1.record(stream)
     torch.cuda.synchronize()
+    if a.time:
+        ms = e0.elapsed_time(e1) / a.time
     status = layer.device_status()
     touched = int(torch.unique(layer.routes(a.tokens)[0].long()).numel())
     print(json.dumps({"experts": a.experts, "tokens": a.tokens, "tp": a.tp, "steps": a.steps,
-                      "codec": a.codec,
+                      "codec": a.codec, "deterministic": a.deterministic, "ms_per_step": ms,
                       "touched_experts": touched, "status": status,
                       "abi": abi.abi_string()}))
     if status:

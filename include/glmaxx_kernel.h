@@ -88,6 +88,13 @@ enum {
    * the shared expert and the deterministic expert-order combine only.  Needs
    * GLMAXX_MOE_ROUTES_GIVEN (route_experts_u16 orders the combine). */
   GLMAXX_MOE_EXTERNAL_ROUTED = 1u << 3,
+  /* routed contributions go through the per-slot plane and the expert-order
+   * combine at every token count (decode and EXL3 layers always do), so the
+   * step's output is the same bits run after run; without it, prefill-size
+   * steps (more than 256 tokens) add each routed row into the output with fp32
+   * atomics, whose order varies.  The plane takes tokens x top_k x hidden x 4
+   * bytes of workspace (glmaxx_moe_layer_workspace_bytes counts it). */
+  GLMAXX_MOE_DETERMINISTIC = 1u << 4,
 };
 
 /* glmaxx_kernel.h:22-57 (unchanged layout). */

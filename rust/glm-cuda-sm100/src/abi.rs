@@ -24,6 +24,9 @@ pub const MOE_ROUTES_GIVEN: u32 = 1 << 0;
 pub const MOE_SHARED_EXPERT: u32 = 1 << 1;
 pub const MOE_EXL3_EXPERTS: u32 = 1 << 2;
 pub const MOE_EXTERNAL_ROUTED: u32 = 1 << 3;
+/// Routed contributions through the per-slot plane and the expert-order combine
+/// at every token count (bit-reproducible prefill).
+pub const MOE_DETERMINISTIC: u32 = 1 << 4;
 
 /// `flags` of [`MoePeerDescriptor`].
 pub const MOE_PEER_ONE_SHOT: u32 = 1;

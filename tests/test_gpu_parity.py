@@ -280,6 +280,30 @@ def test_gpu_layer_deterministic_decode():
         assert torch.equal(o, outs[0])
 
 
+def test_gpu_layer_prefill_deterministic_flag():
+    """GLMAXX_MOE_DETERMINISTIC on a prefill-size step (T=1024, TP2 shard): the
+    routed rows go through the slot plane and the expert-order combine, so five
+    runs give the same bits; the output is within the layer tolerance of the
+    oracle on a token subset, and within fp32 reassociation of the atomic path."""
+    cfg = MoEConfig(tp=2, rank=0)
+    dev = cuda()
+    T = 1024
+    w = synth.make_rank_weights(cfg, seed=6, device=dev)
+    x = synth.make_input(T, cfg.hidden, seed=6, device=dev)
+    det = RoutedMoE(cfg, w, T, deterministic=True)
+    outs = [det(x, path=abi.PREFILL_GROUPED).clone() for _ in range(5)]
+    torch.cuda.synchronize()
+    assert det.device_status() == []
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    subset = np.arange(3, T, 41, dtype=np.uint32)
+    ref = _oracle_layer(det, x, cfg, subset=subset)
+    assert_layer_close(outs[0].cpu().numpy()[subset], ref, "deterministic prefill subset")
+    atomic = RoutedMoE(cfg, w, T)(x, path=abi.PREFILL_GROUPED)
+    torch.cuda.synchronize()
+    assert rel_l2(outs[0].cpu().numpy(), atomic.cpu().numpy()) < 1e-5
+
+
 @pytest.mark.parametrize("path,T", [(abi.DECODE_PERSISTENT, 64), (abi.PREFILL_GROUPED, 512)])
 def test_gpu_layer_in_cuda_graph_matches_eager(path, T):
     """The shared expert runs on a side stream forked from the launch stream and
