@@ -70,8 +70,43 @@ CPU_PREFILL_SAMPLE_TOKENS = 512
 # the host's available memory, else rebuilt (untimed) every step
 CPU_HOLD_FRACTION = 0.6
 REF_TIME_BUDGET_S = 120.0
-# measured peer copy over NVLink 5 on this pool, per direction per GPU
+# Peer copy over NVLink 5, per direction per GPU: measured live by every
+# multi-GPU run with the peer finish (peer_copy_gbs); this earlier measurement on
+# the same pool is the denominator only where no live number exists (the NCCL
+# reduce mode).
 NVLINK_PEER_GBS = 770.0
+PEER_PROBE_BYTES = 64 << 20
+
+
+def peer_copy_gbs(group, dev, stream, reps: int = 10) -> float:
+    """Per-direction NVLink copy bandwidth of this box, measured now: every rank
+    copies PEER_PROBE_BYTES from its own probe buffer into its right neighbour's
+    (cudaMemcpyAsync through the peer mapping; all ranks at once, so every GPU
+    sends and receives at the same time), CUDA events around `reps` copies,
+    the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+
+    from glmaxx_b200.peer import device_view
+    half = PEER_PROBE_BYTES
+    local = group.tensor("probe")                  # [2 * half] bytes: send half, receive half
+    right = (group.rank + 1) % group.ranks
+    dst = device_view(group.pointer("probe", right) + half, (half,), torch.uint8, dev)
+    src = local[:half]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        dst.copy_(src, non_blocking=True)
+        stream.synchronize()
+        dist.barrier()
+        e0.record(stream)
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return half / (float(t.item()) * 1e-3) / 1e9
 
 
 def parse():
@@ -513,7 +548,8 @@ def run_ours(args):
     if use_peer:
         # every rank maps every rank's partial, output and stacked-layer buffers
         from glmaxx_b200.peer import PeerGroup
-        bufs = {"partial": ((T, HIDDEN), torch.float32), "out": ((T, HIDDEN), torch.float32)}
+        bufs = {"partial": ((T, HIDDEN), torch.float32), "out": ((T, HIDDEN), torch.float32),
+                "probe": ((2 * PEER_PROBE_BYTES,), torch.uint8)}
         for li in range(1, n_layers):
             bufs[f"rs{li}"] = ((T, HIDDEN), torch.bfloat16)
             bufs[f"xs{li}"] = ((T, HIDDEN), torch.bfloat16)
@@ -677,15 +713,19 @@ def run_ours(args):
         if mode == "auto":
             mode = "two" if two_shot_pays(T * HIDDEN, world) else "one"
         busbw = 2 * (world - 1) / world * S / (red_ms * 1e-3) / 1e9
+        peer_gbs = peer_copy_gbs(group, dev, stream) if use_peer else NVLINK_PEER_GBS
         reduce_info = {
             "kind": f"peer {mode}-shot (fused finish kernel)" if use_peer else "NCCL all-reduce",
             "us_per_launch": red_ms * 1e3, "bytes": S,
             "nvlink_bytes_per_rank": ((world - 1) * S if use_peer and mode == "one"
                                       else 2 * (world - 1) * S // world),
-            "busbw_gbs": busbw, "peak_gbs": NVLINK_PEER_GBS,
-            "frac": busbw / 2 / NVLINK_PEER_GBS,
+            "busbw_gbs": busbw, "peak_gbs": peer_gbs,
+            "peak_kind": ("peer copy measured in this run (every rank into its right "
+                          "neighbour at once, 64 MiB, max over ranks)" if use_peer else
+                          "earlier peer-copy measurement on this pool"),
+            "frac": busbw / 2 / peer_gbs,
             "note": "busbw = 2(N-1)/N x bytes / time (the all-reduce convention); frac = the "
-                    "per-direction (N-1)/N x bytes / time against the measured 770 GB/s peer copy"}
+                    "per-direction (N-1)/N x bytes / time against the peer copy rate"}
         if use_peer and int(peer_status.item()):
             raise RuntimeError(f"peer finish status: {int(peer_status.item())}")
 

@@ -125,12 +125,15 @@ __global__ void __launch_bounds__(kRbThreads) router_logits_kernel(
     const float* xr = buf + xrow * kRbPitch;
     const float* wr = buf + wrow * kRbPitch;
     const uint32_t kn = min(kRbPhaseK, chunk - p * kRbPhaseK);
+    // operands of step k + 4 are loaded before the fmas of step k (the fmas
+    // otherwise wait on the shared-memory loads they follow)
+    auto ld = [](const float* q) { return *reinterpret_cast<const float4*>(q); };
+    float4 xa = ld(xr), xb = ld(xr + 8 * kRbPitch), wa = ld(wr), wb = ld(wr + 4 * kRbPitch);
 #pragma unroll 4
     for (uint32_t k = 0; k < kn; k += 4) {
-      const float4 xa = *reinterpret_cast<const float4*>(xr + k);
-      const float4 xb = *reinterpret_cast<const float4*>(xr + 8 * kRbPitch + k);
-      const float4 wa = *reinterpret_cast<const float4*>(wr + k);
-      const float4 wb = *reinterpret_cast<const float4*>(wr + 4 * kRbPitch + k);
+      const uint32_t kk = k + 4 < kn ? k + 4 : k;
+      const float4 nxa = ld(xr + kk), nxb = ld(xr + 8 * kRbPitch + kk);
+      const float4 nwa = ld(wr + kk), nwb = ld(wr + 4 * kRbPitch + kk);
       const float xv[2][4] = {{xa.x, xa.y, xa.z, xa.w}, {xb.x, xb.y, xb.z, xb.w}};
       const float wv[2][4] = {{wa.x, wa.y, wa.z, wa.w}, {wb.x, wb.y, wb.z, wb.w}};
 #pragma unroll
@@ -139,6 +142,10 @@ __global__ void __launch_bounds__(kRbThreads) router_logits_kernel(
         for (int i = 0; i < 2; ++i)
 #pragma unroll
           for (int j = 0; j < 2; ++j) acc[i][j] = fmaf(xv[i][q], wv[j][q], acc[i][j]);
+      xa = nxa;
+      xb = nxb;
+      wa = nwa;
+      wb = nwb;
     }
   }
   cp_async_wait<0>();

@@ -1,4 +1,5 @@
-"""Reduce-alone timing of the peer finish against NCCL, one process per GPU.
+"""Measurement harness, not library API: reduce-alone timing of the peer finish
+against NCCL, one process per GPU.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N \\
         --master-addr 127.0.0.1 --master-port 29541 -m glmaxx_b200.peer_bench [--tokens 64,2048]

@@ -1,4 +1,5 @@
-"""Run a few routed-MoE layer steps of a chosen shape (the target of ncu captures).
+"""Measurement harness, not library API: run a few routed-MoE layer steps of a
+chosen shape (the target of ncu captures and single-GPU A/B timings).
 
     python -m glmaxx_b200.profile_case --experts 64 --tokens 64 --steps 3 [--tp 1] [--path 1]
         [--codec nvfp4|exl3|hybrid]
