@@ -713,7 +713,12 @@ def run_ours(args):
         if mode == "auto":
             mode = "two" if two_shot_pays(T * HIDDEN, world) else "one"
         busbw = 2 * (world - 1) / world * S / (red_ms * 1e-3) / 1e9
-        peer_gbs = peer_copy_gbs(group, dev, stream) if use_peer else NVLINK_PEER_GBS
+        peer_gbs, peer_live = NVLINK_PEER_GBS, False
+        if use_peer:
+            try:
+                peer_gbs, peer_live = peer_copy_gbs(group, dev, stream), True
+            except Exception as exc:  # noqa: BLE001 -- same failure on every rank
+                print(f"peer copy probe failed: {exc!r}", file=sys.stderr)
         reduce_info = {
             "kind": f"peer {mode}-shot (fused finish kernel)" if use_peer else "NCCL all-reduce",
             "us_per_launch": red_ms * 1e3, "bytes": S,
@@ -721,7 +726,7 @@ def run_ours(args):
                                       else 2 * (world - 1) * S // world),
             "busbw_gbs": busbw, "peak_gbs": peer_gbs,
             "peak_kind": ("peer copy measured in this run (every rank into its right "
-                          "neighbour at once, 64 MiB, max over ranks)" if use_peer else
+                          "neighbour at once, 64 MiB, max over ranks)" if peer_live else
                           "earlier peer-copy measurement on this pool"),
             "frac": busbw / 2 / peer_gbs,
             "note": "busbw = 2(N-1)/N x bytes / time (the all-reduce convention); frac = the "
@@ -941,6 +946,12 @@ def run_ours(args):
             outs, out, xs, rs = None, None, None, None
             group.close()
         dist.barrier()
+        if routers is not None:
+            # the NCCL communicator was used inside captured graphs: end the process
+            # once every rank is past the barrier, without waiting on its teardown
+            sys.stdout.flush()
+            sys.stderr.flush()
+            os._exit(0)
         dist.destroy_process_group()
 
 

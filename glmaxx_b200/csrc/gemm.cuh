@@ -537,25 +537,32 @@ __global__ void __launch_bounds__(GemmShape<FP4, DUAL, NT>::kThreads, 1)
                   *reinterpret_cast<uint32_t*>(tb + jj * ET::kPitch + 4 * lane) = v;
               }
               __syncwarp();
-              const uint32_t jj = lane & 15, half = lane >> 4;
-              const uint32_t rd = __shfl_sync(0xffffffffu, src_d, 16 * hf + jj);
-              if (ch * 32 + 16 * hf + jj < t.rows) {
-                const uint8_t* rowp = tb + jj * ET::kPitch;
-                if (ET::kBf16) {
+              if (ET::kBf16) {
+                const uint32_t jj = lane & 15, half = lane >> 4;
+                const uint32_t rd = __shfl_sync(0xffffffffu, src_d, 16 * hf + jj);
+                if (ch * 32 + 16 * hf + jj < t.rows) {
+                  const uint8_t* rowp = tb + jj * ET::kPitch;
                   uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(args.out) +
                                                       uint64_t(rd) * args.ldo + colbase + half * 16);
                   o[0] = *reinterpret_cast<const uint4*>(rowp + half * 32);
                   o[1] = *reinterpret_cast<const uint4*>(rowp + half * 32 + 16);
-                } else {
-                  float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo + colbase +
-                             half * 16;
+                }
+              } else {
+                // fp32 rows: each instruction covers 4 token rows, 8 lanes per row
+                // writing its 32 columns as one whole 128-byte line (the vector
+                // atomics then fill whole L2 sectors)
 #pragma unroll
-                  for (int q = 0; q < 4; ++q) {
-                    const float4 f = *reinterpret_cast<const float4*>(rowp + half * 64 + 16 * q);
+                for (int q = 0; q < 4; ++q) {
+                  const uint32_t jj = 4 * q + (lane >> 3), c4 = (lane & 7) * 4;
+                  const uint32_t rd = __shfl_sync(0xffffffffu, src_d, 16 * hf + jj);
+                  if (ch * 32 + 16 * hf + jj < t.rows) {
+                    const float4 f = *reinterpret_cast<const float4*>(tb + jj * ET::kPitch + 4 * c4);
+                    float* o = reinterpret_cast<float*>(args.out) + uint64_t(rd) * args.ldo +
+                               colbase + c4;
                     if (EPI == kEpiRoutedAtomic)
-                      red_add_v4(o + 4 * q, f);
+                      red_add_v4(o, f);
                     else
-                      *reinterpret_cast<float4*>(o + 4 * q) = f;
+                      *reinterpret_cast<float4*>(o) = f;
                   }
                 }
               }
