@@ -22,6 +22,16 @@ namespace glmaxx {
 namespace {
 
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+// the two fp16 halves of a 32-bit word (low half = the lower k)
+__device__ __forceinline__ void exl3_halves(uint32_t v, uint16_t& lo, uint16_t& hi) {
+  asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(v));
+}
+// c + a*b in fp32 with one rounding, a and b fp16
+__device__ __forceinline__ float exl3_fma_f16(uint16_t a, uint16_t b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
 
@@ -52,7 +62,11 @@ __global__ void exl3_rotate_in(const uint16_t* __restrict__ x, const uint16_t* _
 // Decode-fused EXL3 GEMV/GEMM: P[row][n] = f16( sum_k x[row][k] * W[k][n] ) with
 // the reference's arithmetic (exl3.rs:404-453: fp32, multiply then add, k
 // ascending from 0, one chain per output), so results are bit-identical to
-// the CPU definition.  One warp owns 32 output columns (two 16x16 trellis tile
+// the CPU definition.  x and W are fp16, so every product x*w is exact in fp32
+// (11 x 11 significant bits, exponents far inside fp32's range): rounding it
+// is the identity, and round(round(x*w) + acc) = round(x*w + acc), one fused
+// multiply-add.  The fma takes the fp16 factors as they are
+// (fma.rn.f32.f16), so neither x nor the weights are widened first.  One warp owns 32 output columns (two 16x16 trellis tile
 // columns); every 16 k it decodes its two tiles cooperatively -- lane l holds
 // weights l*8 .. l*8+7 of a tile's 256-weight circular bitstream, the 4x2
 // block (k, n) = (2(l&3) + (w&1) + 8((w>>1)&1), 2((l>>3)&3) + ((l>>2)&1) +
@@ -82,7 +96,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
   // of a warp on distinct banks
   constexpr int kPitch = 40;
   __shared__ __align__(16) uint16_t ws[32 * kPitch];
-  __shared__ __align__(16) float xs[RB][kExl3KChunk];    // x of this item's rows
+  __shared__ __align__(16) uint16_t xs[RB][kExl3KChunk]; // x of this item's rows (fp16)
   const uint32_t lane = threadIdx.x;
   const Exl3LaneWindow lw = exl3_lane_window(lane);
   const uint32_t c0 = blockIdx.x * 32;                   // first column of this warp
@@ -106,7 +120,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
       __syncwarp();
       for (uint32_t i = lane; i < nr * kExl3KChunk; i += 32) {  // only this item's rows
         const uint32_t r = i / kExl3KChunk, k = i % kExl3KChunk;
-        xs[r][k] = k < kn ? h2f(a.x[uint64_t(r0 + r) * a.K + kc + k]) : 0.f;
+        xs[r][k] = k < kn ? a.x[uint64_t(r0 + r) * a.K + kc + k] : uint16_t(0);
       }
       __syncwarp();
       uint32_t span[2][3];
@@ -137,33 +151,21 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
         const uint4 c01 = *reinterpret_cast<const uint4*>(&ws[lane * kPitch]);
         const uint4 c23 = *reinterpret_cast<const uint4*>(&ws[lane * kPitch + 8]);
         const uint32_t cw[8] = {c01.x, c01.y, c01.z, c01.w, c23.x, c23.y, c23.z, c23.w};
-        float wf[16];
+        uint16_t wl[8], wh[8];  // weights k16 + 2q (low half) and k16 + 2q + 1 (high half)
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          wf[2 * q] = h2f(uint16_t(cw[q] & 0xffffu));
-          wf[2 * q + 1] = h2f(uint16_t(cw[q] >> 16));
-        }
-        if (RB == 1 || nr == 1) {
+        for (int q = 0; q < 8; ++q) exl3_halves(cw[q], wl[q], wh[q]);
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const float4 xv = *reinterpret_cast<const float4*>(&xs[0][k16 + 4 * k4]);
-            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.x, wf[4 * k4]));
-            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.y, wf[4 * k4 + 1]));
-            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.z, wf[4 * k4 + 2]));
-            acc[0] = __fadd_rn(acc[0], __fmul_rn(xv.w, wf[4 * k4 + 3]));
-          }
-        } else {
+        for (int r = 0; r < RB; ++r) {
+          if (r >= static_cast<int>(nr)) break;  // nr is the same for the whole warp
+          const uint4 x01 = *reinterpret_cast<const uint4*>(&xs[r][k16]);
+          const uint4 x23 = *reinterpret_cast<const uint4*>(&xs[r][k16 + 8]);
+          const uint32_t xw[8] = {x01.x, x01.y, x01.z, x01.w, x23.x, x23.y, x23.z, x23.w};
 #pragma unroll
-          for (int r = 0; r < RB; ++r) {
-            if (r >= static_cast<int>(nr)) break;  // nr is the same for the whole warp
-#pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4) {
-              const float4 xv = *reinterpret_cast<const float4*>(&xs[r][k16 + 4 * k4]);
-              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.x, wf[4 * k4]));
-              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.y, wf[4 * k4 + 1]));
-              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.z, wf[4 * k4 + 2]));
-              acc[r] = __fadd_rn(acc[r], __fmul_rn(xv.w, wf[4 * k4 + 3]));
-            }
+          for (int q = 0; q < 8; ++q) {
+            uint16_t xl, xh;
+            exl3_halves(xw[q], xl, xh);
+            acc[r] = exl3_fma_f16(xl, wl[q], acc[r]);
+            acc[r] = exl3_fma_f16(xh, wh[q], acc[r]);
           }
         }
         __syncwarp();
