@@ -131,6 +131,9 @@ def parse():
     # 4.56 / 3.23 / 2.33 ms), or the slot plane + expert-order combine
     # (GLMAXX_MOE_DETERMINISTIC, the same bits run after run)
     p.add_argument("--combine", choices=["atomic", "plane"], default="atomic")
+    # N > 1, one layer: run the step as this many token chunks, each chunk's peer
+    # finish (reduce) on a second stream overlapping the next chunk's layer
+    p.add_argument("--chunks", type=int, default=1)
     # --workload load: rank files loaded at once (1, or a TP4 node's 4 on threads)
     p.add_argument("--rank-files", type=int, choices=[1, 4], default=1)
     a = p.parse_args()
@@ -584,8 +587,38 @@ def run_ours(args):
         else:
             group.finish("partial", out_f32="out", mode=args.peer_mode, status=peer_status)
 
+    chunks = args.chunks if (use_peer and n_layers == 1 and args.chunks > 1
+                             and T % args.chunks == 0) else 1
+    fin_stream = torch.cuda.Stream(device=dev) if chunks > 1 else None
+    chunk_done = [torch.cuda.Event() for _ in range(chunks)]
+    fin_done = torch.cuda.Event()
+
+    def chunked_layer_and_finish(li):
+        """The step as token chunks: chunk c's layer on the launch stream, then its
+        rows' peer finish on fin_stream, overlapping chunk c+1's layer; the launch
+        stream joins fin_stream at the end.  Every rank issues the same finishes
+        in the same order (one signal buffer, used by one finish at a time)."""
+        tc = T // chunks
+        routes = routers[li](xs[li]) if routers is not None else None
+        cur = torch.cuda.current_stream()
+        fin_stream.wait_stream(cur)
+        for c in range(chunks):
+            lo, hi = c * tc, (c + 1) * tc
+            r = None if routes is None else (routes[0][lo:hi], routes[1][lo:hi])
+            layers[li](xs[li][lo:hi], outs[li][lo:hi], routes=r)
+            chunk_done[c].record(cur)
+            fin_stream.wait_event(chunk_done[c])
+            with torch.cuda.stream(fin_stream):
+                group.finish("partial", out_f32="out", mode=args.peer_mode, status=peer_status,
+                             rows=(lo, hi), row_elems=HIDDEN)
+        fin_done.record(fin_stream)
+        cur.wait_event(fin_done)
+
     def layer_and_finish(li):
         """layer li, and (stack) the finish that forms layer li+1's bf16 input."""
+        if chunks > 1:
+            chunked_layer_and_finish(li)
+            return
         if routers is not None:
             layers[li](xs[li], outs[li], routes=routers[li](xs[li]))
         else:
@@ -898,6 +931,13 @@ def run_ours(args):
         except Exception as exc:  # noqa: BLE001
             cpu = {"value": None, "unit": UNIT, "error": repr(exc)[:200]}
 
+    if reduce_info is not None and n_layers == 1:
+        # the part of the step the reduce adds on top of the layer's own stages
+        # (stage times: eager launches of the whole step's layer on this rank)
+        layer_ms = sum(stage_avg.values())
+        reduce_info["layer_stages_ms"] = layer_ms
+        reduce_info["exposed_us"] = (ms - layer_ms) * 1e3
+        reduce_info["chunks"] = chunks
     if rank == 0:
         line = {
             "metric": wl["metric"], "value": T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
@@ -917,6 +957,10 @@ def run_ours(args):
                                           if deterministic or T <= 256 or codec is not None
                                           else "fp32 atomics into the output"),
                        "l2": "weights per step >> 126 MB L2 (no flush needed)",
+                       "chunks": chunks,
+                       "pipeline": (f"{chunks} token chunks; each chunk's peer finish runs on a "
+                                    "second stream, overlapping the next chunk's layer"
+                                    if chunks > 1 else "none"),
                        "timing": ("CUDA-graph replay of the layer and its peer finish"
                                   if use_peer else "CUDA-graph replay of the layer"
                                   + (" + eager NCCL all-reduce" if world > 1 else ""))

@@ -170,11 +170,19 @@ class PeerGroup:
     def finish_descriptors(self, partial: str, residual: torch.Tensor | None = None,
                            attention: torch.Tensor | None = None, out_f32=None, out_bf16=None,
                            norm_bf16=None, hidden: int = 0, eps: float = 1e-6,
-                           mode: str = "auto", status: torch.Tensor | None = None):
+                           mode: str = "auto", status: torch.Tensor | None = None,
+                           rows: tuple[int, int] | None = None, row_elems: int = 0):
         """(finish descriptor, peer descriptor) for the peer finish of buffer
         `partial`.  Outputs are buffer names of this group (any mode) or local
-        tensors (one-shot only)."""
-        elements = self.slots[partial].nbytes // 4
+        tensors (one-shot only).  rows=(lo, hi) with row_elems elements per row
+        finishes only those rows of every buffer (a token chunk of the step); a
+        local residual or output tensor is then the chunk's own rows."""
+        if rows is None:
+            first, elements = 0, self.slots[partial].nbytes // 4
+        else:
+            first, elements = rows[0] * row_elems, (rows[1] - rows[0]) * row_elems
+            if elements <= 0 or first + elements > self.slots[partial].nbytes // 4:
+                raise ValueError(f"rows {rows} outside the buffer")
         outs = {"f32": out_f32, "bf16": out_bf16, "norm": norm_bf16}
         named = all(v is None or isinstance(v, str) for v in outs.values())
         if mode == "auto":
@@ -184,10 +192,15 @@ class PeerGroup:
         if mode == "two" and not named:
             raise ValueError("the two-shot finish writes every rank's outputs: name group buffers")
 
+        def at(name, rank=None):
+            # element `first` of a named buffer
+            size = torch.empty((), dtype=self.slots[name].dtype).element_size()
+            return self.pointer(name, rank) + first * size
+
         def own(v):
             if v is None:
                 return 0
-            return self.pointer(v) if isinstance(v, str) else v.data_ptr()
+            return at(v) if isinstance(v, str) else v.data_ptr()
 
         keep = []
 
@@ -203,7 +216,7 @@ class PeerGroup:
             residual_bf16=residual.data_ptr() if residual is not None and
             residual.dtype == torch.bfloat16 else 0,
             attention_f32=0 if attention is None else attention.data_ptr(),
-            partials_f32=array(self.pointers(partial)),
+            partials_f32=array([at(partial, r) for r in range(self.ranks)]),
             output_f32=own(out_f32), output_bf16=own(out_bf16), norm_bf16=own(norm_bf16),
             hidden=hidden, eps=eps)
         p = abi.MoePeerDescriptor.new(
@@ -212,9 +225,10 @@ class PeerGroup:
             signals_u32=array(self.signal_pointers()),
             status_u32=0 if status is None else status.data_ptr())
         if mode == "two":
-            p.outputs_f32 = array(self.pointers(out_f32)) if out_f32 else 0
-            p.outputs_bf16 = array(self.pointers(out_bf16)) if out_bf16 else 0
-            p.norms_bf16 = array(self.pointers(norm_bf16)) if norm_bf16 else 0
+            every = lambda n: array([at(n, r) for r in range(self.ranks)])
+            p.outputs_f32 = every(out_f32) if out_f32 else 0
+            p.outputs_bf16 = every(out_bf16) if out_bf16 else 0
+            p.norms_bf16 = every(norm_bf16) if norm_bf16 else 0
         d._arrays = keep  # the arrays are read at launch time
         return d, p
 

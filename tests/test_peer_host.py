@@ -92,6 +92,13 @@ def _worker(rank, world, port, q):
         res["own_out"] = d.output_f32
         d1, p1 = g.finish_descriptors("partial", out_f32="out", mode="one")
         res["one"] = (p1.flags, p1.outputs_f32, d1.elements)
+        # a token chunk: rows 16..48 of every buffer
+        d2, p2 = g.finish_descriptors("partial", out_f32="out", norm_bf16="norm", hidden=H,
+                                      mode="two", rows=(16, 48), row_elems=H)
+        res["chunk"] = (d2.elements, arr(d2.partials_f32), arr(p2.outputs_f32),
+                        arr(p2.norms_bf16), d2.output_f32)
+        with pytest.raises(ValueError):
+            g.finish_descriptors("partial", out_f32="out", rows=(60, 72), row_elems=H)
         with pytest.raises(ValueError):
             g.finish_descriptors("partial", out_f32=torch.empty(1), mode="two")
         g.close()
@@ -129,6 +136,12 @@ def test_peer_group_two_ranks_gloo():
         assert res["flags"] == abi.PEER_TWO_SHOT
         assert res["one"] == (abi.PEER_ONE_SHOT, 0, T * H)
         assert res["closed"] == [("close", expect[1 - r]), ("free", own[r])]
+        elements, parts, outs, norms, own_out = res["chunk"]
+        assert elements == 32 * H
+        assert parts == [b + slots["partial"].offset + 16 * H * 4 for b in expect]
+        assert outs == [b + slots["out"].offset + 16 * H * 4 for b in expect]
+        assert norms == [b + slots["norm"].offset + 16 * H * 2 for b in expect]
+        assert own_out == outs[r]
 
 
 def test_peer_launch_rejects_bad_descriptors_without_a_device():
