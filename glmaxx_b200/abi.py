@@ -262,6 +262,7 @@ SIGNATURES = {
     "glmaxx_moe_ep_dispatch_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_moe_ep_return_launch": (ctypes.c_int32, [_P, _P]),
     "glmaxx_nvfp4_codec_selfcheck_launch": (ctypes.c_int32, [_P, _P]),
+    "glmaxx_nvfp4_quotient_selfcheck_launch": (ctypes.c_int32, [_P, ctypes.c_uint32, _P, _P]),
     "glmaxx_nvfp4_mma_peak_launch": (ctypes.c_int32, [u32, u32, u32, u32, u32, u32, _P, _P, _P]),
     "glmaxx_nvfp4_pack_launch": (ctypes.c_int32, [u64, ctypes.c_int32, u32, u32, u32, u64, u64,
                                                   u64, u64, u64, u64, _P]),

@@ -392,6 +392,41 @@ __device__ __forceinline__ uint32_t e4m3_cvt_pos(float v) {
   return out & 0xffu;
 }
 
+// E2M1 codes of 8 quotients v[i] / dec, each quotient first rounded to fp32 as
+// the reference computes it (code(fl(v / dec))); a zero value gives code 0.
+// fast (dec and 1/dec normal): q' = fl(v * rdec), rdec = fl(1 / dec), is within
+// 3 * 2^-24 (relative) of the exact quotient, and so is its correctly rounded
+// value.  fl(q' * (1 - 2^-20)) and fl(q' * (1 + 2^-20)) bracket both with room to
+// spare; the E2M1 rounding is monotone in the magnitude, so when the two ends
+// have the same code every value between them -- the rounded quotient included
+// -- has it too.  Otherwise (an E2M1 midpoint lies within ~8 ulp) the quotients
+// are divided exactly.  The bracket is checked for 8 codes at once.
+__device__ __forceinline__ uint32_t e2m1x8_quotient(const float* v, float dec, float rdec,
+                                                    bool fast) {
+  constexpr float kDown = 0.99999904632568359375f;  // 1 - 2^-20
+  constexpr float kUp = 1.00000095367431640625f;    // 1 + 2^-20
+  if (fast) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float q = __fmul_rn(v[i], rdec);
+      lo[i] = v[i] == 0.0f ? 0.0f : __fmul_rn(q, kDown);
+      hi[i] = v[i] == 0.0f ? 0.0f : __fmul_rn(q, kUp);
+    }
+    const uint32_t a = e2m1x8_cvt(lo), b = e2m1x8_cvt(hi);
+    if (a == b) return a;
+  }
+  float q[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q[i] = v[i] == 0.0f ? 0.0f : __fdiv_rn(v[i], dec);
+  return e2m1x8_cvt(q);
+}
+
+// Whether e2m1x8_quotient may take its fast path for this divisor.
+__device__ __forceinline__ bool quotient_fast_ok(float dec) {
+  return dec >= 0x1p-122f && dec <= 0x1p122f;
+}
+
 // Quantise one 16-element block (nvfp4.rs:567-608): scale code from the block
 // amax, then each value divided by decode(scale) * global.  Returns the scale
 // code; writes the 16 codes as 8 bytes (even element in the low nibble).  A zero
@@ -403,15 +438,15 @@ __device__ __forceinline__ uint32_t nvfp4_block(const float* v, float global_sca
   for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   uint32_t sc = 0;
   if (amax != 0.0f) sc = e4m3_cvt_pos(__fdiv_rn(__fdiv_rn(amax, 6.0f), global_scale));
-  const float dec = __fmul_rn(e4m3_decode(sc), global_scale);
-  float q0[8], q1[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    q0[i] = (v[i] == 0.0f || sc == 0) ? 0.0f : __fdiv_rn(v[i], dec);
-    q1[i] = (v[i + 8] == 0.0f || sc == 0) ? 0.0f : __fdiv_rn(v[i + 8], dec);
+  if (sc == 0) {
+    *packed = make_uint2(0, 0);
+    return 0;
   }
-  packed->x = e2m1x8_cvt(q0);
-  packed->y = e2m1x8_cvt(q1);
+  const float dec = __fmul_rn(e4m3_decode(sc), global_scale);
+  const bool fast = quotient_fast_ok(dec);
+  const float rdec = fast ? __frcp_rn(dec) : 0.0f;
+  packed->x = e2m1x8_quotient(v, dec, rdec, fast);
+  packed->y = e2m1x8_quotient(v + 8, dec, rdec, fast);
   return sc;
 }
 

@@ -711,6 +711,18 @@ int32_t glmaxx_moe_ep_return_launch(const struct glmaxx_moe_ep_descriptor* descr
  * mismatching input (0 = none). */
 int32_t glmaxx_nvfp4_codec_selfcheck_launch(unsigned long long* result_u64x4, void* cuda_stream);
 
+/* Self-check (no reference counterpart): every finite fp32 value v against each
+ * divisor decs[0..n_decs) (device, n_decs <= 4096): the E2M1 code the
+ * quantisation kernels give v / dec (a reciprocal product bracketed within
+ * 2^-20, the exact quotient where an E2M1 midpoint is that close) against the
+ * code of the exactly rounded quotient fl(v / dec), the reference's
+ * (nvfp4.rs:567-608).  result_u64x4 (device): [0] mismatches, [1] (divisor
+ * index << 32 | v bits) + 1 of one mismatch (0 = none), [2] values decided on
+ * the bracket alone, [3] values checked. */
+int32_t glmaxx_nvfp4_quotient_selfcheck_launch(const float* decs, uint32_t n_decs,
+                                               unsigned long long* result_u64x4,
+                                               void* cuda_stream);
+
 #if defined(__cplusplus)
 }
 

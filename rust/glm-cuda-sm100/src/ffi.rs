@@ -217,6 +217,12 @@ unsafe extern "C" {
     pub fn glmaxx_moe_ep_dispatch_launch(descriptor: *const MoeEpDescriptor, stream: *mut c_void) -> i32;
     pub fn glmaxx_moe_ep_return_launch(descriptor: *const MoeEpDescriptor, stream: *mut c_void) -> i32;
     pub fn glmaxx_nvfp4_codec_selfcheck_launch(result_u64x4: *mut u64, stream: *mut c_void) -> i32;
+    pub fn glmaxx_nvfp4_quotient_selfcheck_launch(
+        decs: *const f32,
+        n_decs: u32,
+        result_u64x4: *mut u64,
+        stream: *mut c_void,
+    ) -> i32;
     pub fn glmaxx_nvfp4_mma_peak_launch(
         n: u32,
         dual: u32,
