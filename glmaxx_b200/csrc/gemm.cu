@@ -128,6 +128,8 @@ cudaError_t launch_gemm(GemmVariant v, const GemmLaunch& g, int num_sms, cudaStr
       return run<true, false, 128, 4, kEpiStoreF32>(g, num_sms, stream);
     case kFc2PrefillFp4PairPlane:
       return run<true, true, 128, 3, kEpiRoutedPlane>(g, num_sms, stream);
+    case kFc2PrefillFp4PairAtomic:
+      return run<true, true, 128, 3, kEpiRoutedAtomic>(g, num_sms, stream);
     case kShared1Bf16N64:
       return run<false, true, 64, 5, kEpiSwiGLU>(g, num_sms, stream);
     case kShared2Bf16N64:

@@ -575,8 +575,11 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     // tile (twice the weight bytes per pipeline stage, half the B-tile and
     // scale-copy work per FLOP).  Prefill with the atomic combine: one M tile per
     // item, whose two accumulator buffers let the MMA run through the atomic
-    // epilogue (FC2 1.34 -> 1.21 ms at T=8192).
-    const bool single = !p.decode && !p.plane_mode;
+    // epilogue (FC2 1.34 -> 1.21 ms at T=8192) -- except on narrow shards
+    // (local intermediate <= 256, one K stage per item), where the shared B tile
+    // wins again (T=8192 TP8-shard layer 1.80 -> 1.73 ms; at TP1 and a TP2 shard
+    // the pair measured slower, 3.89 -> 3.95 and 2.50 -> 2.63 ms).
+    const bool single = !p.decode && !p.plane_mode && p.I > 256;
     a.m_tiles = single ? p.H / 128 : p.H / 256;
     a.m_stride = single ? 128 : 256;
     a.up_row_offset = single ? 0 : 128;
@@ -594,8 +597,10 @@ int32_t moe_layer_launch(const glmaxx_moe_layer_descriptor* desc, void* cuda_str
     a.row_slot = q.row_slot;
     a.row_weight = q.row_weight;
     a.status = status;
-    CHECK(launch_gemm(p.decode ? kFc2DecodeFp4Pair
-                             : (p.plane_mode ? kFc2PrefillFp4PairPlane : kFc2PrefillFp4),
+    CHECK(launch_gemm(p.decode       ? kFc2DecodeFp4Pair
+                      : p.plane_mode ? kFc2PrefillFp4PairPlane
+                      : single       ? kFc2PrefillFp4
+                                     : kFc2PrefillFp4PairAtomic,
                       g, info.sms, stream));
   }
   // 8. deterministic combine (plane mode): ascending-expert sum + shared

@@ -188,6 +188,7 @@ enum GemmVariant : int {
   kShared1Bf16N64Split = 10,  // BF16, gate+up, N tile 64, split-K partials
   kShared2Bf16N64Split = 11,  // BF16, N tile 64, split-K partials
   kFc2DecodeFp4Pair = 12,     // NVFP4, two adjacent M tiles per item, N tile 32, routed plane
+  kFc2PrefillFp4PairAtomic = 13, // NVFP4, two adjacent M tiles per item, N tile 128, routed atomics
   kFc2PrefillFp4PairPlane = 14,  // as 13, writing the routed plane (deterministic combine)
 };
 
