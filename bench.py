@@ -752,18 +752,24 @@ def run_ours(args):
                 peer_gbs, peer_live = peer_copy_gbs(group, dev, stream), True
             except Exception as exc:  # noqa: BLE001 -- same failure on every rank
                 print(f"peer copy probe failed: {exc!r}", file=sys.stderr)
+        # bytes each GPU sends (and receives) over NVLink per reduce: one-shot, its
+        # partial to each of the N-1 peers; two-shot (and a ring all-reduce), its
+        # 1/N slice-reduction inputs to N-1 peers plus its reduced slice to N-1
+        # peers, 2(N-1)/N of the partial -- both directions busy at once
+        link_bytes = ((world - 1) * S if use_peer and mode == "one"
+                      else 2 * (world - 1) * S // world)
         reduce_info = {
             "kind": f"peer {mode}-shot (fused finish kernel)" if use_peer else "NCCL all-reduce",
             "us_per_launch": red_ms * 1e3, "bytes": S,
-            "nvlink_bytes_per_rank": ((world - 1) * S if use_peer and mode == "one"
-                                      else 2 * (world - 1) * S // world),
+            "nvlink_bytes_per_rank": link_bytes,
             "busbw_gbs": busbw, "peak_gbs": peer_gbs,
             "peak_kind": ("peer copy measured in this run (every rank into its right "
                           "neighbour at once, 64 MiB, max over ranks)" if peer_live else
                           "earlier peer-copy measurement on this pool"),
-            "frac": busbw / 2 / peer_gbs,
+            "frac": link_bytes / (red_ms * 1e-3) / 1e9 / peer_gbs,
             "note": "busbw = 2(N-1)/N x bytes / time (the all-reduce convention); frac = the "
-                    "per-direction (N-1)/N x bytes / time against the peer copy rate"}
+                    "bytes each GPU sends per direction (nvlink_bytes_per_rank) / time, "
+                    "against the peer copy rate"}
         if use_peer and int(peer_status.item()):
             raise RuntimeError(f"peer finish status: {int(peer_status.item())}")
 
