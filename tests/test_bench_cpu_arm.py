@@ -52,3 +52,19 @@ def test_cpu_sample_rule():
     assert np.array_equal(bench.cpu_sample(64, "decode", 1), np.arange(64))
     s = bench.cpu_sample(8192, "prefill", 1)
     assert s.size == bench.CPU_PREFILL_SAMPLE_TOKENS and np.all(np.diff(s) > 0)
+
+
+def test_bench_options_defaults_and_workload_tokens(monkeypatch):
+    """The driver runs `bench.py` with no workload flags: decode at T=64, the
+    peer finish, token-split routing where it pays, atomic prefill combine and
+    an unchunked step; a workload flag picks that configuration's token count."""
+    import sys
+    monkeypatch.setattr(sys, "argv", ["bench.py"])
+    a = bench.parse()
+    assert (a.workload, a.tokens, a.gpus, a.reduce, a.split_route, a.combine, a.chunks) == \
+        ("decode", 64, 1, "peer", "auto", "atomic", 1)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--workload", "prefill", "--chunks", "2"])
+    a = bench.parse()
+    assert (a.tokens, a.chunks) == (8192, 2)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--workload", "exl3"])
+    assert bench.parse().tokens == 32
