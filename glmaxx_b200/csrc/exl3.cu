@@ -130,9 +130,9 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
       exl3_load_span(tile_ptr(kc, 0), lw, span[0]);
       exl3_load_span(tile_ptr(kc, 1), lw, span[1]);
       for (uint32_t k16 = 0; k16 < kn; k16 += 16) {
-        uint16_t w16[2][8];
-        exl3_decode_span(span[0], lw.off, w16[0]);
-        exl3_decode_span(span[1], lw.off, w16[1]);
+        uint32_t wp[2][4];
+        exl3_decode_span_pairs(span[0], lw.off, wp[0]);
+        exl3_decode_span_pairs(span[1], lw.off, wp[1]);
         if (k16 + 16 < kn) {  // next step's words are in flight during this step
           exl3_load_span(tile_ptr(kc + k16 + 16, 0), lw, span[0]);
           exl3_load_span(tile_ptr(kc + k16 + 16, 1), lw, span[1]);
@@ -144,8 +144,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
           for (int w = 0; w < 8; w += 2) {
             const uint32_t lr = lrb + 8 * ((w >> 1) & 1);
             const uint32_t lc = lcb + 8 * ((w >> 2) & 1);
-            *reinterpret_cast<uint32_t*>(&ws[(16 * j + lc) * kPitch + lr]) =
-                uint32_t(w16[j][w]) | (uint32_t(w16[j][w + 1]) << 16);
+            *reinterpret_cast<uint32_t*>(&ws[(16 * j + lc) * kPitch + lr]) = wp[j][w / 2];
           }
         __syncwarp();
         const uint4 c01 = *reinterpret_cast<const uint4*>(&ws[lane * kPitch]);

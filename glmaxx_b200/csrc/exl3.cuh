@@ -38,17 +38,32 @@ __device__ __forceinline__ void exl3_load_span(const uint16_t* __restrict__ base
 // 3INST decode of the 8 windows in the span: value = window * 0xCBAC1FED,
 // (value & 0x8FFF8FFF) ^ 0x3B603B60 read as two fp16 halves, summed.  Both halves
 // have exponent fields 12..15, so their exact sum fits fp32 and the fp16 add
-// rounds it once, exactly as fp16(f32(lo) + f32(hi)) of the reference.
-__device__ __forceinline__ void exl3_decode_span(const uint32_t (&wd)[3], uint32_t off,
-                                                 uint16_t (&w16)[8]) {
-  const uint64_t v = (uint64_t(wd[0]) << 32) | wd[1];
-  const uint64_t span = off ? ((v << off) | (wd[2] >> (32 - off))) : v;  // bit 63 = span start
+// rounds it once, exactly as fp16(f32(lo) + f32(hi)) of the reference.  The 8
+// weights come out as 4 packed pairs (weight 2j in the low half of p[j], 2j + 1
+// in the high half): the layout both consumers store.  The
+// span is assembled with funnel shifts (no special case for a zero offset); for
+// each pair the two masked products are regrouped into (low halves) and (high
+// halves) by two byte permutes, and one fp16x2 add gives both sums -- each half
+// of that add rounds once, exactly as the single add per weight above.
+__device__ __forceinline__ void exl3_decode_span_pairs(const uint32_t (&wd)[3], uint32_t off,
+                                                       uint32_t (&p)[4]) {
+  const uint32_t hi = __funnelshift_l(wd[1], wd[0], off);  // span bits 63..32
+  const uint32_t lo = __funnelshift_l(wd[2], wd[1], off);  // span bits 31..0
+  uint32_t win[8];
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    const uint32_t window = uint32_t(span >> (48 - 3 * w)) & 0xffffu;
-    const uint32_t packed = ((window * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
-    const __half2 h = *reinterpret_cast<const __half2*>(&packed);
-    w16[w] = __half_as_ushort(__hadd(__low2half(h), __high2half(h)));
+    const int sh = 48 - 3 * w;  // the window is span bits sh + 15 .. sh
+    win[w] = (sh >= 32 ? hi >> (sh - 32) : __funnelshift_r(lo, hi, sh)) & 0xffffu;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t q0 = ((win[2 * j] * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    const uint32_t q1 = ((win[2 * j + 1] * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+    const uint32_t los = __byte_perm(q0, q1, 0x5410);  // (q0 low half, q1 low half)
+    const uint32_t his = __byte_perm(q0, q1, 0x7632);  // (q0 high half, q1 high half)
+    const __half2 sum = __hadd2(*reinterpret_cast<const __half2*>(&los),
+                                *reinterpret_cast<const __half2*>(&his));
+    p[j] = *reinterpret_cast<const uint32_t*>(&sum);
   }
 }
 

@@ -227,15 +227,15 @@ __global__ void __launch_bounds__(kXThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kXKtPerDecoder; ++kk) {
           const uint32_t ktl = kt0 + kk;
-          uint16_t w16[8];
-          exl3_decode_span(wd[kk], lw.off, w16);
+          uint32_t wp[4];
+          exl3_decode_span_pairs(wd[kk], lw.off, wp);
 #pragma unroll
           for (int w = 0; w < 8; w += 2) {
             const uint32_t n = dw * 16 + lcb + 8 * ((w >> 2) & 1);
             const uint32_t k = ktl * 16 + lrb + 8 * ((w >> 1) & 1);  // even
             const uint32_t byte = 2 * k;
             uint8_t* dst = a + n * 128 + ((((byte >> 4) ^ (n & 7)) << 4) | (byte & 15));
-            *reinterpret_cast<uint32_t*>(dst) = uint32_t(w16[w]) | (uint32_t(w16[w + 1]) << 16);
+            *reinterpret_cast<uint32_t*>(dst) = wp[w / 2];
           }
         }
         fence_proxy_async_smem();
