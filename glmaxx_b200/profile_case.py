@@ -69,11 +69,20 @@ def main():
     if a.time:
         ms = e0.elapsed_time(e1) / a.time
     status = layer.device_status()
-    touched = int(torch.unique(layer.routes(a.tokens)[0].long()).numel())
-    print(json.dumps({"experts": a.experts, "tokens": a.tokens, "tp": a.tp, "steps": a.steps,
-                      "codec": a.codec, "deterministic": a.deterministic, "ms_per_step": ms,
-                      "touched_experts": touched, "status": status,
-                      "abi": abi.abi_string()}))
+    routed = layer.routes(a.tokens)[0].long().flatten()
+    touched = int(torch.unique(routed).numel())
+    info = {"experts": a.experts, "tokens": a.tokens, "tp": a.tp, "steps": a.steps,
+            "codec": a.codec, "deterministic": a.deterministic, "ms_per_step": ms,
+            "touched_experts": touched, "status": status, "abi": abi.abi_string()}
+    if a.codec == "exl3":
+        # weights the decode-fused projection decodes per projection of one step:
+        # every work item (an expert's rows in blocks of 4; experts with 8 or
+        # more rows take the tensor-core path) decodes its expert's whole matrix
+        rows = torch.bincount(routed, minlength=a.experts).tolist()
+        items = sum((r + 3) // 4 for r in rows if 0 < r < 8)
+        info["gemv_items"] = items
+        info["gemv_weights_per_projection"] = items * cfg.hidden * cfg.local_intermediate
+    print(json.dumps(info))
     if status:
         raise SystemExit(1)
 
