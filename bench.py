@@ -878,8 +878,10 @@ def run_ours(args):
                 "frac": achieved / hbm_peak, "peak_kind": f"{peak_kind} HBM copy",
                 "traffic": None, "algorithmic_bytes_per_launch": ex_bytes,
                 "alu": {"decoded_weights_per_s": touched * 3 * HIDDEN * Ir / (fc1_ms * 1e-3),
-                        "note": "3INST trellis decode is ALU-bound: ~10 integer/fp16 ops per "
-                                "weight, fp32 multiply-then-add chains in the reference order"}}
+                        "note": "3INST trellis decode is ALU-bound: ~15 thread instructions "
+                                "per decoded weight (ncu), one fp32 fma of fp16 factors per "
+                                "weight and row (the product is exact, so it equals the "
+                                "reference's multiply then add), k ascending"}}
     elif codec == "hybrid":
         layer_ms = ms / n_layers
         nv_touched = int(torch.unique(re.long()[nvfp4_mask.to(re.device)[re.long()]]).numel())
