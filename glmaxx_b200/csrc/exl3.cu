@@ -87,6 +87,13 @@ struct Exl3GemvArgs {
   uint32_t implicit_rows;
   uint16_t* out;                 // [rows][N] f16
   uint32_t K, N;
+  // optional second projection of the same rows, shape and item list (the up
+  // projection beside gate): blocks N/32 .. 2N/32 - 1 take x2 / trellis2 / out2,
+  // so one launch holds twice the work units and its last wave is relatively
+  // shorter; null: one projection
+  const uint16_t* x2;
+  const uint16_t* trellis2;
+  uint16_t* out2;
 };
 
 template <int RB>
@@ -99,7 +106,12 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
   __shared__ __align__(16) uint16_t xs[RB][kExl3KChunk]; // x of this item's rows (fp16)
   const uint32_t lane = threadIdx.x;
   const Exl3LaneWindow lw = exl3_lane_window(lane);
-  const uint32_t c0 = blockIdx.x * 32;                   // first column of this warp
+  const uint32_t ncw = a.N / 32;                         // column warps per projection
+  const bool second = blockIdx.x >= ncw;                 // block-uniform
+  const uint16_t* __restrict__ xin = second ? a.x2 : a.x;
+  const uint16_t* __restrict__ trellis = second ? a.trellis2 : a.trellis;
+  uint16_t* __restrict__ out = second ? a.out2 : a.out;
+  const uint32_t c0 = (blockIdx.x - (second ? ncw : 0)) * 32;  // first column of this warp
   const uint32_t nt0 = c0 / 16;                          // first tile column
   const uint32_t lcb = 2 * ((lane >> 3) & 3) + ((lane >> 2) & 1);
   const uint32_t lrb = 2 * (lane & 3);
@@ -111,7 +123,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
     const uint32_t r0 = (listed ? a.group_rows[g] : 0) + blk * RB;
     const uint32_t rend = listed ? a.group_rows[g + 1] : a.implicit_rows;
     const uint32_t nr = min(uint32_t(RB), rend - r0);
-    const uint16_t* tr = a.trellis + uint64_t(g) * a.trellis_stride;
+    const uint16_t* tr = trellis + uint64_t(g) * a.trellis_stride;
     float acc[RB];
 #pragma unroll
     for (int r = 0; r < RB; ++r) acc[r] = 0.f;
@@ -120,7 +132,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
       __syncwarp();
       for (uint32_t i = lane; i < nr * kExl3KChunk; i += 32) {  // only this item's rows
         const uint32_t r = i / kExl3KChunk, k = i % kExl3KChunk;
-        xs[r][k] = k < kn ? a.x[uint64_t(r0 + r) * a.K + kc + k] : uint16_t(0);
+        xs[r][k] = k < kn ? xin[uint64_t(r0 + r) * a.K + kc + k] : uint16_t(0);
       }
       __syncwarp();
       uint32_t span[2][3];
@@ -172,7 +184,7 @@ __global__ void __launch_bounds__(32) exl3_gemv_kernel(Exl3GemvArgs a) {
     }
 #pragma unroll
     for (int r = 0; r < RB; ++r)
-      if (r < static_cast<int>(nr)) a.out[uint64_t(r0 + r) * a.N + c0 + lane] = f2h(acc[r]);
+      if (r < static_cast<int>(nr)) out[uint64_t(r0 + r) * a.N + c0 + lane] = f2h(acc[r]);
   }
 }
 
@@ -377,7 +389,7 @@ constexpr int kExl3GroupRowBlock = 4;
 
 template <int RB>
 cudaError_t run_exl3_gemv(const Exl3GemvArgs& a, uint32_t max_items, cudaStream_t stream) {
-  dim3 grid(a.N / 32, max_items < 4096 ? max_items : 4096);
+  dim3 grid((a.x2 != nullptr ? 2 : 1) * (a.N / 32), max_items < 4096 ? max_items : 4096);
   exl3_gemv_kernel<RB><<<grid, 32, 0, stream>>>(a);
   return cudaPeekAtLastError();
 }
@@ -409,12 +421,15 @@ cudaError_t launch_exl3_items(const uint32_t* group_rows, uint32_t groups, const
   return cudaPeekAtLastError();
 }
 
-// Grouped projection over the item list of launch_exl3_items.
+// Grouped projection over the item list of launch_exl3_items; with x2 set, a
+// second projection of the same shape (x2, trellis2 -> out2) in the same launch.
 cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
                                      uint64_t trellis_stride, const uint32_t* group_rows,
                                      uint32_t max_items, const uint32_t* items,
                                      const uint32_t* n_items, uint32_t K, uint32_t N, uint16_t* out,
-                                     cudaStream_t stream) {
+                                     cudaStream_t stream, const uint16_t* x2 = nullptr,
+                                     const uint16_t* trellis2 = nullptr,
+                                     uint16_t* out2 = nullptr) {
   if (K % 16 || N % 32) return cudaErrorInvalidValue;
   Exl3GemvArgs a{};
   a.x = x;
@@ -426,6 +441,9 @@ cudaError_t launch_exl3_gemv_grouped(const uint16_t* x, const uint16_t* trellis,
   a.out = out;
   a.K = K;
   a.N = N;
+  a.x2 = x2;
+  a.trellis2 = trellis2;
+  a.out2 = out2;
   return run_exl3_gemv<kExl3GroupRowBlock>(a, max_items, stream);
 }
 
@@ -471,21 +489,25 @@ cudaError_t launch_exl3_experts(const Exl3ExpertsLaunch& L, cudaStream_t stream)
   } while (0)
   X3(launch_exl3_items(L.offsets, L.E, L.codec, kExl3TcMinRows, items, n_items, stream));
   X3(launch_exl3_tc_tiles(L.offsets, L.E, L.codec, kExl3TcMinRows, tc_tiles, tc_count, stream));
-  // gate / up: rotate the token rows with each projection's suh, project, rotate out
+  // gate / up: rotate the token rows with each projection's suh (gate into xr,
+  // up into p2, which holds nothing until the down projection), project both in
+  // one decode-fused launch, then each projection's tensor-core rows, rotate out
+  uint16_t* xr_up = p2;
   for (int proj = 0; proj < 2; ++proj) {
-    const uint16_t* suh = proj ? L.up_suh : L.gate_suh;
-    const uint16_t* svh = proj ? L.up_svh : L.gate_svh;
+    exl3_rows_rotate_in<<<A, 256, 0, stream>>>(m, L.x_bf16, L.row_token, nullptr,
+                                                proj ? L.up_suh : L.gate_suh, H,
+                                                proj ? xr_up : xr, kExl3TcMinRows);
+    X3(cudaPeekAtLastError());
+  }
+  X3(launch_exl3_gemv_grouped(xr, L.gate_trellis, gate_stride, L.offsets, max_items, items,
+                              n_items, H, I, p0, stream, xr_up, L.up_trellis, p1));
+  for (int proj = 0; proj < 2; ++proj) {
     const uint16_t* tr = proj ? L.up_trellis : L.gate_trellis;
     uint16_t* pout = proj ? p1 : p0;
-    exl3_rows_rotate_in<<<A, 256, 0, stream>>>(m, L.x_bf16, L.row_token, nullptr, suh, H, xr,
-                                                kExl3TcMinRows);
-    X3(cudaPeekAtLastError());
-    X3(launch_exl3_gemv_grouped(xr, tr, gate_stride, L.offsets, max_items, items, n_items, H, I,
-                                pout, stream));
-    X3(launch_exl3_tc(xr, A, H, tr, gate_stride, tc_tiles, tc_count, I, pout, L.status, L.num_sms,
-                      stream));
-    exl3_rows_rotate_out<<<A, 256, 0, stream>>>(m, pout, svh, I, nullptr, nullptr, nullptr,
-                                                 nullptr, 0, kExl3TcMinRows);
+    X3(launch_exl3_tc(proj ? xr_up : xr, A, H, tr, gate_stride, tc_tiles, tc_count, I, pout,
+                      L.status, L.num_sms, stream));
+    exl3_rows_rotate_out<<<A, 256, 0, stream>>>(m, pout, proj ? L.up_svh : L.gate_svh, I, nullptr,
+                                                 nullptr, nullptr, nullptr, 0, kExl3TcMinRows);
     X3(cudaPeekAtLastError());
   }
   exl3_rows_swiglu<<<dim3((I + 255) / 256, A), 256, 0, stream>>>(m, p0, p1, I, h);
